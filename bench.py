@@ -1,0 +1,470 @@
+"""Benchmark of the B200 BiGEMM hot path (one JSON line on rank 0).
+
+Workload (the operator sweep the metric is quoted on):
+B=128 per GPU, bf16 compute with fp32 accumulation, forward + backward
+(dX and all weight gradients) of every stage shape {56x56x128 d64,
+28x28x256 d64, 14x14x512 d128, 7x7x1024 d128} under each of the local,
+shifted and radix routes.  One step = those 12 fwd+bwd calls.  Inputs are
+seeded synthetic tensors (x, dY ~ N(0,1), default-init weights cast to bf16,
+seed order of scripts/benchmark.py:56-110); the per-step working set
+(~1 GB) is far larger than the 126 MB L2, so every step streams from HBM.
+
+``value`` = algorithmic FLOPs of all ranks / max-over-ranks device time
+(CUDA events, inputs resident in HBM).  FLOPs per tile follow the operator
+definition: fwd = 4g^2 d + 2g^2 rd + 6 g d rd over padded tiles, bwd = 2x fwd.
+``e2e`` = the same FLOPs timed through the public ``bigemm`` API with inputs
+copied from pinned host memory and outputs and gradients copied back inside
+the timed region.
+
+``--impl reference`` times the CPU restatement of the reference algorithm
+(``oracle``, numpy float32, all host cores) on a bounded sample of the same
+workload.  Under torchrun only rank 0 runs it.
+
+Multi-GPU: one process per GPU; the batch is sharded (each rank runs its own
+B=128 sweep, no data-path collective), so scaling is weak.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+SHAPES = [(56, 56, 128, 64), (28, 28, 256, 64), (14, 14, 512, 128), (7, 7, 1024, 128)]
+ROUTES = [("local", 0), ("shifted", 0), ("radix", 0)]
+BATCH = 128
+G = 16
+METRIC = "BiGEMM TFLOP/s (fwd+bwd, bf16, operator sweep B=128)"
+
+
+def fwd_flops(b: int, h: int, w: int, c: int, d: int) -> float:
+    qs = math.ceil(h * w / G)
+    qc = math.ceil(c / d)
+    rd = 2 * d
+    return float(b * qs * qc * (4 * G * G * d + 2 * G * G * rd + 6 * G * d * rd))
+
+
+def fwd_bytes(b, h, w, c, elem=2) -> float:
+    return 2.0 * b * h * w * c * elem
+
+
+def step_flops(batch: int) -> float:
+    return sum(3.0 * fwd_flops(batch, h, w, c, d) for (h, w, c, d) in SHAPES for _ in ROUTES)
+
+
+# ---------------------------------------------------------------------------
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def _make_case(h, w, c, d, batch, dev, seed):
+    """Seeded operator tensors (scripts/benchmark.py:56-110 scales)."""
+    import torch.nn as nn
+
+    from omniwave_b200 import build_route_plan
+
+    torch.manual_seed(seed)
+    qc = math.ceil(c / d)
+    rd = 2 * d
+
+    def init(shape, fn):
+        t = torch.empty(shape, dtype=torch.float32, device=dev)
+        fn(t)
+        return t.to(torch.bfloat16)
+
+    tensors = dict(
+        x=torch.randn(batch, h, w, c, device=dev, dtype=torch.bfloat16),
+        a_u=init((G, G), nn.init.orthogonal_), a_v=init((G, G), nn.init.orthogonal_),
+        a_o=init((G, G), nn.init.eye_),
+        b_u=init((qc, d, rd), nn.init.xavier_uniform_), b_v=init((qc, d, rd), nn.init.xavier_uniform_),
+        b_o=init((qc, rd, d), nn.init.xavier_uniform_),
+        gamma=torch.full((c,), 1e-5, device=dev, dtype=torch.bfloat16),
+    )
+    dout = torch.randn(batch, h, w, c, device=dev, dtype=torch.bfloat16)
+    return tensors, dout
+
+
+class _Clocks:
+    """nvidia-smi sampler running during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+        return False
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in (self.out or "").splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+def run_ours(args) -> None:
+    from omniwave_b200 import _lib, bigemm, build_route_plan
+
+    world, rank, local = _dist()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", device_id=dev,
+                                             timeout=datetime.timedelta(seconds=120))
+    lib = _lib.load()
+    names = ("x", "a_u", "a_v", "a_o", "b_u", "b_v", "b_o", "gamma")
+
+    cases = []
+    for si, (h, w, c, d) in enumerate(SHAPES):
+        for ri, (route, lvl) in enumerate(ROUTES):
+            tensors, dout = _make_case(h, w, c, d, BATCH, dev, seed=1 + 1000 * rank + 10 * si + ri)
+            plan = build_route_plan(h, w, c, G, d, route, lvl)
+            leaves = {k: v.detach().requires_grad_(True) for k, v in tensors.items()}
+            cases.append(dict(shape=(h, w, c, d), route=f"{route}{lvl}", plan=plan,
+                              leaves=leaves, dout=dout))
+
+    def one_case(cs, ev=None):
+        if ev is not None:
+            ev[0].record()
+        out = bigemm(plan=cs["plan"], backend="cuda", **cs["leaves"])
+        if ev is not None:
+            ev[1].record()
+        grads = torch.autograd.grad(out, [cs["leaves"][k] for k in names], cs["dout"])
+        if ev is not None:
+            ev[2].record()
+        return out, grads
+
+    def step(evs=None):
+        for i, cs in enumerate(cases):
+            one_case(cs, None if evs is None else evs[i])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    # --- device-timed region -------------------------------------------------
+    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in cases]
+           for _ in range(args.steps)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    launches0 = lib.ow_launch_count()
+    with _Clocks(dev.index) as clk:
+        t0.record()
+        for s in range(args.steps):
+            step(evs[s])
+        t1.record()
+        torch.cuda.synchronize()
+    launches = lib.ow_launch_count() - launches0
+    if world > 1:
+        torch.distributed.barrier()
+    ms = t0.elapsed_time(t1)
+    ms_t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(ms_t, op=torch.distributed.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    flops = step_flops(BATCH) * args.steps * world
+    value = flops / (ms_max * 1e-3) / 1e12
+
+    # Per-call breakdown (fwd / bwd of each case) from the in-region events.
+    per = {}
+    for i, cs in enumerate(cases):
+        f = statistics.mean(evs[s][i][0].elapsed_time(evs[s][i][1]) for s in range(args.steps))
+        b = statistics.mean(evs[s][i][1].elapsed_time(evs[s][i][2]) for s in range(args.steps))
+        per[(cs["shape"], cs["route"])] = (f, b)
+    # Dominant call: the largest total time.
+    dom_key, (dom_f, dom_b) = max(per.items(), key=lambda kv: kv[1][0] + kv[1][1])
+    (h, w, c, d), route = dom_key
+    dom_phase = "bwd" if dom_b >= dom_f else "fwd"
+    dom_ms = max(dom_f, dom_b)
+    dom_flops = (2.0 if dom_phase == "bwd" else 1.0) * fwd_flops(BATCH, h, w, c, d)
+    peaks = _peaks()
+    achieved = dom_flops / (dom_ms * 1e-3) / 1e12
+
+    # --- end-to-end through the public API with host buffers -----------------
+    e2e = _e2e(args, cases, names, dev, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = _cpu_baseline(args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 3),
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_max / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) inputs and upstream grads, default-init weights)",
+            "config": {
+                "workload": "bigemm_sweep_fwd_bwd",
+                "batch_per_gpu": BATCH,
+                "global_batch": BATCH * world,
+                "shapes": [f"{h}x{w}x{c}/d{d}" for (h, w, c, d) in SHAPES],
+                "routes": [f"{r}{l}" for r, l in ROUTES],
+                "parallelism": f"batch-shard x{world}",
+                "l2": "per-step working set ~1 GB > 126 MB L2 (inputs larger than L2)",
+                "flops_per_step_per_gpu": step_flops(BATCH),
+            },
+            "roofline": {
+                "bound": "tensor",
+                "kernel": f"bigemm {dom_phase} {h}x{w}x{c}/d{d} {route}",
+                "achieved": round(achieved, 3),
+                "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s",
+                "frac": round(achieved / peaks["bf16_tflops"], 4),
+                "peak_source": peaks["source"],
+                "traffic": None,
+            },
+            "per_call_ms": {f"{k[0][0]}x{k[0][1]}x{k[0][2]}/{k[1]}": [round(v[0], 4), round(v[1], 4)]
+                            for k, v in per.items()},
+            "e2e": e2e,
+            "gpu_launches": int(launches),
+            "clocks": clk.summary(),
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def _e2e(args, cases, names, dev, world):
+    """Same metric through ``bigemm`` with pinned host inputs/outputs."""
+    from omniwave_b200 import bigemm
+
+    host = []
+    for cs in cases:
+        hx = {k: v.detach().cpu().pin_memory() for k, v in cs["leaves"].items()}
+        hd = cs["dout"].cpu().pin_memory()
+        outs = {k: torch.empty(v.shape, dtype=v.dtype).pin_memory() for k, v in cs["leaves"].items()}
+        hout = torch.empty(cs["leaves"]["x"].shape, dtype=torch.bfloat16).pin_memory()
+        host.append((hx, hd, outs, hout))
+    h2d = d2h = 0
+
+    def run_step(count):
+        nonlocal h2d, d2h
+        for cs, (hx, hd, outs, hout) in zip(cases, host):
+            lv = {k: v.to(dev, non_blocking=True).requires_grad_(True) for k, v in hx.items()}
+            go = hd.to(dev, non_blocking=True)
+            out = bigemm(plan=cs["plan"], backend="cuda", **lv)
+            grads = torch.autograd.grad(out, [lv[k] for k in names], go)
+            hout.copy_(out, non_blocking=True)
+            for k, g in zip(names, grads):
+                outs[k].copy_(g, non_blocking=True)
+            if count:
+                h2d += sum(v.numel() * v.element_size() for v in hx.values()) + hd.numel() * hd.element_size()
+                d2h += out.numel() * out.element_size() + sum(g.numel() * g.element_size() for g in grads)
+
+    steps = max(1, min(args.steps, 3))
+    run_step(False)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(steps):
+        run_step(True)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+    val = step_flops(BATCH) * steps * world / (float(ms.item()) * 1e-3) / 1e12
+    return {"value": round(val, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d // steps,
+            "d2h_bytes_per_step": d2h // steps}
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            j = json.load(f)
+        return {"bf16_tflops": float(j["bf16_tflops"]), "hbm_gbs": float(j["hbm_gbs"]),
+                "source": "measured (MEASURED_PEAKS.json, burst)"}
+    except (OSError, KeyError, ValueError):
+        return {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (the oracle restatement of the reference algorithm)
+# ---------------------------------------------------------------------------
+def _cpu_sample_cases(batch):
+    import numpy as np
+
+    from oracle import bigemm as O
+
+    out = []
+    rng = np.random.default_rng(0)
+    for (h, w, c, d) in SHAPES:
+        for route, lvl in ROUTES:
+            p = O.make_plan(h, w, c, G, d, route, lvl)
+            qc = math.ceil(c / d)
+            rd = 2 * d
+            f32 = np.float32
+            ws = [rng.standard_normal((G, G)).astype(f32) / 4 for _ in range(3)]
+            ws += [(rng.standard_normal((qc, d, rd)) / np.sqrt(d)).astype(f32) for _ in range(2)]
+            ws += [(rng.standard_normal((qc, rd, d)) / np.sqrt(rd)).astype(f32),
+                   np.full(c, 1e-5, dtype=f32)]
+            x = rng.standard_normal((batch, h, w, c)).astype(f32)
+            dy = rng.standard_normal((batch, h, w, c)).astype(f32)
+            out.append((p, x, dy, ws, 3.0 * fwd_flops(batch, h, w, c, d)))
+    return out
+
+
+def _cpu_run(cases, seconds):
+    from oracle import bigemm as O
+
+    flops = 0.0
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        for p, x, dy, ws, f in cases:
+            O.forward(x, p, *ws)
+            O.backward(dy, x, p, *ws)
+            flops += f
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return flops, el, reps
+
+
+def _cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def _cpu_baseline(seconds):
+    batch = 2
+    cases = _cpu_sample_cases(batch)
+    flops, el, reps = _cpu_run(cases, seconds)
+    return {"value": round(flops / el / 1e12, 5), "unit": "TFLOP/s", "cores": _cpu_threads(),
+            "kind": "port",
+            "sample": f"oracle numpy float32 fwd+bwd of the 12-case sweep at B={batch} "
+                      f"(x{reps} repetitions, {el:.1f} s)"}
+
+
+def run_reference(args) -> None:
+    world, rank, _ = _dist()
+    if rank != 0:
+        return
+    batch = 2
+    cases = _cpu_sample_cases(batch)
+    _cpu_run(cases[:1], 0.0)  # warm the BLAS threads
+    for _ in range(args.warmup):
+        _cpu_run(cases, 0.0)
+    t0 = time.perf_counter()
+    flops = 0.0
+    for _ in range(args.steps):
+        f, _, _ = _cpu_run(cases, 0.0)
+        flops += f
+    el = time.perf_counter() - t0
+    val = flops / el / 1e12
+    cores = _cpu_threads()
+    sample = f"oracle numpy float32 fwd+bwd of the 12-case sweep at B={batch} per step"
+    print(json.dumps({
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(val, 5),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(el * 1e3 / args.steps, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": "bigemm_sweep_fwd_bwd", "batch_per_step": batch,
+                   "shapes": [f"{h}x{w}x{c}/d{d}" for (h, w, c, d) in SHAPES],
+                   "routes": [f"{r}{l}" for r, l in ROUTES]},
+        "cpu_baseline": {"value": round(val, 5), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(val, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,182 @@
+/*
+ * omniwave_b200 -- C ABI of the B200-native BiGEMM operator.
+ *
+ * BiGEMM (OmniWeave's structured two-sided tiled GEMM) maps an NHWC activation
+ * x[B,H,W,C] to a residual delta of the same shape.  For every spatial tile q_s
+ * (16 tokens chosen by a route plan) and channel group q_c (d channels):
+ *
+ *     T = x[b, tok_idx[q_s,:], ch_idx[q_c,:]]                 (16 x d)
+ *     U = A_u T B_u[q_c],  V = A_v T B_v[q_c]                (16 x rd)
+ *     Z = silu(U) * V
+ *     delta = (A_o Z B_o[q_c]) * mask * gamma[ch]            (16 x d)
+ *
+ * and delta is scattered back to the positions it was gathered from.  This is
+ * the computation of the reference's ``bigemm_delta_reference``
+ * (omniweave/ops/reference.py:120-173) with ``pack_tiles`` (:16-64) and
+ * ``unpack_tiles`` (:67-117) folded into the kernels' loads and stores.
+ *
+ * Conventions
+ *  - All tensor pointers are device pointers owned by the caller; the library
+ *    only borrows them for the duration of the call.  It keeps no state
+ *    between calls except immutable per-device kernel attributes.
+ *  - ``stream`` is a ``cudaStream_t`` passed as ``void*``.  Calls are
+ *    asynchronous on that stream and never synchronise the device.
+ *  - Every entry point returns OW_OK (0) or an error code; no C++ exception
+ *    crosses the ABI.  ``ow_last_error()`` returns a thread-local message for
+ *    the last failing call made by the calling thread.
+ *  - Functions are reentrant: concurrent calls on different streams are safe
+ *    as long as their workspaces do not overlap.
+ */
+#ifndef OMNIWAVE_B200_H
+#define OMNIWAVE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OW_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define OW_API __attribute__((visibility("default")))
+#else
+#define OW_API
+#endif
+
+/* Element types. */
+enum {
+  OW_DTYPE_F32 = 0,
+  OW_DTYPE_F64 = 1,
+  OW_DTYPE_BF16 = 2,
+  OW_DTYPE_F16 = 3
+};
+
+/* Status codes. */
+enum {
+  OW_OK = 0,
+  OW_ERR_INVALID = 1,      /* bad argument: null pointer, shape mismatch, ... */
+  OW_ERR_UNSUPPORTED = 2,  /* valid but not supported (dtype, tile size, device) */
+  OW_ERR_CUDA = 3,         /* a CUDA runtime call or kernel launch failed */
+  OW_ERR_WORKSPACE = 4     /* workspace missing or smaller than required */
+};
+
+/*
+ * Route description of one BiGEMM call.  Mirrors the reference ``RoutePlan``
+ * (omniweave/models/routing.py:17-33): ``tok_idx`` is
+ * ``plan.token_indices`` and ``ch_idx`` is ``plan.channel_indices``, both as
+ * int32 device arrays, with pad index H*W for tokens and C for channels.
+ * Pad entries are exactly the masked-off entries of the reference's masks.
+ * Valid (non-pad) token indices must be distinct, and so must valid channel
+ * indices (every plan the reference builds satisfies this).
+ */
+typedef struct ow_route_t {
+  int32_t batch, height, width, channels; /* B, H, W, C of the NHWC activation */
+  int32_t q_s, q_c;                       /* number of spatial tiles / channel groups */
+  int32_t g, d, rd;                       /* tile tokens (16), channel tile, expanded tile */
+  const int32_t* tok_idx;                 /* [q_s * g] */
+  const int32_t* ch_idx;                  /* [q_c * d] */
+} ow_route_t;
+
+/*
+ * Inputs of a forward (and of the matching backward).
+ *
+ * Operator mode (``rstd == NULL``, ``residual == 0``) computes exactly the
+ * reference ``bigemm(x=..., plan=..., ...)`` delta.  Block mode
+ * (``rstd != NULL``, ``residual == 1``) fuses ``OmniWeaveBlock.forward``
+ * (omniweave/models/block.py:80-108): the tile loads apply RMSNorm
+ * ``x * rstd[token] * norm_w[c]`` and the stores write ``x + scale[b]*delta``.
+ */
+typedef struct ow_bigemm_args_t {
+  ow_route_t route;
+  const void* x;            /* [B,H,W,C] contiguous, dtype x_dtype */
+  int32_t x_dtype;
+  int32_t compute_dtype;    /* F64/F32: exact CUDA-core path; BF16/F16: tensor-core path */
+  const void* rstd;         /* [B*H*W], F64 when compute is F64 else F32; NULL in operator mode */
+  const void* norm_w;       /* [C] RMSNorm weight (block mode only) */
+  const void* a_u;          /* [g,g] */
+  const void* a_v;          /* [g,g] */
+  const void* a_o;          /* [g,g] */
+  const void* b_u;          /* [q_c,d,rd] */
+  const void* b_v;          /* [q_c,d,rd] */
+  const void* b_o;          /* [q_c,rd,d] */
+  const void* gamma;        /* [C] LayerScale */
+  int32_t w_dtype;          /* dtype of norm_w, a_*, b_*, gamma as stored */
+  const float* sample_scale;/* [B] per-sample drop-path scale, or NULL */
+  int32_t residual;         /* 1: out = x + delta (block mode) */
+  void* out;                /* [B,H,W,C], dtype out_dtype (forward only) */
+  int32_t out_dtype;
+  void* workspace;          /* device scratch, >= ow_bigemm_workspace_size() bytes */
+  size_t workspace_bytes;
+} ow_bigemm_args_t;
+
+/* Gradients written by ow_bigemm_bwd (all outputs overwrite, never accumulate). */
+typedef struct ow_bigemm_grads_t {
+  const void* dout;   /* [B,H,W,C] gradient of the forward's out, dtype out_dtype */
+  void* dx;           /* [B,H,W,C] dtype x_dtype (block mode: includes the residual path) */
+  void* da_u;         /* [g,g]     dtype w_dtype */
+  void* da_v;
+  void* da_o;
+  void* db_u;         /* [q_c,d,rd] */
+  void* db_v;
+  void* db_o;         /* [q_c,rd,d] */
+  void* dgamma;       /* [C] */
+  void* dnorm_w;      /* [C] block mode only, else ignored */
+} ow_bigemm_grads_t;
+
+/*
+ * Number of kernels this library has launched in this process (all devices,
+ * all threads).  Lets a caller check that work really ran on the GPU.
+ */
+OW_API uint64_t ow_launch_count(void);
+
+/* ABI version compiled into the library (OW_ABI_VERSION). */
+OW_API int ow_abi_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+OW_API const char* ow_last_error(void);
+
+/*
+ * Returns 1 if ``device`` can run this library's kernels (sm_100a), else 0.
+ * Does not change the current device.
+ */
+OW_API int ow_device_supported(int device);
+
+/*
+ * Bytes of workspace a forward (``for_backward == 0``) or backward
+ * (``for_backward == 1``) call with these arguments needs.  Only the shape
+ * and dtype fields of ``args`` are read.
+ */
+OW_API size_t ow_bigemm_workspace_size(const ow_bigemm_args_t* args, int for_backward);
+
+/*
+ * Per-token reciprocal RMS for the fused block: ``rstd[r] = 1/sqrt(mean_c
+ * x[r,c]^2 + eps)``, the mean taken in float32 as the reference does
+ * (omniweave/models/block.py:83-84).  ``rstd`` is F64 when compute_dtype is
+ * F64, else F32.
+ */
+OW_API int ow_rmsnorm_rstd(const void* x, int32_t x_dtype, int32_t compute_dtype,
+                    int64_t rows, int32_t channels, double eps, void* rstd, void* stream);
+
+/*
+ * Forward.  Replaces the reference's ``bigemm(...)`` dispatch target
+ * (omniweave/ops/bigemm.py:24-73) for backend "cuda", and in block mode the
+ * body of ``OmniWeaveBlock.forward`` (omniweave/models/block.py:80-108).
+ */
+OW_API int ow_bigemm_fwd(const ow_bigemm_args_t* args, void* stream);
+
+/*
+ * Backward of ow_bigemm_fwd with the same ``args`` (``out`` is ignored).
+ * Replaces the autograd backward the reference takes through
+ * ``bigemm_delta_reference`` (and, in block mode, through RMSNorm and the
+ * residual add).  Weight gradients are reduced in a fixed order, so results
+ * are bitwise reproducible run to run.
+ */
+OW_API int ow_bigemm_bwd(const ow_bigemm_args_t* args, const ow_bigemm_grads_t* grads, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OMNIWAVE_B200_H */

@@ -1,0 +1,55 @@
+// Internal interfaces between the C-ABI layer (ow_api.cu) and the kernel
+// files.  Not part of the public ABI.
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "omniwave_b200.h"
+
+namespace ow {
+
+// Shape of one call, derived and validated from ow_route_t.
+struct Prob {
+  int B, H, W, C, N;
+  int Qs, Qc, g, d, rd;
+  const int32_t* tok;  // [Qs*g]
+  const int32_t* ch;   // [Qc*d]
+#ifdef __CUDACC__
+  __host__ __device__
+#endif
+  int64_t BQ() const { return (int64_t)B * Qs; }
+#ifdef __CUDACC__
+  __host__ __device__
+#endif
+  int64_t ntiles() const { return BQ() * Qc; }
+};
+
+// Workspace carve-up helper: hands out aligned sub-ranges of one buffer and
+// tracks the total size (a dry run with base == nullptr measures it).
+struct Carver {
+  char* base;
+  size_t used = 0;
+  explicit Carver(void* b) : base((char*)b) {}
+  void* take(size_t bytes) {
+    used = (used + 255) / 256 * 256;
+    void* p = base ? base + used : nullptr;
+    used += bytes;
+    return p;
+  }
+};
+
+// CUDA-core path (exact fp32 / fp64; also any shape the tensor path lacks).
+int simt_forward(const ow_bigemm_args_t* a, const Prob& p, void* stream, Carver& ws);
+int simt_backward(const ow_bigemm_args_t* a, const ow_bigemm_grads_t* gr, const Prob& p,
+                  void* stream, Carver& ws);
+int rmsnorm_rstd(const void* x, int x_dtype, int compute_dtype, int64_t rows, int C,
+                 double eps, void* rstd, void* stream);
+
+// Tensor-core path (bf16/f16 compute, g=16, d in {64,128}, rd=2d).
+bool tc_supported(const ow_bigemm_args_t* a, const Prob& p, const char** why);
+int tc_forward(const ow_bigemm_args_t* a, const Prob& p, void* stream, Carver& ws);
+int tc_backward(const ow_bigemm_args_t* a, const ow_bigemm_grads_t* gr, const Prob& p,
+                void* stream, Carver& ws);
+
+}  // namespace ow

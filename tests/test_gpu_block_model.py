@@ -1,0 +1,111 @@
+"""Fused block and OmniWeave-T on the GPU against golden vectors.
+
+Block: forward and all gradients of ``OmniWeaveBlock`` (RMSNorm prologue,
+residual epilogue fused) against the reference's autograd (fp64 case;
+tolerance 1e-6 because the reference takes the RMS variance in float32).
+Model: OmniWeave-T logits at 64x64 input against the reference (fp32, TF32 off).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden, rel_err
+from oracle import bigemm as O
+
+pytestmark = pytest.mark.gpu
+
+PARAMS = ("norm_weight", "a_u", "a_v", "a_o", "b_u", "b_v", "b_o", "gamma")
+
+
+def _golden_block(dev, dtype):
+    from omniwave_b200 import OmniWeaveBlock
+
+    z = load_golden("block_f64")
+    blk = OmniWeaveBlock(8, 8, 128, 64, "shifted", 0, layer_scale_init=0.5)
+    with torch.no_grad():
+        for k in PARAMS:
+            getattr(blk, k).copy_(torch.from_numpy(z[f"param_{k}"]))
+    return z, blk.to(device=dev, dtype=dtype)
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float64, 1e-6), (torch.float32, 1e-4)])
+def test_block_matches_reference(cuda_device, dtype, tol):
+    z, blk = _golden_block(cuda_device, dtype)
+    x = torch.tensor(z["in_x"], dtype=dtype, device=cuda_device, requires_grad=True)
+    out = blk(x)
+    assert out.dtype == dtype
+    assert rel_err(out.detach().cpu().numpy(), z["out"]) <= tol
+    grads = torch.autograd.grad(out, [x] + [getattr(blk, k) for k in PARAMS],
+                                torch.tensor(z["dout"], dtype=dtype, device=cuda_device))
+    assert rel_err(grads[0].cpu().numpy(), z["grad_x"]) <= tol
+    for k, g in zip(PARAMS, grads[1:]):
+        assert rel_err(g.cpu().numpy(), z[f"grad_{k}"]) <= tol, k
+
+
+def test_block_autocast_bf16(cuda_device):
+    """fp32 residual stream under bf16 autocast (the training configuration)."""
+    z, blk = _golden_block(cuda_device, torch.float32)
+    x = torch.tensor(z["in_x"], dtype=torch.float32, device=cuda_device, requires_grad=True)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        out = blk(x)
+    assert out.dtype == torch.float32
+    assert rel_err(out.detach().cpu().numpy(), z["out"]) <= 2e-2
+    grads = torch.autograd.grad(out, [x] + [getattr(blk, k) for k in PARAMS],
+                                torch.tensor(z["dout"], dtype=torch.float32, device=cuda_device))
+    assert rel_err(grads[0].cpu().numpy(), z["grad_x"]) <= 2e-2
+    for k, g in zip(PARAMS, grads[1:]):
+        assert rel_err(g.cpu().numpy(), z[f"grad_{k}"]) <= 2e-2, k
+
+
+def test_block_drop_path_scale(cuda_device):
+    """Per-sample drop-path scale is applied to the delta only."""
+    from omniwave_b200.ops import block_forward
+
+    z, blk = _golden_block(cuda_device, torch.float64)
+    x = torch.tensor(z["in_x"], dtype=torch.float64, device=cuda_device)
+    scale = torch.tensor([0.0, 2.0], device=cuda_device)
+    out = block_forward(x, blk.plan, blk.norm_weight, blk.a_u, blk.a_v, blk.a_o, blk.b_u,
+                        blk.b_v, blk.b_o, blk.gamma, scale)
+    ref = O.block_forward(z["in_x"], O.Plan(z["tok"], z["ch"], z["tmask"], z["cmask"], 8, 8, 128),
+                          *[z[f"param_{k}"] for k in PARAMS], scale=np.array([0.0, 2.0]))
+    assert rel_err(out.detach().cpu().numpy(), ref) <= 1e-6
+    assert torch.equal(out[0], x[0])
+
+
+def test_model_logits_match_reference(cuda_device):
+    from omniwave_b200 import create_model
+
+    z = load_golden("model_f32")
+    torch.manual_seed(5)
+    model = create_model("omniweave_t", input_size=64, layer_scale_init=0.5).to(cuda_device).eval()
+    with torch.no_grad():
+        logits = model(torch.from_numpy(z["inp"]).to(cuda_device))
+    assert rel_err(logits.cpu().numpy(), z["logits"]) <= 1e-4
+
+
+def test_model_bf16_inference_and_train_step(cuda_device):
+    from omniwave_b200 import create_model
+
+    torch.manual_seed(0)
+    model = create_model("omniweave_t").to(cuda_device)
+    x = torch.randn(4, 3, 224, 224, device=cuda_device)
+    with torch.no_grad():
+        m16 = create_model("omniweave_t").to(cuda_device).to(torch.bfloat16).eval()
+        m16.load_state_dict(model.state_dict())
+        out = m16(x.to(torch.bfloat16))
+    assert out.shape == (4, 1000) and torch.isfinite(out).all()
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-3, weight_decay=0.05)
+    labels = torch.randint(0, 1000, (4,), device=cuda_device)
+    losses = []
+    for _ in range(3):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = torch.nn.functional.cross_entropy(model(x), labels)
+        opt.zero_grad(set_to_none=True)
+        loss.backward()
+        opt.step()
+        losses.append(float(loss))
+    assert all(np.isfinite(losses))
+    assert all(p.grad is not None and torch.isfinite(p.grad).all() for p in model.parameters())
