@@ -144,6 +144,13 @@ OW_API const char* ow_last_error(void);
 OW_API int ow_device_supported(int device);
 
 /*
+ * Fault word of the tensor-core kernels on ``device``: 0 when no kernel ever
+ * gave up on a bounded wait, otherwise a nonzero code.  Synchronises with the
+ * device.  ``reset`` != 0 clears the word after reading it.
+ */
+OW_API int ow_device_fault(int device, int reset);
+
+/*
  * Bytes of workspace a forward (``for_backward == 0``) or backward
  * (``for_backward == 1``) call with these arguments needs.  Only the shape
  * and dtype fields of ``args`` are read.

@@ -106,6 +106,8 @@ int ow_device_supported(int device) {
   return (major == 10 && minor == 0) ? 1 : 0;
 }
 
+int ow_device_fault(int device, int reset) { return tc_fault(device, reset); }
+
 size_t ow_bigemm_workspace_size(const ow_bigemm_args_t* args, int for_backward) {
   Prob p;
   if (make_prob(args, &p, false) != OW_OK) return 0;

@@ -49,6 +49,7 @@ int rmsnorm_rstd(const void* x, int x_dtype, int compute_dtype, int64_t rows, in
 // Tensor-core path (bf16/f16 compute, g=16, d in {64,128}, rd=2d).
 bool tc_supported(const ow_bigemm_args_t* a, const Prob& p, const char** why);
 int tc_forward(const ow_bigemm_args_t* a, const Prob& p, void* stream, Carver& ws);
+int tc_fault(int device, int reset);
 int tc_backward(const ow_bigemm_args_t* a, const ow_bigemm_grads_t* gr, const Prob& p,
                 void* stream, Carver& ws);
 

@@ -1,0 +1,271 @@
+// sm_100a building blocks for the tensor-core BiGEMM kernels: mbarriers with
+// bounded waits, bulk copies, tcgen05 (TMEM alloc, UMMA issue/commit, TMEM
+// loads), warp-level mma.sync for the 16x16 token mixes, ldmatrix, and the
+// 128-byte-swizzled K-major shared-memory layout the UMMA descriptors use.
+//
+// Layout convention ("SW128 K-major"): an operand with R rows and K columns
+// (K a multiple of 64 16-bit elements) is stored as K/64 "atoms"; atom a holds
+// columns [64a, 64a+64) of every row as one 128-byte line per row, 8-row
+// groups 1024 bytes apart, and the 16-byte chunk j of row r stored at chunk
+// position j ^ (r % 8).  Every atom starts on a 1024-byte boundary.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace ow {
+namespace sm100 {
+
+// Device-wide fault word of the including translation unit: set when a
+// bounded wait gives up (never expected in a correct run).  Read back on the
+// host through ow_device_fault().
+static __device__ int g_fault = 0;
+
+constexpr int kFaultWait = 1;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+                   smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait for the phase with the given parity to complete.  Gives up after
+// kWaitLimitNs of wall time, records a fault and sets *abort so the caller's
+// loops wind down instead of hanging; once *abort is set every wait returns
+// false immediately.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  if (*abort) return false;
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    for (int i = 0; i < 256; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (*abort) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      atomicExch(&g_fault, kFaultWait);
+      *abort = 1;
+      return false;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- bulk copy
+// 1-D global -> shared copy completing on an mbarrier (both addresses 16-byte
+// aligned, size a multiple of 16).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- tcgen05
+__device__ __forceinline__ void tmem_alloc(uint32_t* holder, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(holder)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (bf16/f16 in, f32 acc).
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on ``bar`` once every tcgen05 op this thread issued so far is done.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+// Instruction descriptor: kind::f16, f32 accumulate, A and B K-major.
+// ``bf16`` selects bf16 operands (else f16).
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16) {
+  return (1u << 4)                                   // D format: f32
+         | ((bf16 ? 1u : 0u) << 7)                   // A format
+         | ((bf16 ? 1u : 0u) << 10)                  // B format
+         | ((uint32_t)(N >> 3) << 17)                // N / 8
+         | ((uint32_t)(M >> 4) << 24);               // M / 16
+}
+
+// Shared-memory matrix descriptor for an SW128 K-major operand whose current
+// 16-element K step starts at byte address ``addr`` (inside a 1024-aligned atom).
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFF)          // start address
+         | ((uint64_t)1 << 16)                     // leading byte offset (unused for SW128 K-major)
+         | ((uint64_t)(1024 >> 4) << 32)           // stride byte offset: 8 rows x 128 B
+         | ((uint64_t)1 << 46)                     // descriptor version (sm100)
+         | ((uint64_t)2 << 61);                    // layout: 128-byte swizzle
+}
+
+// Byte offset of element (r, k) in an SW128 K-major operand of ``rows`` rows.
+__host__ __device__ __forceinline__ uint32_t sw128_off(int r, int k, int rows) {
+  return (uint32_t)((k >> 6) * rows * 128 + (r >> 3) * 1024 + (r & 7) * 128 +
+                    ((((k & 63) >> 3) ^ (r & 7)) << 4) + (k & 7) * 2);
+}
+
+// Address of the K step ``kk`` (16 elements) of an SW128 operand at ``base``.
+__device__ __forceinline__ uint32_t sw128_kstep(uint32_t base, int kk, int rows) {
+  return base + (uint32_t)((kk >> 2) * rows * 128 + (kk & 3) * 32);
+}
+
+// TMEM load: 32 lanes x 32 consecutive 32-bit columns (thread i <- lane i).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---------------------------------------------------------------- warp MMA
+template <bool BF16>
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (BF16) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                              uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+// Two floats -> packed 16-bit pair (low = a, high = b).
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  if constexpr (BF16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+
+template <bool BF16>
+__device__ __forceinline__ float2 unpack2(uint32_t v) {
+  if constexpr (BF16) {
+    __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&v);
+    return __bfloat1622float2(h);
+  } else {
+    __half2 h = *reinterpret_cast<__half2*>(&v);
+    return __half22float2(h);
+  }
+}
+
+// silu(u) * v on a packed 16-bit pair, sigmoid via the hardware tanh:
+// sigmoid(u) = 0.5 + 0.5 tanh(u / 2).
+template <bool BF16>
+__device__ __forceinline__ uint32_t silu_mul2(uint32_t u, uint32_t v) {
+  uint32_t out;
+  const uint32_t half2 = BF16 ? 0x3F003F00u : 0x38003800u;  // (0.5, 0.5)
+  if constexpr (BF16) {
+    asm("{\n\t.reg .b32 h, t, s, z;\n\t"
+        "mul.rn.bf16x2 h, %1, %3;\n\t"        // u / 2
+        "tanh.approx.bf16x2 t, h;\n\t"
+        "fma.rn.bf16x2 s, t, %3, %3;\n\t"     // 0.5 t + 0.5 = sigmoid(u)
+        "mul.rn.bf16x2 z, %1, s;\n\t"
+        "mul.rn.bf16x2 %0, z, %2;\n\t}"
+        : "=r"(out)
+        : "r"(u), "r"(v), "r"(half2));
+  } else {
+    asm("{\n\t.reg .b32 h, t, s, z;\n\t"
+        "mul.rn.f16x2 h, %1, %3;\n\t"
+        "tanh.approx.f16x2 t, h;\n\t"
+        "fma.rn.f16x2 s, t, %3, %3;\n\t"
+        "mul.rn.f16x2 z, %1, s;\n\t"
+        "mul.rn.f16x2 %0, z, %2;\n\t}"
+        : "=r"(out)
+        : "r"(u), "r"(v), "r"(half2));
+  }
+  return out;
+}
+
+}  // namespace sm100
+}  // namespace ow

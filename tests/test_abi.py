@@ -23,7 +23,7 @@ def _declared():
 
 
 def test_header_declares_the_bound_functions():
-    assert set(_declared()) == set(_lib.EXPORTS) | {"ow_launch_count"}
+    assert set(_declared()) == set(_lib.EXPORTS)
 
 
 def test_library_exports_every_declared_symbol():
