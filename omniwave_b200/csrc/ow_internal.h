@@ -50,6 +50,18 @@ int rmsnorm_rstd(const void* x, int x_dtype, int compute_dtype, int64_t rows, in
 bool tc_supported(const ow_bigemm_args_t* a, const Prob& p, const char** why);
 int tc_forward(const ow_bigemm_args_t* a, const Prob& p, void* stream, Carver& ws);
 int tc_fault(int device, int reset);
+
+// RMSNorm backward of block mode from the f32 gradient w.r.t. the normalised
+// input (CUDA cores, row-wise).  norm_bwd_take() carves its partials from
+// the workspace (also in a dry run); norm_bwd_run() launches it.
+struct NormBwd {
+  float* part;
+  int grid, nwarps;
+};
+NormBwd norm_bwd_take(int64_t rows, int C, Carver& ws);
+int norm_bwd_run(const NormBwd& nb, const void* x, int x_dt, const void* dout, int dout_dt, const float* rstd,
+                 const float* nw, const float* dxn, int64_t rows, int C, void* dx, void* dnorm_w, int w_dt,
+                 void* stream);
 int tc_backward(const ow_bigemm_args_t* a, const ow_bigemm_grads_t* gr, const Prob& p,
                 void* stream, Carver& ws);
 

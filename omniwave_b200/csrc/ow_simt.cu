@@ -665,6 +665,38 @@ int simt_backward(const ow_bigemm_args_t* a, const ow_bigemm_grads_t* gr, const 
   return simt_backward_t<float>(a, gr, p, st, ws);
 }
 
+NormBwd norm_bwd_take(int64_t rows, int C, Carver& ws) {
+  NormBwd nb;
+  nb.grid = (int)std::min<int64_t>((rows + 63) / 64, 296);
+  nb.nwarps = nb.grid * 8;
+  nb.part = (float*)ws.take((size_t)nb.nwarps * C * sizeof(float));
+  return nb;
+}
+
+int norm_bwd_run(const NormBwd& nb, const void* x, int x_dt, const void* dout, int dout_dt, const float* rstd,
+                 const float* nw, const float* dxn, int64_t rows, int C, void* dx, void* dnorm_w, int w_dt,
+                 void* stream) {
+  cudaStream_t st = (cudaStream_t)stream;
+  auto run = [&](auto* tx, auto* to) -> int {
+    using TX = std::remove_pointer_t<decltype(tx)>;
+    using TO = std::remove_pointer_t<decltype(to)>;
+    return launch_norm_bwd<TX, TO, float>(nb.grid, st, (const TX*)x, rstd, nw, dxn, (const TO*)dout, rows, C,
+                                          (TX*)dx, nb.part);
+  };
+  int rc = dispatch_io<float>(x_dt, dout_dt, run);
+  OW_RETURN_IF(rc);
+  const int gs = grid_for(C);
+  switch (w_dt) {
+    case OW_DTYPE_F32: launch(simt_sum_parts_kernel<float, float>, gs, 256, 0, st, (const float*)nb.part, nb.nwarps, (int64_t)C, 1, (float*)dnorm_w); break;
+    case OW_DTYPE_F64: launch(simt_sum_parts_kernel<float, double>, gs, 256, 0, st, (const float*)nb.part, nb.nwarps, (int64_t)C, 1, (double*)dnorm_w); break;
+    case OW_DTYPE_BF16: launch(simt_sum_parts_kernel<float, __nv_bfloat16>, gs, 256, 0, st, (const float*)nb.part, nb.nwarps, (int64_t)C, 1, (__nv_bfloat16*)dnorm_w); break;
+    case OW_DTYPE_F16: launch(simt_sum_parts_kernel<float, __half>, gs, 256, 0, st, (const float*)nb.part, nb.nwarps, (int64_t)C, 1, (__half*)dnorm_w); break;
+    default: set_error("unsupported weight dtype"); return OW_ERR_UNSUPPORTED;
+  }
+  OW_CHECK_LAUNCH("norm weight reduction");
+  return OW_OK;
+}
+
 int rmsnorm_rstd(const void* x, int x_dtype, int compute_dtype, int64_t rows, int C, double eps,
                  void* rstd, void* stream) {
   cudaStream_t st = (cudaStream_t)stream;

@@ -644,10 +644,4 @@ int tc_forward(const ow_bigemm_args_t* a, const Prob& p, void* stream, Carver& w
   return bf ? tc_forward_t<128, true>(a, p, st, ws) : tc_forward_t<128, false>(a, p, st, ws);
 }
 
-int tc_backward(const ow_bigemm_args_t* a, const ow_bigemm_grads_t* gr, const Prob& p, void* stream,
-                Carver& ws) {
-  // Backward runs on the CUDA-core path until the tensor-core backward lands.
-  return simt_backward(a, gr, p, stream, ws);
-}
-
 }  // namespace ow

@@ -1,0 +1,1120 @@
+// Tensor-core BiGEMM backward for sm_100a (bf16 / f16 compute, g = 16,
+// d in {64, 128}, rd = 2d).
+//
+// The gradient of the forward (reference.py:147-171, taken by autograd in the
+// reference) is, per tile with G' = mask * scale * dOut and G = G' * gamma:
+//
+//   dY' = A_o^T G             dZ = dY' B_o^T          (Z = silu(U) * V)
+//   dU  = dZ * V * silu'(U)   dV = dZ * silu(U)
+//   dP_u = dU B_u^T           dP_v = dV B_v^T
+//   dT  = A_u^T dP_u + A_v^T dP_v                          -> dX (scattered)
+//   dA_u = sum dP_u T^T,  dA_v = sum dP_v T^T,  dA_o = sum G (Z B_o)^T
+//   dB_u = sum P_u^T dU,  dB_v = sum P_v^T dV
+//   M_o  = sum (A_o Z)^T G'  ->  dB_o = M_o * gamma,  dgamma = sum_e B_o * M_o
+//
+// The weight gradients sum over every tile of a channel group; their f32
+// accumulators (3 x d x rd) do not fit one SM's 512 TMEM columns next to the
+// working set at d = 128, so one persistent launch runs three CTA roles that
+// each recompute the forward operands they need from x and dOut:
+//
+//   DGRAD  (any item)      U, V, dZ -> dU, dV -> dP_u, dP_v (TMEM)   -> dX, dA_u, dA_v
+//   UV(h)  (one group)     U, V, dZ on rd half h -> dU, dV -> TMEM += dU^T P_u, dV^T P_v
+//   O      (one group)     U, V -> Z -> A_o Z; TMEM Y += Z B_o, M_o += (A_o Z)^T G'  -> dA_o
+//
+// The UV and O weight-gradient products read the token-major tiles already
+// in shared memory through MN-major UMMA descriptors.  Each CTA writes f32
+// partials; a reduction kernel sums them in a fixed order (bitwise
+// reproducible).  Per-role thread layout is the forward's: 8 compute warps,
+// one MMA-issuing warp that owns TMEM, one warp streaming weight chunks.
+
+#include <algorithm>
+#include <type_traits>
+
+#include "ow_common.cuh"
+#include "ow_internal.h"
+#include "ow_sm100.cuh"
+
+namespace ow {
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128;
+constexpr int NC = 64;
+constexpr int NCOMP_WARPS = 8;
+constexpr int NCOMP = NCOMP_WARPS * 32;
+constexpr int MMA_WARP = NCOMP_WARPS;
+constexpr int PROD_WARP = NCOMP_WARPS + 1;
+constexpr int TC_THREADS = (NCOMP_WARPS + 2) * 32;
+constexpr int STG_LD = 72;
+constexpr int STG_BYTES = BM * STG_LD * 2;
+constexpr int TMEM_COLS = 512;
+
+enum Role { R_DGRAD = 0, R_UV = 1, R_O = 2 };
+
+template <int D>
+struct BCfg {
+  static constexpr int RD = 2 * D;
+  static constexpr int NQ = RD / NC;
+  static constexpr int NQH = 2;                 // chunks per 128-feature half
+  static constexpr int NH = RD / 128;           // halves
+  static constexpr int P_BYTES = BM * D * 2;
+  static constexpr int Z_BYTES = BM * NC * 2;   // 16 KB
+  static constexpr int BU_BYTES = NC * D * 2;   // one weight sub-image
+  static constexpr int IMG_BYTES = 6 * BU_BYTES;  // Bu | Bv | BoT | BuT | BvT | Bo
+  // Shared-memory plans (bytes).  Common: P_u at 0, P_v at P, X1 at 2P.
+  static constexpr int OFF_PU = 0, OFF_PV = P_BYTES, OFF_X1 = 2 * P_BYTES;
+  // DGRAD
+  static constexpr int D_S = 3 * P_BYTES;                    // dU | dV (chunk)
+  static constexpr int D_W = D_S + 2 * Z_BYTES;              // g1 (3 sub) | g2 (2 sub)
+  static constexpr int D_END = D_W + 5 * BU_BYTES;
+  // UV
+  static constexpr int U_S = 3 * P_BYTES;                    // dU_h | dV_h (128 features each)
+  static constexpr int U_W = U_S + 4 * Z_BYTES;
+  static constexpr int U_END = U_W + 3 * BU_BYTES;
+  // O
+  static constexpr int O_Z = 3 * P_BYTES;
+  static constexpr int O_ZO = O_Z + Z_BYTES;                 // pair of chunks (128 features)
+  static constexpr int O_W = O_ZO + 2 * Z_BYTES;             // Bu | Bv | Bo
+  static constexpr int O_END = O_W + 3 * BU_BYTES;
+  static constexpr int MAX_END = D_END > U_END ? (D_END > O_END ? D_END : O_END) : (U_END > O_END ? U_END : O_END);
+  static constexpr int OFF_META = MAX_END;
+  static constexpr int META_BYTES = (2 * BM + D) * 4;
+  static constexpr int OFF_BAR = OFF_META + META_BYTES;
+  static constexpr int BAR_BYTES = 16 * 8 + 16;
+  static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024;
+  static_assert(SMEM <= 232448, "shared memory budget");
+  static_assert(3 * STG_BYTES <= 3 * P_BYTES + 2 * Z_BYTES, "epilogue staging alias");
+  // TMEM columns.
+  static constexpr int T_U = 0, T_V = 64, T_DZ = 128;
+  static constexpr int T_DPU = 256, T_DPV = 256 + D;          // DGRAD
+  static constexpr int T_ACCU = 256, T_ACCV = 256 + D;        // UV
+  static constexpr int T_Y = 128, T_ACCO = 256;               // O (NH blocks of D)
+  static_assert(T_DPV + D <= TMEM_COLS && T_ACCO + NH * D <= TMEM_COLS, "TMEM budget");
+};
+
+// Grid plan and workspace layout (bytes).
+template <int D>
+struct BPlan {
+  int nD, nUVq, nOq, nH, grid;
+  size_t img, amat, gg, nw, contig, pdA, pdAo, puv, po, dxn, total;
+  BPlan(const Prob& p, bool block, int sms) {
+    using C = BCfg<D>;
+    nH = C::NH;
+    // Split one wave of CTAs by the roles' relative tensor work per item:
+    // DGRAD 5, UV 2.5 per half (5 for d=64's single half), O 4.
+    const double wD = 5.0, wU = (D == 64 ? 5.0 : 2.5) * nH, wO = 4.0, tot = wD + wU + wO;
+    const int64_t nMB = (p.BQ() + 7) / 8;
+    nUVq = std::max(1, (int)(sms * (wU / nH) / tot) / p.Qc);
+    nOq = std::max(1, (int)(sms * wO / tot) / p.Qc);
+    nUVq = (int)std::min<int64_t>(nUVq, nMB);
+    nOq = (int)std::min<int64_t>(nOq, nMB);
+    nD = std::max(1, sms - nH * p.Qc * nUVq - p.Qc * nOq);
+    nD = (int)std::min<int64_t>(nD, nMB * p.Qc);
+    grid = nD + nH * p.Qc * nUVq + p.Qc * nOq;
+    size_t o = 0;
+    auto take = [&](size_t n) { size_t r = o; o = (o + n + 255) / 256 * 256; return r; };
+    img = take((size_t)p.Qc * C::NQ * C::IMG_BYTES);
+    amat = take(3 * 256 * 2);
+    gg = take((size_t)p.Qc * D * 4);
+    nw = take((size_t)p.C * 4);
+    contig = take((size_t)p.Qc * 4);
+    pdA = take((size_t)nD * NCOMP_WARPS * 2 * 256 * 4);
+    pdAo = take((size_t)p.Qc * nOq * NCOMP_WARPS * 256 * 4);
+    puv = take((size_t)nH * p.Qc * nUVq * 2 * 128 * D * 4);
+    po = take((size_t)p.Qc * nOq * C::RD * D * 4);
+    dxn = block ? take((size_t)p.B * p.N * p.C * 4) : 0;
+    total = o;
+  }
+};
+
+// ---------------------------------------------------------------------------
+// Weight preparation (same conventions as the forward's prep kernel).
+// ---------------------------------------------------------------------------
+template <int D, typename TW, bool BF16>
+__global__ void tc_bwd_prep_kernel(Prob p, const TW* __restrict__ au, const TW* __restrict__ av,
+                                   const TW* __restrict__ ao, const TW* __restrict__ bu,
+                                   const TW* __restrict__ bv, const TW* __restrict__ bo,
+                                   const TW* __restrict__ gamma, const TW* __restrict__ nw_in,
+                                   unsigned char* __restrict__ img, uint16_t* __restrict__ amat,
+                                   float* __restrict__ gg, float* __restrict__ nw, int* __restrict__ contig) {
+  using C = BCfg<D>;
+  using T16 = std::conditional_t<BF16, __nv_bfloat16, __half>;
+  const int64_t per_sub = (int64_t)NC * D;
+  const int64_t per_chunk = 6 * per_sub;
+  const int64_t n_img = (int64_t)p.Qc * C::NQ * per_chunk;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  for (int64_t i = tid; i < n_img; i += stride) {
+    const int64_t chunk = i / per_chunk;
+    const int e = (int)(i - chunk * per_chunk);
+    const int sub = (int)(e / per_sub), r = (int)(e - sub * per_sub);
+    const int qc = (int)(chunk / C::NQ), q = (int)(chunk - (int64_t)qc * C::NQ);
+    const int f0 = q * NC;
+    float v;
+    uint32_t off;
+    if (sub < 3) {  // rows = 64 features n, K = D channels k
+      const int n = r / D, k = r - n * D;
+      if (sub == 0) v = load_as<float>(bu, ((int64_t)qc * D + k) * C::RD + f0 + n);
+      else if (sub == 1) v = load_as<float>(bv, ((int64_t)qc * D + k) * C::RD + f0 + n);
+      else v = load_as<float>(bo, ((int64_t)qc * C::RD + f0 + n) * D + k);
+      off = sub * C::BU_BYTES + sw128_off(n, k, NC);
+    } else {  // rows = D channels n, K = 64 features k
+      const int n = r / NC, k = r - n * NC;
+      if (sub == 3) v = load_as<float>(bu, ((int64_t)qc * D + n) * C::RD + f0 + k);
+      else if (sub == 4) v = load_as<float>(bv, ((int64_t)qc * D + n) * C::RD + f0 + k);
+      else v = load_as<float>(bo, ((int64_t)qc * C::RD + f0 + k) * D + n);
+      off = sub * C::BU_BYTES + sw128_off(n, k, D);
+    }
+    *reinterpret_cast<T16*>(img + chunk * C::IMG_BYTES + off) = Elem<T16>::from(v);
+  }
+  for (int64_t i = tid; i < 3 * 256; i += stride) {
+    const TW* src = i < 256 ? au : (i < 512 ? av : ao);
+    T16 h = Elem<T16>::from(load_as<float>(src, i & 255));
+    amat[i] = *reinterpret_cast<uint16_t*>(&h);
+  }
+  for (int64_t i = tid; i < (int64_t)p.Qc * D; i += stride) {
+    const int c = p.ch[i];
+    gg[i] = c < p.C ? load_as<float>(gamma, c) : 0.f;
+  }
+  if (nw_in)
+    for (int64_t i = tid; i < p.C; i += stride) nw[i] = load_as<float>(nw_in, i);
+  for (int64_t qc = tid; qc < p.Qc; qc += stride) {
+    const int c0 = p.ch[qc * D];
+    int ok = (c0 % 8 == 0) && (c0 + D <= p.C) && (p.C % 8 == 0);
+    for (int k = 1; k < D && ok; ++k) ok = p.ch[qc * D + k] == c0 + k;
+    contig[qc] = ok;
+  }
+}
+
+__device__ __forceinline__ void comp_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NCOMP) : "memory"); }
+
+// Instruction descriptor with both operands MN-major (weight-gradient products).
+__host__ __device__ constexpr uint32_t idesc_f16_mn(int M, int N, bool bf16) {
+  return idesc_f16(M, N, bf16) | (1u << 15) | (1u << 16);
+}
+
+// Descriptor of an SW128 tile read MN-major: 64-element MN atoms ``lbo`` bytes
+// apart, 8-row K groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t sdesc_sw128_mn(uint32_t addr, uint32_t lbo) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// m16n8k16 A fragment of a 16x16 matrix in shared/global row-major 16-bit
+// storage (optionally transposed).
+__device__ __forceinline__ void load_afrag(const uint16_t* A, bool trans, int g, int t4, uint32_t (&f)[4]) {
+  auto el = [&](int m, int k) -> uint32_t { return trans ? A[k * 16 + m] : A[m * 16 + k]; };
+  f[0] = el(g, 2 * t4) | (el(g, 2 * t4 + 1) << 16);
+  f[1] = el(g + 8, 2 * t4) | (el(g + 8, 2 * t4 + 1) << 16);
+  f[2] = el(g, 2 * t4 + 8) | (el(g, 2 * t4 + 9) << 16);
+  f[3] = el(g + 8, 2 * t4 + 8) | (el(g + 8, 2 * t4 + 9) << 16);
+}
+
+template <typename T>
+__device__ __forceinline__ void load8v(const T* __restrict__ src, float (&v)[8]) {
+  if constexpr (sizeof(T) == 2) {
+    uint4 u = __ldg(reinterpret_cast<const uint4*>(src));
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 f = unpack2<std::is_same_v<T, __nv_bfloat16>>(w[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  } else {
+    float4 a = __ldg(reinterpret_cast<const float4*>(src));
+    float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+}
+
+struct GatherCtx {
+  const int* tok;   // [BM] token or -1
+  const int* rowb;  // [BM] batch
+  const int* ch;    // [D] channel indices
+  int N, C;
+  bool cont;
+};
+
+// Gather one 64-channel half of the M-block (128 rows) into 16-bit storage.
+// src element (row, ch) times (rstd[row] * nw[ch]) in x mode, times
+// scale[b] * (gg[k] if given) in gradient mode.  ``sw`` selects the SW128
+// K-major layout (rows BM) instead of the padded row-major staging layout.
+template <typename TS, bool BF16>
+__device__ __forceinline__ void gather_half(const GatherCtx& gc, const TS* __restrict__ src, int hf,
+                                            const float* __restrict__ rstd, const float* __restrict__ nw,
+                                            int x_dt, const float* __restrict__ scale,
+                                            const float* __restrict__ ggq, unsigned char* dst, bool sw, int tid) {
+  auto offs = [&](int r, int k) -> uint32_t {
+    return sw ? sw128_off(r, k, BM) : (uint32_t)((r * STG_LD + (k & 63)) * 2);
+  };
+  if (gc.cont) {
+    const int ch0 = gc.ch[0];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int unit = tid + u * NCOMP;
+      const int r = unit >> 3, cj = unit & 7;
+      const int k = hf * 64 + cj * 8;
+      float v[8];
+      const int tok = gc.tok[r];
+      if (tok >= 0) {
+        const int64_t row = (int64_t)gc.rowb[r] * gc.N + tok;
+        const int ch = ch0 + k;
+        load8v<TS>(src + row * gc.C + ch, v);
+        if (rstd) {
+          const float rs = rstd[row];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            float t = round_through(v[e] * rs, x_dt);
+            v[e] = round_through(t * nw[ch + e], x_dt);
+          }
+        }
+        const float s = scale ? scale[gc.rowb[r]] : 1.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] *= s * (ggq ? ggq[k + e] : 1.f);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = 0.f;
+      }
+      uint4 w;
+      w.x = pack2<BF16>(v[0], v[1]);
+      w.y = pack2<BF16>(v[2], v[3]);
+      w.z = pack2<BF16>(v[4], v[5]);
+      w.w = pack2<BF16>(v[6], v[7]);
+      *reinterpret_cast<uint4*>(dst + offs(r, k)) = w;
+    }
+  } else {
+    for (int e = tid; e < BM * 64; e += NCOMP) {
+      const int r = e >> 6, k = hf * 64 + (e & 63);
+      const int tok = gc.tok[r], ch = gc.ch[k];
+      float v = 0.f;
+      if (tok >= 0 && ch < gc.C) {
+        const int64_t row = (int64_t)gc.rowb[r] * gc.N + tok;
+        v = load_as<float>(src, row * gc.C + ch);
+        if (rstd) {
+          v = round_through(v * rstd[row], x_dt);
+          v = round_through(v * nw[ch], x_dt);
+        }
+        v *= (scale ? scale[gc.rowb[r]] : 1.f) * (ggq ? ggq[k] : 1.f);
+      }
+      const uint32_t pk = pack2<BF16>(v, 0.f);
+      *reinterpret_cast<uint16_t*>(dst + offs(r, k)) = (uint16_t)(pk & 0xFFFF);
+    }
+  }
+}
+
+// Token mix of one 64-channel half: dst[rows of tile ``warp``] = A * staging,
+// written in SW128 K-major layout at channel offset hf*64.
+template <bool BF16>
+__device__ __forceinline__ void mix_half(uint32_t aStg, const uint32_t (&fa)[4], unsigned char* dst, int hf,
+                                         int warp, int lane) {
+  const int g = lane >> 2, t4 = lane & 3;
+#pragma unroll
+  for (int np = 0; np < 4; ++np) {
+    uint32_t b0, b1, b2, b3;
+    ldsm_x4_trans(aStg + ((warp * 16 + (lane & 15)) * STG_LD + np * 16 + (lane >> 4) * 8) * 2, b0, b1, b2, b3);
+    float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+    mma16816<BF16>(c0, fa, b0, b1);
+    mma16816<BF16>(c1, fa, b2, b3);
+    const int r0 = warp * 16 + g, k0 = hf * 64 + np * 16 + 2 * t4;
+    *reinterpret_cast<uint32_t*>(dst + sw128_off(r0, k0, BM)) = pack2<BF16>(c0[0], c0[1]);
+    *reinterpret_cast<uint32_t*>(dst + sw128_off(r0 + 8, k0, BM)) = pack2<BF16>(c0[2], c0[3]);
+    *reinterpret_cast<uint32_t*>(dst + sw128_off(r0, k0 + 8, BM)) = pack2<BF16>(c1[0], c1[1]);
+    *reinterpret_cast<uint32_t*>(dst + sw128_off(r0 + 8, k0 + 8, BM)) = pack2<BF16>(c1[2], c1[3]);
+  }
+}
+
+// acc[nb] (16x8 blocks nb = 0,1 of a 16x16 result) += L[16 x 64] * R[16 x 64]^T
+// for the tile of ``warp``.  L rows come from ``lrow(row, col)`` addresses,
+// R rows from ``rrow(row, col)`` (both 16-bit, 16-byte chunks contiguous).
+template <bool BF16, typename LA, typename RA>
+__device__ __forceinline__ void gram16(float (&acc)[2][4], LA lrow, RA rrow, int lane) {
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) {
+    const int k0 = ks * 16;
+    uint32_t a[4], b[4];
+    ldsm_x4(lrow((lane & 7) + ((lane >> 3) & 1) * 8, k0 + (lane >> 4) * 8), a[0], a[1], a[2], a[3]);
+    ldsm_x4(rrow((lane & 7) + (lane >> 4) * 8, k0 + ((lane >> 3) & 1) * 8), b[0], b[1], b[2], b[3]);
+    mma16816<BF16>(acc[0], a, b[0], b[1]);
+    mma16816<BF16>(acc[1], a, b[2], b[3]);
+  }
+}
+
+__device__ __forceinline__ float sigm_fast(float u) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * u));
+  return fmaf(0.5f, t, 0.5f);
+}
+
+struct BwdArgs {
+  Prob p;
+  const void* x;
+  const void* dout;
+  const float* rstd;
+  const float* scale;
+  int x_dt;
+  const unsigned char* img;
+  const uint16_t* amat;
+  const float* gg;
+  const float* nw;
+  const int* contig;
+  int vec_ok;
+  void* dx;       // operator mode: x dtype
+  float* dxn;     // block mode
+  float* pdA;     // [nD][8][2][256]
+  float* pdAo;    // [Qc*nOq][8][256]
+  float* puv;     // [nH*Qc*nUVq][2][128][D]
+  float* po;      // [Qc*nOq][RD][D]
+  int nD, nUVq, nOq, nH;
+};
+
+template <int D, bool BF16, typename TX, typename TO>
+__global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
+  using C = BCfg<D>;
+  const Prob& p = a.p;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  unsigned char* sPu = sm + C::OFF_PU;
+  unsigned char* sPv = sm + C::OFF_PV;
+  unsigned char* sX1 = sm + C::OFF_X1;
+  int* sTok = reinterpret_cast<int*>(sm + C::OFF_META);
+  int* sRowB = sTok + BM;
+  int* sCh = sRowB + BM;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
+  uint64_t* bar_p = bars + 0;
+  uint64_t* bar_a = bars + 1;
+  uint64_t* bar_du = bars + 2;
+  uint64_t* bar_b = bars + 3;
+  uint64_t* bar_w = bars + 4;
+  uint64_t* bar_zo = bars + 5;
+  uint64_t* bar_g1 = bars + 6;
+  uint64_t* bar_g2 = bars + 7;
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t BQ = (int64_t)p.B * p.Qs;
+  const int nMB = (int)((BQ + 7) / 8);
+
+  // ---- role of this CTA and its item range
+  int role, qc_fix = 0, h = 0, wslot = 0;
+  int64_t it0 = 0, it_step = 1, n_items = 0;
+  {
+    const int b = blockIdx.x;
+    const int nUV = a.nH * p.Qc * a.nUVq;
+    if (b < a.nD) {
+      role = R_DGRAD;
+      it0 = b;
+      it_step = a.nD;
+      const int64_t items = (int64_t)p.Qc * nMB;
+      n_items = items > b ? (items - 1 - b) / a.nD + 1 : 0;
+    } else {
+      int local, nq;
+      if (b < a.nD + nUV) {
+        role = R_UV;
+        local = b - a.nD;
+        h = local / (p.Qc * a.nUVq);
+        local -= h * p.Qc * a.nUVq;
+        nq = a.nUVq;
+        wslot = (h * p.Qc + local / nq) * nq + local % nq;
+      } else {
+        role = R_O;
+        local = b - a.nD - nUV;
+        nq = a.nOq;
+        wslot = local;
+      }
+      qc_fix = local / nq;
+      const int j = local % nq;
+      const int64_t m0 = (int64_t)nMB * j / nq, m1 = (int64_t)nMB * (j + 1) / nq;
+      it0 = (int64_t)qc_fix * nMB + m0;
+      it_step = 1;
+      n_items = m1 - m0;
+    }
+  }
+  const int nchunks = role == R_UV ? C::NQH : C::NQ;
+  const int q_base = role == R_UV ? h * C::NQH : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_p, NCOMP);
+    mbar_init(bar_a, 1);
+    mbar_init(bar_du, NCOMP);
+    mbar_init(bar_b, 1);
+    mbar_init(bar_w, 1);
+    mbar_init(bar_zo, NCOMP);
+    mbar_init(bar_g1, 1);
+    mbar_init(bar_g2, 1);
+    *sAbort = 0;
+    fence_mbar_init();
+  }
+  if (warp == MMA_WARP) tmem_alloc(sTmem, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *sTmem;
+
+  // Weight sub-image groups per role: g1 = first group (bytes from the chunk
+  // image start), g2 = second group.
+  int g1_off = 0, g1_bytes = 0, g2_off = 0, g2_bytes = 0;
+  unsigned char* sW = nullptr;
+  if (role == R_DGRAD) {
+    sW = sm + C::D_W; g1_off = 0; g1_bytes = 3 * C::BU_BYTES; g2_off = 3 * C::BU_BYTES; g2_bytes = 2 * C::BU_BYTES;
+  } else if (role == R_UV) {
+    sW = sm + C::U_W; g1_off = 0; g1_bytes = 3 * C::BU_BYTES;
+  } else {
+    sW = sm + C::O_W; g1_off = 0; g1_bytes = 2 * C::BU_BYTES; g2_off = 5 * C::BU_BYTES; g2_bytes = C::BU_BYTES;
+  }
+  unsigned char* sW2 = sW + g1_bytes;
+  const int total_chunks = (int)n_items * nchunks;
+  auto chunk_img = [&](int c) {
+    const int it = c / nchunks, j = c - it * nchunks;
+    const int64_t item = it0 + (int64_t)it * it_step;
+    const int qc = (int)(item / nMB);
+    return a.img + ((int64_t)qc * C::NQ + q_base + j) * C::IMG_BYTES;
+  };
+
+  if (warp == PROD_WARP) {
+    // ------------------------------------------------ weight producer
+    if (lane == 0 && total_chunks > 0) {
+      auto load1 = [&](int c) {
+        mbar_arrive_expect_tx(bar_g1, g1_bytes);
+        bulk_g2s(sW, chunk_img(c) + g1_off, g1_bytes, bar_g1);
+      };
+      auto load2 = [&](int c) {
+        mbar_arrive_expect_tx(bar_g2, g2_bytes);
+        bulk_g2s(sW2, chunk_img(c) + g2_off, g2_bytes, bar_g2);
+      };
+      load1(0);
+      if (g2_bytes) load2(0);
+      for (int c = 0; c + 1 < total_chunks; ++c) {
+        if (mbar_wait(bar_a, c & 1, sAbort)) load1(c + 1);
+        if (g2_bytes && mbar_wait(bar_b, c & 1, sAbort)) load2(c + 1);
+        if (*sAbort) break;
+      }
+    }
+  } else if (warp == MMA_WARP) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t ID_N64 = idesc_f16(BM, NC, BF16);
+      constexpr uint32_t ID_ND = idesc_f16(BM, D, BF16);
+      constexpr uint32_t ID_MN = idesc_f16_mn(BM, D, BF16);
+      const uint32_t aPu = smem_u32(sPu), aPv = smem_u32(sPv), aX1 = smem_u32(sX1);
+      const uint32_t aW = smem_u32(sW);
+      auto kmma = [&](uint32_t tcol, uint32_t aA, int arows, uint32_t aB, int brows, int ksteps, uint32_t id,
+                      bool acc0) {
+        for (int kk = 0; kk < ksteps; ++kk)
+          umma_f16(tbase + tcol, sdesc_sw128(sw128_kstep(aA, kk, arows)), sdesc_sw128(sw128_kstep(aB, kk, brows)),
+                   id, (acc0 || kk > 0) ? 1u : 0u);
+      };
+      auto mnmma = [&](uint32_t tcol, uint32_t aA, uint32_t aB, bool acc0) {
+        for (int kk = 0; kk < BM / 16; ++kk)
+          umma_f16(tbase + tcol, sdesc_sw128_mn(aA + kk * 2048, BM * 128), sdesc_sw128_mn(aB + kk * 2048, BM * 128),
+                   ID_MN, (acc0 || kk > 0) ? 1u : 0u);
+      };
+      int c = 0, pc = 0;
+      for (int it = 0; it < (int)n_items; ++it) {
+        mbar_wait(bar_p, it & 1, sAbort);
+        tc_fence_after();
+        for (int j = 0; j < nchunks; ++j, ++c) {
+          mbar_wait(bar_g1, c & 1, sAbort);
+          tc_fence_after();
+          if (!*sAbort) {
+            kmma(C::T_U, aPu, BM, aW, NC, D / 16, ID_N64, false);
+            kmma(C::T_V, aPv, BM, aW + C::BU_BYTES, NC, D / 16, ID_N64, false);
+            if (role != R_O) kmma(C::T_DZ, aX1, BM, aW + 2 * C::BU_BYTES, NC, D / 16, ID_N64, false);
+          }
+          umma_commit(bar_a);
+          mbar_wait(bar_du, c & 1, sAbort);
+          tc_fence_after();
+          if (role == R_DGRAD) {
+            mbar_wait(bar_g2, c & 1, sAbort);
+            tc_fence_after();
+            if (!*sAbort) {
+              const uint32_t aS = smem_u32(sm + C::D_S);
+              kmma(C::T_DPU, aS, BM, aW + 3 * C::BU_BYTES, D, NC / 16, ID_ND, j > 0);
+              kmma(C::T_DPV, aS + C::Z_BYTES, BM, aW + 4 * C::BU_BYTES, D, NC / 16, ID_ND, j > 0);
+            }
+            umma_commit(bar_b);
+          } else if (role == R_O) {
+            mbar_wait(bar_g2, c & 1, sAbort);
+            tc_fence_after();
+            if (!*sAbort) kmma(C::T_Y, smem_u32(sm + C::O_Z), BM, smem_u32(sW2), D, NC / 16, ID_ND, j > 0);
+            umma_commit(bar_b);
+            if (j & 1) {
+              mbar_wait(bar_zo, pc & 1, sAbort);
+              tc_fence_after();
+              if (!*sAbort)
+                mnmma(C::T_ACCO + (j >> 1) * D, smem_u32(sm + C::O_ZO), aX1, it > 0);
+              umma_commit(bar_w);
+              ++pc;
+            }
+          }
+        }
+        if (role == R_UV) {
+          if (!*sAbort) {
+            const uint32_t aS = smem_u32(sm + C::U_S);
+            mnmma(C::T_ACCU, aS, aPu, it > 0);
+            mnmma(C::T_ACCV, aS + 2 * C::Z_BYTES, aPv, it > 0);
+          }
+          umma_commit(bar_w);
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------ compute warps
+    const int tid = threadIdx.x;
+    const int g = lane >> 2, t4 = lane & 3;
+    const int lq = warp & 3, cb = (warp >> 2) * 32;
+    const int r = lq * 32 + lane;
+    const uint32_t trow = tbase + ((uint32_t)(lq * 32) << 16);
+    uint32_t fAoT[4], fAuT[4], fAvT[4], fAo[4];
+    load_afrag(a.amat + 512, true, g, t4, fAoT);
+    load_afrag(a.amat + 0, true, g, t4, fAuT);
+    load_afrag(a.amat + 256, true, g, t4, fAvT);
+    load_afrag(a.amat + 512, false, g, t4, fAo);
+    uint32_t fAu[4], fAv[4];
+    load_afrag(a.amat + 0, false, g, t4, fAu);
+    load_afrag(a.amat + 256, false, g, t4, fAv);
+    float accA[2][2][4] = {};  // DGRAD: dA_u, dA_v ; O: dA_o in accA[0]
+    const TX* x = (const TX*)a.x;
+    const TO* dout = (const TO*)a.dout;
+    int c = 0, pc = 0;
+    unsigned char* stg_a = role == R_O ? sm + C::O_Z : sm + C::D_S;  // phase-A staging
+    for (int it = 0; it < (int)n_items; ++it) {
+      const int64_t item = it0 + (int64_t)it * it_step;
+      const int qc = (int)(item / nMB), mb = (int)(item - (int64_t)qc * nMB);
+      GatherCtx gc{sTok, sRowB, sCh, p.N, p.C, a.vec_ok && a.contig[qc] != 0};
+      const float* ggq = a.gg + (int64_t)qc * D;
+      // UV: the previous item's weight-gradient products read P and dU/dV.
+      if (role == R_UV && it > 0) {
+        mbar_wait(bar_w, (it - 1) & 1, sAbort);
+        __syncwarp();
+      }
+      if (role == R_O && it > 0) {
+        mbar_wait(bar_w, (pc - 1) & 1, sAbort);
+        __syncwarp();
+      }
+      comp_sync();
+      for (int rr = tid; rr < BM; rr += NCOMP) {
+        const int64_t t = (int64_t)mb * 8 + (rr >> 4);
+        int tok = p.N, b = 0;
+        if (t < BQ) {
+          b = (int)(t / p.Qs);
+          tok = p.tok[(t - (int64_t)b * p.Qs) * 16 + (rr & 15)];
+        }
+        sTok[rr] = tok < p.N ? tok : -1;
+        sRowB[rr] = b;
+      }
+      for (int k = tid; k < D; k += NCOMP) sCh[k] = p.ch[qc * D + k];
+      comp_sync();
+      // ---- phase A: P_u, P_v from x; dY' (or G') from dOut
+      const uint32_t aStg = smem_u32(stg_a);
+      for (int hf = 0; hf < D / 64; ++hf) {
+        gather_half<TX, BF16>(gc, x, hf, a.rstd, a.nw, a.x_dt, nullptr, nullptr, stg_a, false, tid);
+        comp_sync();
+        __syncwarp();
+        mix_half<BF16>(aStg, fAu, sPu, hf, warp, lane);
+        mix_half<BF16>(aStg, fAv, sPv, hf, warp, lane);
+        comp_sync();
+        if (role == R_O) {
+          gather_half<TO, BF16>(gc, dout, hf, nullptr, nullptr, 0, a.scale, nullptr, sX1, true, tid);
+        } else {
+          gather_half<TO, BF16>(gc, dout, hf, nullptr, nullptr, 0, a.scale, ggq, stg_a, false, tid);
+          comp_sync();
+          __syncwarp();
+          mix_half<BF16>(aStg, fAoT, sX1, hf, warp, lane);
+          comp_sync();
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(bar_p);
+
+      // ---- chunk loop
+      for (int j = 0; j < nchunks; ++j, ++c) {
+        mbar_wait(bar_a, c & 1, sAbort);
+        __syncwarp();
+        tc_fence_after();
+        uint32_t ur[32], vr[32], zr[32];
+        tmem_ld32(trow + C::T_U + cb, ur);
+        tmem_ld32(trow + C::T_V + cb, vr);
+        if (role != R_O) tmem_ld32(trow + C::T_DZ + cb, zr);
+        tmem_ld_wait();
+        if (role == R_DGRAD) {
+          if (j > 0) mbar_wait(bar_b, (c - 1) & 1, sAbort);  // dP(c-1) done with dU/dV
+          unsigned char* sdu = sm + C::D_S;
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            uint32_t wu[4], wv[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float du[2], dv[2];
+#pragma unroll
+              for (int h2 = 0; h2 < 2; ++h2) {
+                const int i = jj * 8 + 2 * e + h2;
+                const float u = __uint_as_float(ur[i]), v = __uint_as_float(vr[i]), dz = __uint_as_float(zr[i]);
+                const float s = sigm_fast(u);
+                du[h2] = dz * v * s * (1.f + u * (1.f - s));
+                dv[h2] = dz * u * s;
+              }
+              wu[e] = pack2<BF16>(du[0], du[1]);
+              wv[e] = pack2<BF16>(dv[0], dv[1]);
+            }
+            const uint32_t off = sw128_off(r, cb + jj * 8, BM);
+            *reinterpret_cast<uint4*>(sdu + off) = make_uint4(wu[0], wu[1], wu[2], wu[3]);
+            *reinterpret_cast<uint4*>(sdu + C::Z_BYTES + off) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+          }
+        } else if (role == R_UV) {
+          unsigned char* sdu = sm + C::U_S;
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            uint32_t wu[4], wv[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float du[2], dv[2];
+#pragma unroll
+              for (int h2 = 0; h2 < 2; ++h2) {
+                const int i = jj * 8 + 2 * e + h2;
+                const float u = __uint_as_float(ur[i]), v = __uint_as_float(vr[i]), dz = __uint_as_float(zr[i]);
+                const float s = sigm_fast(u);
+                du[h2] = dz * v * s * (1.f + u * (1.f - s));
+                dv[h2] = dz * u * s;
+              }
+              wu[e] = pack2<BF16>(du[0], du[1]);
+              wv[e] = pack2<BF16>(dv[0], dv[1]);
+            }
+            const uint32_t off = sw128_off(r, j * 64 + cb + jj * 8, BM);
+            *reinterpret_cast<uint4*>(sdu + off) = make_uint4(wu[0], wu[1], wu[2], wu[3]);
+            *reinterpret_cast<uint4*>(sdu + 2 * C::Z_BYTES + off) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+          }
+        } else {  // R_O: Z = silu(U) * V
+          if (j > 0) mbar_wait(bar_b, (c - 1) & 1, sAbort);  // Y(c-1) done with Z
+          unsigned char* sz = sm + C::O_Z;
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            uint32_t wz[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int i0 = jj * 8 + 2 * e;
+              const uint32_t u2 = pack2<BF16>(__uint_as_float(ur[i0]), __uint_as_float(ur[i0 + 1]));
+              const uint32_t v2 = pack2<BF16>(__uint_as_float(vr[i0]), __uint_as_float(vr[i0 + 1]));
+              wz[e] = silu_mul2<BF16>(u2, v2);
+            }
+            *reinterpret_cast<uint4*>(sz + sw128_off(r, cb + jj * 8, BM)) = make_uint4(wz[0], wz[1], wz[2], wz[3]);
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(bar_du);
+        if (role == R_O) {
+          // Zo chunk = A_o Z into the pair buffer (atom j & 1).
+          if ((j & 1) == 0 && (it > 0 || j > 0)) mbar_wait(bar_w, (pc - 1) & 1, sAbort);
+          comp_sync();
+          __syncwarp();
+          const unsigned char* sz = sm + C::O_Z;
+          unsigned char* szo = sm + C::O_ZO;
+#pragma unroll
+          for (int np = 0; np < 4; ++np) {
+            const int rowr = warp * 16 + (lane & 15), colr = np * 16 + (lane >> 4) * 8;
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_trans(smem_u32(sz + sw128_off(rowr, colr, BM)), b0, b1, b2, b3);
+            float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+            mma16816<BF16>(c0, fAo, b0, b1);
+            mma16816<BF16>(c1, fAo, b2, b3);
+            const int r0 = warp * 16 + g, k0 = (j & 1) * 64 + np * 16 + 2 * t4;
+            *reinterpret_cast<uint32_t*>(szo + sw128_off(r0, k0, BM)) = pack2<BF16>(c0[0], c0[1]);
+            *reinterpret_cast<uint32_t*>(szo + sw128_off(r0 + 8, k0, BM)) = pack2<BF16>(c0[2], c0[3]);
+            *reinterpret_cast<uint32_t*>(szo + sw128_off(r0, k0 + 8, BM)) = pack2<BF16>(c1[0], c1[1]);
+            *reinterpret_cast<uint32_t*>(szo + sw128_off(r0 + 8, k0 + 8, BM)) = pack2<BF16>(c1[2], c1[3]);
+          }
+          if (j & 1) {
+            fence_proxy_async_smem();
+            mbar_arrive(bar_zo);
+            ++pc;
+          }
+          comp_sync();  // every warp is done reading Z before it is rewritten
+        }
+      }
+
+      // ---- per-item epilogue
+      if (role == R_DGRAD) {
+        mbar_wait(bar_b, (c - 1) & 1, sAbort);
+        __syncwarp();
+        tc_fence_after();
+        unsigned char* stA = sm;                  // dP_u half
+        unsigned char* stB = sm + STG_BYTES;      // dP_v half
+        unsigned char* stC = sm + 2 * STG_BYTES;  // T half
+        const uint32_t aA = smem_u32(stA), aB = smem_u32(stB), aC = smem_u32(stC);
+        for (int hf = 0; hf < D / 64; ++hf) {
+          uint32_t pr[32], qr[32];
+          tmem_ld32(trow + C::T_DPU + hf * 64 + cb, pr);
+          tmem_ld32(trow + C::T_DPV + hf * 64 + cb, qr);
+          tmem_ld_wait();
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            uint4 w1, w2;
+            w1.x = pack2<BF16>(__uint_as_float(pr[jj * 8 + 0]), __uint_as_float(pr[jj * 8 + 1]));
+            w1.y = pack2<BF16>(__uint_as_float(pr[jj * 8 + 2]), __uint_as_float(pr[jj * 8 + 3]));
+            w1.z = pack2<BF16>(__uint_as_float(pr[jj * 8 + 4]), __uint_as_float(pr[jj * 8 + 5]));
+            w1.w = pack2<BF16>(__uint_as_float(pr[jj * 8 + 6]), __uint_as_float(pr[jj * 8 + 7]));
+            w2.x = pack2<BF16>(__uint_as_float(qr[jj * 8 + 0]), __uint_as_float(qr[jj * 8 + 1]));
+            w2.y = pack2<BF16>(__uint_as_float(qr[jj * 8 + 2]), __uint_as_float(qr[jj * 8 + 3]));
+            w2.z = pack2<BF16>(__uint_as_float(qr[jj * 8 + 4]), __uint_as_float(qr[jj * 8 + 5]));
+            w2.w = pack2<BF16>(__uint_as_float(qr[jj * 8 + 6]), __uint_as_float(qr[jj * 8 + 7]));
+            *reinterpret_cast<uint4*>(stA + (r * STG_LD + cb + jj * 8) * 2) = w1;
+            *reinterpret_cast<uint4*>(stB + (r * STG_LD + cb + jj * 8) * 2) = w2;
+          }
+          gather_half<TX, BF16>(gc, x, hf, a.rstd, a.nw, a.x_dt, nullptr, nullptr, stC, false, tid);
+          comp_sync();
+          __syncwarp();
+          // dA_u += dP_u T^T, dA_v += dP_v T^T (tile ``warp``)
+          auto rowA = [&](int rr, int k) { return aA + ((warp * 16 + rr) * STG_LD + k) * 2; };
+          auto rowB = [&](int rr, int k) { return aB + ((warp * 16 + rr) * STG_LD + k) * 2; };
+          auto rowC = [&](int rr, int k) { return aC + ((warp * 16 + rr) * STG_LD + k) * 2; };
+          gram16<BF16>(accA[0], rowA, rowC, lane);
+          gram16<BF16>(accA[1], rowB, rowC, lane);
+          // dT = A_u^T dP_u + A_v^T dP_v, scattered to dX / dxn
+          const int row0 = warp * 16 + g;
+          const int tokA = sTok[row0], tokB = sTok[row0 + 8];
+          const int bA = sRowB[row0], bB = sRowB[row0 + 8];
+#pragma unroll
+          for (int np = 0; np < 4; ++np) {
+            __syncwarp();
+            uint32_t b0, b1, b2, b3, e0, e1, e2, e3;
+            ldsm_x4_trans(aA + ((warp * 16 + (lane & 15)) * STG_LD + np * 16 + (lane >> 4) * 8) * 2, b0, b1, b2, b3);
+            ldsm_x4_trans(aB + ((warp * 16 + (lane & 15)) * STG_LD + np * 16 + (lane >> 4) * 8) * 2, e0, e1, e2, e3);
+            float cc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+            mma16816<BF16>(cc[0], fAuT, b0, b1);
+            mma16816<BF16>(cc[1], fAuT, b2, b3);
+            mma16816<BF16>(cc[0], fAvT, e0, e1);
+            mma16816<BF16>(cc[1], fAvT, e2, e3);
+#pragma unroll
+            for (int nb = 0; nb < 2; ++nb) {
+              const int k = hf * 64 + np * 16 + nb * 8 + 2 * t4;
+#pragma unroll
+              for (int hr = 0; hr < 2; ++hr) {
+                const int tok = hr ? tokB : tokA;
+                if (tok < 0) continue;
+                const int64_t row = (int64_t)(hr ? bB : bA) * p.N + tok;
+                const float d0 = cc[nb][2 * hr], d1 = cc[nb][2 * hr + 1];
+                if (gc.cont) {
+                  const int64_t off = row * p.C + sCh[0] + k;
+                  if (a.dxn) {
+                    *reinterpret_cast<float2*>(a.dxn + off) = make_float2(d0, d1);
+                  } else if constexpr (std::is_same_v<TX, float>) {
+                    *reinterpret_cast<float2*>((float*)a.dx + off) = make_float2(d0, d1);
+                  } else {
+                    *reinterpret_cast<uint32_t*>((TX*)a.dx + off) = pack2<std::is_same_v<TX, __nv_bfloat16>>(d0, d1);
+                  }
+                } else {
+#pragma unroll
+                  for (int e = 0; e < 2; ++e) {
+                    const int ch = sCh[k + e];
+                    if (ch >= p.C) continue;
+                    const int64_t off = row * p.C + ch;
+                    const float dv = e ? d1 : d0;
+                    if (a.dxn) a.dxn[off] = dv;
+                    else ((TX*)a.dx)[off] = Elem<TX>::from(dv);
+                  }
+                }
+              }
+            }
+          }
+          comp_sync();
+        }
+        tc_fence_before();
+      } else if (role == R_O) {
+        mbar_wait(bar_b, (c - 1) & 1, sAbort);   // Y complete
+        mbar_wait(bar_w, (pc - 1) & 1, sAbort);  // M_o done with the pair buffer
+        __syncwarp();
+        tc_fence_after();
+        unsigned char* stY = sm + C::O_Z;
+        const uint32_t aY = smem_u32(stY), aG = smem_u32(sX1);
+        for (int hf = 0; hf < D / 64; ++hf) {
+          uint32_t yr[32];
+          tmem_ld32(trow + C::T_Y + hf * 64 + cb, yr);
+          tmem_ld_wait();
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            uint4 w;
+            const int k = hf * 64 + cb + jj * 8;
+            w.x = pack2<BF16>(__uint_as_float(yr[jj * 8 + 0]) * ggq[k + 0], __uint_as_float(yr[jj * 8 + 1]) * ggq[k + 1]);
+            w.y = pack2<BF16>(__uint_as_float(yr[jj * 8 + 2]) * ggq[k + 2], __uint_as_float(yr[jj * 8 + 3]) * ggq[k + 3]);
+            w.z = pack2<BF16>(__uint_as_float(yr[jj * 8 + 4]) * ggq[k + 4], __uint_as_float(yr[jj * 8 + 5]) * ggq[k + 5]);
+            w.w = pack2<BF16>(__uint_as_float(yr[jj * 8 + 6]) * ggq[k + 6], __uint_as_float(yr[jj * 8 + 7]) * ggq[k + 7]);
+            *reinterpret_cast<uint4*>(stY + (r * STG_LD + cb + jj * 8) * 2) = w;
+          }
+          comp_sync();
+          __syncwarp();
+          auto rowG = [&](int rr, int k) { return aG + sw128_off(warp * 16 + rr, hf * 64 + k, BM); };
+          auto rowY = [&](int rr, int k) { return aY + ((warp * 16 + rr) * STG_LD + k) * 2; };
+          gram16<BF16>(accA[0], rowG, rowY, lane);
+          comp_sync();
+        }
+        tc_fence_before();
+      }
+    }
+
+    // ---- end of the CTA's items: write partials
+    if (role == R_DGRAD) {
+      float* dst = a.pdA + ((int64_t)blockIdx.x * NCOMP_WARPS + warp) * 512;
+#pragma unroll
+      for (int m = 0; m < 2; ++m)
+#pragma unroll
+        for (int nb = 0; nb < 2; ++nb) {
+          const int col = nb * 8 + 2 * t4;
+          dst[m * 256 + g * 16 + col] = accA[m][nb][0];
+          dst[m * 256 + g * 16 + col + 1] = accA[m][nb][1];
+          dst[m * 256 + (g + 8) * 16 + col] = accA[m][nb][2];
+          dst[m * 256 + (g + 8) * 16 + col + 1] = accA[m][nb][3];
+        }
+    } else if (n_items > 0) {
+      if (role == R_UV) mbar_wait(bar_w, ((int)n_items - 1) & 1, sAbort);
+      __syncwarp();
+      tc_fence_after();
+      if (role == R_UV) {
+        float* dst = a.puv + (int64_t)wslot * 2 * 128 * D;
+        for (int m = 0; m < 2; ++m)
+          for (int c0 = 0; c0 < D; c0 += 64) {
+            uint32_t vr[32];
+            tmem_ld32(trow + (m ? C::T_ACCV : C::T_ACCU) + c0 + cb, vr);
+            tmem_ld_wait();
+            float* o = dst + ((int64_t)m * 128 + r) * D + c0 + cb;
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              *reinterpret_cast<float4*>(o + i) = make_float4(__uint_as_float(vr[i]), __uint_as_float(vr[i + 1]),
+                                                              __uint_as_float(vr[i + 2]), __uint_as_float(vr[i + 3]));
+          }
+      } else {
+        float* dst = a.po + (int64_t)wslot * C::RD * D;
+        for (int hb = 0; hb < C::NH; ++hb)
+          for (int c0 = 0; c0 < D; c0 += 64) {
+            uint32_t vr[32];
+            tmem_ld32(trow + C::T_ACCO + hb * D + c0 + cb, vr);
+            tmem_ld_wait();
+            float* o = dst + ((int64_t)hb * 128 + r) * D + c0 + cb;
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              *reinterpret_cast<float4*>(o + i) = make_float4(__uint_as_float(vr[i]), __uint_as_float(vr[i + 1]),
+                                                              __uint_as_float(vr[i + 2]), __uint_as_float(vr[i + 3]));
+          }
+        float* da = a.pdAo + ((int64_t)wslot * NCOMP_WARPS + warp) * 256;
+#pragma unroll
+        for (int nb = 0; nb < 2; ++nb) {
+          const int col = nb * 8 + 2 * t4;
+          da[g * 16 + col] = accA[0][nb][0];
+          da[g * 16 + col + 1] = accA[0][nb][1];
+          da[(g + 8) * 16 + col] = accA[0][nb][2];
+          da[(g + 8) * 16 + col + 1] = accA[0][nb][3];
+        }
+      }
+      tc_fence_before();
+    } else if (role == R_O) {
+      // No items: zero partials so the reduction stays well defined.
+      float* da = a.pdAo + ((int64_t)wslot * NCOMP_WARPS + warp) * 256;
+      for (int i = lane; i < 256; i += 32) da[i] = 0.f;
+      float* dst = a.po + (int64_t)wslot * C::RD * D;
+      for (int i = tid; i < C::RD * D; i += NCOMP) dst[i] = 0.f;
+    } else {
+      float* dst = a.puv + (int64_t)wslot * 2 * 128 * D;
+      for (int i = tid; i < 2 * 128 * D; i += NCOMP) dst[i] = 0.f;
+    }
+  }
+
+  __syncwarp();
+  __syncthreads();
+  if (*sAbort) {
+    for (int i = 0; i < 1000; ++i) __nanosleep(1000);
+  }
+  if (warp == MMA_WARP) {
+    tc_fence_after();
+    tmem_dealloc(tbase, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Reduction of the per-CTA partials into the gradient outputs (fixed order).
+// ---------------------------------------------------------------------------
+template <int D, typename TW>
+__global__ void tc_bwd_reduce_kernel(Prob p, BwdArgs a, const TW* __restrict__ bo, TW* __restrict__ da_u,
+                                     TW* __restrict__ da_v, TW* __restrict__ da_o, TW* __restrict__ db_u,
+                                     TW* __restrict__ db_v, TW* __restrict__ db_o, TW* __restrict__ dgamma) {
+  using C = BCfg<D>;
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t nB = (int64_t)p.Qc * D * C::RD;
+  // dB_u, dB_v : [qc][c][e]; partial layout [h][qc][j][m][e%128][c]
+  for (int64_t i = tid; i < 2 * nB; i += stride) {
+    const int m = (int)(i / nB);
+    const int64_t rem = i - m * nB;
+    const int qc = (int)(rem / (D * C::RD));
+    const int c = (int)((rem / C::RD) % D), e = (int)(rem % C::RD);
+    const int hh = e / 128, el = e % 128;
+    float s = 0.f;
+    for (int j = 0; j < a.nUVq; ++j)
+      s += a.puv[((((int64_t)(hh * p.Qc + qc) * a.nUVq + j) * 2 + m) * 128 + el) * D + c];
+    (m ? db_v : db_u)[rem] = Elem<TW>::from(s);
+  }
+  // dB_o = gamma * M_o : [qc][e][c]
+  for (int64_t i = tid; i < nB; i += stride) {
+    const int qc = (int)(i / (C::RD * D));
+    const int64_t rem = i - (int64_t)qc * C::RD * D;
+    float s = 0.f;
+    for (int j = 0; j < a.nOq; ++j) s += a.po[((int64_t)qc * a.nOq + j) * C::RD * D + rem];
+    const int cidx = (int)(rem % D);
+    db_o[i] = Elem<TW>::from(s * a.gg[(int64_t)qc * D + cidx]);
+  }
+  // dgamma[ch[qc][c]] = sum_e B_o[qc][e][c] * M_o[qc][e][c]
+  for (int64_t i = tid; i < (int64_t)p.Qc * D; i += stride) {
+    const int qc = (int)(i / D), cidx = (int)(i % D);
+    const int ch = p.ch[i];
+    if (ch >= p.C) continue;
+    float s = 0.f;
+    for (int e = 0; e < C::RD; ++e) {
+      float m = 0.f;
+      for (int j = 0; j < a.nOq; ++j) m += a.po[(((int64_t)qc * a.nOq + j) * C::RD + e) * D + cidx];
+      s += load_as<float>(bo, ((int64_t)qc * C::RD + e) * D + cidx) * m;
+    }
+    dgamma[ch] = Elem<TW>::from(s);
+  }
+  // token-mix gradients
+  for (int64_t i = tid; i < 3 * 256; i += stride) {
+    const int m = (int)(i / 256), e = (int)(i % 256);
+    float s = 0.f;
+    if (m < 2) {
+      for (int b = 0; b < a.nD; ++b)
+        for (int w = 0; w < NCOMP_WARPS; ++w) s += a.pdA[((int64_t)b * NCOMP_WARPS + w) * 512 + m * 256 + e];
+    } else {
+      const int64_t n = (int64_t)p.Qc * a.nOq * NCOMP_WARPS;
+      for (int64_t b = 0; b < n; ++b) s += a.pdAo[b * 256 + e];
+    }
+    (m == 0 ? da_u : (m == 1 ? da_v : da_o))[e] = Elem<TW>::from(s);
+  }
+}
+
+int num_sms_b() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!cached[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+template <int D, bool BF16>
+int tc_backward_t(const ow_bigemm_args_t* ar, const ow_bigemm_grads_t* gr, const Prob& p, cudaStream_t st,
+                  Carver& ws) {
+  const bool block = ar->rstd != nullptr;
+  BPlan<D> pl(p, block, num_sms_b());
+  unsigned char* base = (unsigned char*)ws.take(pl.total);
+  NormBwd nbw{};
+  if (block) nbw = norm_bwd_take((int64_t)p.B * p.N, p.C, ws);
+  if (!ws.base) return OW_OK;
+  BwdArgs a{};
+  a.p = p;
+  a.x = ar->x;
+  a.dout = gr->dout;
+  a.rstd = (const float*)ar->rstd;
+  a.scale = ar->sample_scale;
+  a.x_dt = ar->x_dtype;
+  a.img = base + pl.img;
+  a.amat = (const uint16_t*)(base + pl.amat);
+  a.gg = (const float*)(base + pl.gg);
+  a.nw = (const float*)(base + pl.nw);
+  a.contig = (const int*)(base + pl.contig);
+  a.vec_ok = ((uintptr_t)ar->x % 16 == 0) && ((uintptr_t)gr->dout % 16 == 0) && ((uintptr_t)gr->dx % 16 == 0) &&
+             (p.C % 8 == 0);
+  a.dx = block ? nullptr : gr->dx;
+  a.dxn = block ? (float*)(base + pl.dxn) : nullptr;
+  a.pdA = (float*)(base + pl.pdA);
+  a.pdAo = (float*)(base + pl.pdAo);
+  a.puv = (float*)(base + pl.puv);
+  a.po = (float*)(base + pl.po);
+  a.nD = pl.nD;
+  a.nUVq = pl.nUVq;
+  a.nOq = pl.nOq;
+  a.nH = pl.nH;
+
+  // Weight images.
+  {
+    const int64_t n = 6LL * p.Qc * D * 2 * D;
+    const int grid = (int)std::min<int64_t>((n + 255) / 256, 148 * 8);
+    auto run = [&](auto* tw) {
+      using TW = std::remove_pointer_t<decltype(tw)>;
+      launch(tc_bwd_prep_kernel<D, TW, BF16>, grid, 256, 0, st, p, (const TW*)ar->a_u, (const TW*)ar->a_v,
+             (const TW*)ar->a_o, (const TW*)ar->b_u, (const TW*)ar->b_v, (const TW*)ar->b_o,
+             (const TW*)ar->gamma, (const TW*)(block ? ar->norm_w : nullptr), base + pl.img,
+             (uint16_t*)(base + pl.amat), (float*)(base + pl.gg), (float*)(base + pl.nw),
+             (int*)(base + pl.contig));
+    };
+    switch (ar->w_dtype) {
+      case OW_DTYPE_F32: run((float*)nullptr); break;
+      case OW_DTYPE_F64: run((double*)nullptr); break;
+      case OW_DTYPE_BF16: run((__nv_bfloat16*)nullptr); break;
+      case OW_DTYPE_F16: run((__half*)nullptr); break;
+      default: set_error("unsupported weight dtype"); return OW_ERR_UNSUPPORTED;
+    }
+    OW_CHECK_LAUNCH("tc_bwd_prep_kernel");
+  }
+
+  auto go = [&](auto* tx, auto* to) -> int {
+    using TX = std::remove_pointer_t<decltype(tx)>;
+    using TO = std::remove_pointer_t<decltype(to)>;
+    auto kern = tc_bwd_kernel<D, BF16, TX, TO>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, BCfg<D>::SMEM);
+    if (e != cudaSuccess) {
+      set_error("tc backward: cannot reserve %d bytes of shared memory: %s", BCfg<D>::SMEM, cudaGetErrorString(e));
+      return OW_ERR_CUDA;
+    }
+    launch(kern, pl.grid, TC_THREADS, BCfg<D>::SMEM, st, a);
+    OW_CHECK_LAUNCH("tc_bwd_kernel");
+    return OW_OK;
+  };
+  using T16 = std::conditional_t<BF16, __nv_bfloat16, __half>;
+  const int xd = ar->x_dtype, od = ar->out_dtype;
+  const int c16 = BF16 ? OW_DTYPE_BF16 : OW_DTYPE_F16;
+  int rc;
+  if (xd == c16 && od == c16) rc = go((T16*)nullptr, (T16*)nullptr);
+  else if (xd == c16 && od == OW_DTYPE_F32) rc = go((T16*)nullptr, (float*)nullptr);
+  else if (xd == OW_DTYPE_F32 && od == OW_DTYPE_F32) rc = go((float*)nullptr, (float*)nullptr);
+  else if (xd == OW_DTYPE_F32 && od == c16) rc = go((float*)nullptr, (T16*)nullptr);
+  else {
+    set_error("tc backward: unsupported dtypes x=%s out=%s", dtype_name(xd), dtype_name(od));
+    return OW_ERR_UNSUPPORTED;
+  }
+  OW_RETURN_IF(rc);
+
+  auto red = [&](auto* tw) {
+    using TW = std::remove_pointer_t<decltype(tw)>;
+    launch(tc_bwd_reduce_kernel<D, TW>, 148 * 4, 256, 0, st, p, a, (const TW*)ar->b_o, (TW*)gr->da_u,
+           (TW*)gr->da_v, (TW*)gr->da_o, (TW*)gr->db_u, (TW*)gr->db_v, (TW*)gr->db_o, (TW*)gr->dgamma);
+  };
+  switch (ar->w_dtype) {
+    case OW_DTYPE_F32: red((float*)nullptr); break;
+    case OW_DTYPE_F64: red((double*)nullptr); break;
+    case OW_DTYPE_BF16: red((__nv_bfloat16*)nullptr); break;
+    case OW_DTYPE_F16: red((__half*)nullptr); break;
+  }
+  OW_CHECK_LAUNCH("tc_bwd_reduce_kernel");
+  if (block)
+    return norm_bwd_run(nbw, ar->x, ar->x_dtype, gr->dout, ar->out_dtype, (const float*)ar->rstd,
+                        (const float*)(base + pl.nw), a.dxn, (int64_t)p.B * p.N, p.C, gr->dx, gr->dnorm_w,
+                        ar->w_dtype, st);
+  return OW_OK;
+}
+
+}  // namespace
+
+int tc_backward(const ow_bigemm_args_t* a, const ow_bigemm_grads_t* gr, const Prob& p, void* stream,
+                Carver& ws) {
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool bf = a->compute_dtype == OW_DTYPE_BF16;
+  if (p.d == 64) return bf ? tc_backward_t<64, true>(a, gr, p, st, ws) : tc_backward_t<64, false>(a, gr, p, st, ws);
+  return bf ? tc_backward_t<128, true>(a, gr, p, st, ws) : tc_backward_t<128, false>(a, gr, p, st, ws);
+}
+
+}  // namespace ow
