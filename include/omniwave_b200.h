@@ -174,6 +174,25 @@ OW_API int ow_rmsnorm_rstd(const void* x, int32_t x_dtype, int32_t compute_dtype
 OW_API int ow_bigemm_fwd(const ow_bigemm_args_t* args, void* stream);
 
 /*
+ * Allocation-free variant of ow_bigemm_fwd, for callers that cannot allocate
+ * device memory when they run the operator (plugin hosts that pass only input
+ * and output buffers, code that must not enter the process's allocator).  It
+ * has no counterpart in the reference.  Same arguments as ow_bigemm_fwd except
+ * that ``workspace``/``workspace_bytes`` are ignored: scratch comes from a
+ * fixed array of ow_noalloc_scratch_limit() bytes (4 MiB) in the library's
+ * device memory, which every GPU that loads the library holds until exit.
+ * Shapes needing more scratch are rejected with OW_ERR_WORKSPACE.  The first
+ * call on a device (with that device current) looks up the array's device
+ * address; make it before any stream capture.  All calls share the array, so
+ * calls that overlap on the GPU race; no scratch contents need to start at
+ * zero.  Allocates nothing (no cudaMalloc/cudaFree).
+ */
+OW_API int ow_bigemm_fwd_noalloc(const ow_bigemm_args_t* args, void* stream);
+
+/* Scratch bytes available to ow_bigemm_fwd_noalloc (no reference counterpart). */
+OW_API size_t ow_noalloc_scratch_limit(void);
+
+/*
  * Backward of ow_bigemm_fwd with the same ``args`` (``out`` is ignored).
  * Replaces the autograd backward the reference takes through
  * ``bigemm_delta_reference`` (and, in block mode, through RMSNorm and the

@@ -66,7 +66,8 @@ class Grads(ctypes.Structure):
 EXPORTS = (
     "ow_abi_version", "ow_last_error", "ow_device_supported", "ow_device_fault",
     "ow_launch_count", "ow_bigemm_workspace_size",
-    "ow_rmsnorm_rstd", "ow_bigemm_fwd", "ow_bigemm_bwd",
+    "ow_rmsnorm_rstd", "ow_bigemm_fwd", "ow_bigemm_bwd", "ow_bigemm_fwd_noalloc",
+    "ow_noalloc_scratch_limit",
 )
 
 _lock = threading.Lock()
@@ -104,6 +105,9 @@ def load() -> ctypes.CDLL:
         lib.ow_rmsnorm_rstd.restype = ctypes.c_int
         lib.ow_bigemm_fwd.argtypes = [ctypes.POINTER(Args), _vp]
         lib.ow_bigemm_fwd.restype = ctypes.c_int
+        lib.ow_bigemm_fwd_noalloc.argtypes = [ctypes.POINTER(Args), _vp]
+        lib.ow_bigemm_fwd_noalloc.restype = ctypes.c_int
+        lib.ow_noalloc_scratch_limit.restype = ctypes.c_size_t
         lib.ow_bigemm_bwd.argtypes = [ctypes.POINTER(Args), ctypes.POINTER(Grads), _vp]
         lib.ow_bigemm_bwd.restype = ctypes.c_int
         v = lib.ow_abi_version()

@@ -84,6 +84,12 @@ static size_t measure(const ow_bigemm_args_t* a, const Prob& p, bool bwd) {
   return c.used + 256;
 }
 
+// Entry points of other translation units reuse the same validation,
+// dispatch and workspace sizing.
+int api_make_prob(const ow_bigemm_args_t* a, Prob* p) { return make_prob(a, p, true); }
+bool api_use_tc(const ow_bigemm_args_t* a, const Prob& p) { return use_tc(a, p); }
+size_t api_measure(const ow_bigemm_args_t* a, const Prob& p, bool bwd) { return measure(a, p, bwd); }
+
 }  // namespace ow
 
 using namespace ow;

@@ -39,6 +39,11 @@ struct Carver {
   }
 };
 
+// Validation / dispatch / workspace sizing shared by every entry point.
+int api_make_prob(const ow_bigemm_args_t* a, Prob* p);
+bool api_use_tc(const ow_bigemm_args_t* a, const Prob& p);
+size_t api_measure(const ow_bigemm_args_t* a, const Prob& p, bool bwd);
+
 // CUDA-core path (exact fp32 / fp64; also any shape the tensor path lacks).
 int simt_forward(const ow_bigemm_args_t* a, const Prob& p, void* stream, Carver& ws);
 int simt_backward(const ow_bigemm_args_t* a, const ow_bigemm_grads_t* gr, const Prob& p,
