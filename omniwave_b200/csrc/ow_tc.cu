@@ -59,8 +59,9 @@ struct Cfg {
   static constexpr int OFF_WUV = OFF_Z + 2 * Z_BYTES;
   static constexpr int OFF_WO = OFF_WUV + 2 * WUV_BYTES;
   static constexpr int OFF_STG = OFF_WO + 2 * WO_BYTES;
-  static constexpr int OFF_META = OFF_STG + STG_BYTES;     // tok[128], rowb[128], ch[D]
-  static constexpr int META_BYTES = (2 * BM + D) * 4;
+  static constexpr int OFF_META = OFF_STG + STG_BYTES;     // 2 x {tok[128], rowb[128], ch[D], gg[D], nw[D], cont}
+  static constexpr int META1 = 2 * BM + 3 * D + 4;         // 32-bit words per buffer
+  static constexpr int META_BYTES = 2 * META1 * 4;
   static constexpr int OFF_BAR = OFF_META + META_BYTES;
   static constexpr int BAR_BYTES = 16 * 8 + 16;
   static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024;  // + alignment slack
@@ -82,7 +83,7 @@ struct TcWs {
     img = take((size_t)p.Qc * Cfg<D>::NQ * Cfg<D>::IMG_BYTES);
     amat = take(3 * 256 * 2);
     gg = take((size_t)p.Qc * D * 4);
-    nw = take((size_t)p.C * 4);
+    nw = take((size_t)p.Qc * D * 4);
     contig = take((size_t)p.Qc * 4);
     total = o;
   }
@@ -139,7 +140,10 @@ __global__ void tc_prep_kernel(Prob p, const TW* __restrict__ au, const TW* __re
     gg[i] = c < p.C ? load_as<float>(gamma, c) : 0.f;
   }
   if (nw_in)
-    for (int64_t i = tid; i < p.C; i += stride) nw[i] = load_as<float>(nw_in, i);
+    for (int64_t i = tid; i < (int64_t)p.Qc * D; i += stride) {
+      int c = p.ch[i];
+      nw[i] = c < p.C ? load_as<float>(nw_in, c) : 0.f;
+    }
   for (int64_t qc = tid; qc < p.Qc; qc += stride) {
     int c0 = p.ch[qc * D];
     int ok = (c0 % 8 == 0) && (c0 + D <= p.C) && (p.C % 8 == 0);
@@ -316,77 +320,159 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const float* __restrict__ rstd, 
       fa[m][3] = *reinterpret_cast<const uint32_t*>(A + (g + 8) * 16 + 2 * t4 + 8);
     }
     const uint32_t aStg = smem_u32(sStg);
-    int c = 0;
-    for (int it = 0; it < my_items; ++it) {
+    int32_t* meta = reinterpret_cast<int32_t*>(sTok);
+    auto mTok = [&](int buf) { return meta + buf * C::META1; };
+    auto mRowB = [&](int buf) { return meta + buf * C::META1 + BM; };
+    auto mCh = [&](int buf) { return meta + buf * C::META1 + 2 * BM; };
+    auto mGG = [&](int buf) { return reinterpret_cast<float*>(meta + buf * C::META1 + 2 * BM + D); };
+    auto mNW = [&](int buf) { return reinterpret_cast<float*>(meta + buf * C::META1 + 2 * BM + 2 * D); };
+    auto mCont = [&](int buf) { return meta + buf * C::META1 + 2 * BM + 3 * D; };
+
+    // Metadata of one item, held in registers between issue and store.
+    struct MetaReg { int tok, b, ch, cont; float gg, nw; };
+    auto meta_issue = [&](int it) {
+      MetaReg m{-1, 0, 0, 0, 0.f, 0.f};
       const int64_t item = blockIdx.x + (int64_t)it * gridDim.x;
       const int qc = (int)(item / nMB), mb = (int)(item - (int64_t)qc * nMB);
-      const bool cont = vec_ok && contig[qc] != 0;
-      comp_sync();  // previous item's epilogue is done with the metadata
-      for (int r = tid; r < BM; r += NCOMP) {
-        int64_t t = (int64_t)mb * 8 + (r >> 4);
+      if (tid < BM) {
+        const int64_t t = (int64_t)mb * 8 + (tid >> 4);
         int tok = p.N, b = 0;
         if (t < BQ) {
           b = (int)(t / p.Qs);
-          tok = p.tok[(t - (int64_t)b * p.Qs) * 16 + (r & 15)];
+          tok = p.tok[(t - (int64_t)b * p.Qs) * 16 + (tid & 15)];
         }
-        sTok[r] = tok < p.N ? tok : -1;
-        sRowB[r] = b;
+        m.tok = tok < p.N ? tok : -1;
+        m.b = b;
       }
-      for (int k = tid; k < D; k += NCOMP) sCh[k] = p.ch[qc * D + k];
+      if (tid < D) {
+        m.ch = p.ch[qc * D + tid];
+        m.gg = gg[(int64_t)qc * D + tid];
+        m.nw = rstd ? nw[(int64_t)qc * D + tid] : 0.f;
+      }
+      if (tid == 0) m.cont = vec_ok && contig[qc] != 0;
+      return m;
+    };
+    auto meta_store = [&](const MetaReg& m, int buf) {
+      if (tid < BM) { mTok(buf)[tid] = m.tok; mRowB(buf)[tid] = m.b; }
+      if (tid < D) { mCh(buf)[tid] = m.ch; mGG(buf)[tid] = m.gg; mNW(buf)[tid] = m.nw; }
+      if (tid == 0) *mCont(buf) = m.cont;
+    };
+
+    // Gathered rows of one 64-channel half, held in registers (contiguous path).
+    constexpr int VW = sizeof(TX) == 2 ? 1 : 2;  // 16-byte vectors per 8 elements
+    struct RowReg { uint4 v[4][VW]; float rs[4]; };
+    auto rows_issue = [&](RowReg& R, int buf, int hf) {
+      const int* tk = mTok(buf);
+      const int* rb = mRowB(buf);
+      const int ch0 = mCh(buf)[0];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int unit = tid + u * NCOMP;
+        const int r = unit >> 3, cj = unit & 7;
+        const int tok = tk[r];
+        R.rs[u] = 1.f;
+        if (tok >= 0) {
+          const int64_t row = (int64_t)rb[r] * p.N + tok;
+          const uint4* src = reinterpret_cast<const uint4*>(x + row * p.C + ch0 + hf * 64 + cj * 8);
+#pragma unroll
+          for (int vv = 0; vv < VW; ++vv) R.v[u][vv] = __ldg(src + vv);
+          if (rstd) R.rs[u] = rstd[row];
+        } else {
+#pragma unroll
+          for (int vv = 0; vv < VW; ++vv) R.v[u][vv] = make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+    };
+    auto rows_store = [&](const RowReg& R, int buf, int hf) {
+      const float* nwq = mNW(buf);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int unit = tid + u * NCOMP;
+        const int r = unit >> 3, cj = unit & 7;
+        float v[8];
+        if constexpr (sizeof(TX) == 2) {
+          const uint32_t w[4] = {R.v[u][0].x, R.v[u][0].y, R.v[u][0].z, R.v[u][0].w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            float2 f = unpack2<std::is_same_v<TX, __nv_bfloat16>>(w[i]);
+            v[2 * i] = f.x;
+            v[2 * i + 1] = f.y;
+          }
+        } else {
+#pragma unroll
+          for (int vv = 0; vv < 2; ++vv) {
+            v[4 * vv + 0] = __uint_as_float(R.v[u][vv].x);
+            v[4 * vv + 1] = __uint_as_float(R.v[u][vv].y);
+            v[4 * vv + 2] = __uint_as_float(R.v[u][vv].z);
+            v[4 * vv + 3] = __uint_as_float(R.v[u][vv].w);
+          }
+        }
+        if (rstd) {
+          const int k0 = hf * 64 + cj * 8;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            float t = round_through(v[e] * R.rs[u], x_dt);
+            v[e] = round_through(t * nwq[k0 + e], x_dt);
+          }
+        }
+        uint4 w;
+        w.x = pack2<BF16>(v[0], v[1]);
+        w.y = pack2<BF16>(v[2], v[3]);
+        w.z = pack2<BF16>(v[4], v[5]);
+        w.w = pack2<BF16>(v[6], v[7]);
+        *reinterpret_cast<uint4*>(sStg + (r * STG_LD + cj * 8) * 2) = w;
+      }
+    };
+    // Element-wise gather (channels not one aligned run): synchronous.
+    auto rows_elem = [&](int buf, int hf) {
+      const int* tk = mTok(buf);
+      const int* rb = mRowB(buf);
+      const int* chs = mCh(buf);
+      const float* nwq = mNW(buf);
+      for (int e = tid; e < BM * 64; e += NCOMP) {
+        const int r = e >> 6, k = e & 63;
+        const int tok = tk[r], ch = chs[hf * 64 + k];
+        float v = 0.f;
+        if (tok >= 0 && ch < p.C) {
+          const int64_t row = (int64_t)rb[r] * p.N + tok;
+          v = load_as<float>(x, row * p.C + ch);
+          if (rstd) {
+            v = round_through(v * rstd[row], x_dt);
+            v = round_through(v * nwq[hf * 64 + k], x_dt);
+          }
+        }
+        uint32_t pk = pack2<BF16>(v, 0.f);
+        *reinterpret_cast<uint16_t*>(sStg + (r * STG_LD + k) * 2) = (uint16_t)(pk & 0xFFFF);
+      }
+    };
+
+    RowReg R;
+    MetaReg mnext{};
+    if (my_items > 0) {
+      meta_store(meta_issue(0), 0);
       comp_sync();
-      const int ch0 = sCh[0];
+      if (*mCont(0)) rows_issue(R, 0, 0);
+      if (my_items > 1) mnext = meta_issue(1);
+    }
+    int c = 0;
+    for (int it = 0; it < my_items; ++it) {
+      const int buf = it & 1;
+      const bool cont = *mCont(buf) != 0;
+      const int* sTk = mTok(buf);
+      const int* sRb = mRowB(buf);
+      const int* sChs = mCh(buf);
+      const float* sG = mGG(buf);
+      const int ch0 = sChs[0];
 
       // -------- gather + token mix, 64 channels at a time
       for (int hf = 0; hf < D / 64; ++hf) {
         if (cont) {
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int unit = tid + u * NCOMP;
-            const int r = unit >> 3, cj = unit & 7;
-            float v[8];
-            const int tok = sTok[r];
-            if (tok >= 0) {
-              const int64_t row = (int64_t)sRowB[r] * p.N + tok;
-              const int ch = ch0 + hf * 64 + cj * 8;
-              load8<TX>(x + row * p.C + ch, v);
-              if (rstd) {
-                const float rs = rstd[row];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                  float t = round_through(v[e] * rs, x_dt);
-                  v[e] = round_through(t * nw[ch + e], x_dt);
-                }
-              }
-            } else {
-#pragma unroll
-              for (int e = 0; e < 8; ++e) v[e] = 0.f;
-            }
-            uint4 w;
-            w.x = pack2<BF16>(v[0], v[1]);
-            w.y = pack2<BF16>(v[2], v[3]);
-            w.z = pack2<BF16>(v[4], v[5]);
-            w.w = pack2<BF16>(v[6], v[7]);
-            *reinterpret_cast<uint4*>(sStg + (r * STG_LD + cj * 8) * 2) = w;
-          }
+          rows_store(R, buf, hf);
+          if (hf + 1 < D / 64) rows_issue(R, buf, hf + 1);
         } else {
-          for (int e = tid; e < BM * 64; e += NCOMP) {
-            const int r = e >> 6, k = e & 63;
-            const int tok = sTok[r], ch = sCh[hf * 64 + k];
-            float v = 0.f;
-            if (tok >= 0 && ch < p.C) {
-              const int64_t row = (int64_t)sRowB[r] * p.N + tok;
-              v = load_as<float>(x, row * p.C + ch);
-              if (rstd) {
-                v = round_through(v * rstd[row], x_dt);
-                v = round_through(v * nw[ch], x_dt);
-              }
-            }
-            uint32_t pk = pack2<BF16>(v, 0.f);
-            *reinterpret_cast<uint16_t*>(sStg + (r * STG_LD + k) * 2) = (uint16_t)(pk & 0xFFFF);
-          }
+          rows_elem(buf, hf);
         }
         comp_sync();
-        // Token mix for tile ``warp`` (rows 16*warp .. +15).
 #pragma unroll
         for (int np = 0; np < 4; ++np) {
           uint32_t b0, b1, b2, b3;
@@ -444,11 +530,18 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const float* __restrict__ rstd, 
         mbar_arrive(bar_z + s);
       }
 
+      // -------- prefetch the next item's metadata and first half of rows
+      if (it + 1 < my_items) {
+        meta_store(mnext, buf ^ 1);
+        comp_sync();
+        if (*mCont(buf ^ 1)) rows_issue(R, buf ^ 1, 0);
+        if (it + 2 < my_items) mnext = meta_issue(it + 2);
+      }
+
       // -------- epilogue: delta = A_o Y, gamma, mask, residual, scatter
       mbar_wait(bar_yz + ((c - 1) & 1), ((c - 1) >> 1) & 1, sAbort);
       __syncwarp();
       tc_fence_after();
-      const float* ggq = gg + (int64_t)qc * D;
       for (int hf = 0; hf < D / 64; ++hf) {
         uint32_t yr[32];
         tmem_ld32(trow + C::T_Y + hf * 64 + cb, yr);
@@ -460,18 +553,19 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const float* __restrict__ rstd, 
           w.y = pack2<BF16>(__uint_as_float(yr[jj * 8 + 2]), __uint_as_float(yr[jj * 8 + 3]));
           w.z = pack2<BF16>(__uint_as_float(yr[jj * 8 + 4]), __uint_as_float(yr[jj * 8 + 5]));
           w.w = pack2<BF16>(__uint_as_float(yr[jj * 8 + 6]), __uint_as_float(yr[jj * 8 + 7]));
-          *reinterpret_cast<uint4*>(sStg + (r * STG_LD + cb + jj * 8) * 2) = w;
+          *reinterpret_cast<uint4*>(sPu + (r * STG_LD + cb + jj * 8) * 2) = w;
         }
         comp_sync();
         const int row0 = warp * 16 + g;
-        const int tokA = sTok[row0], tokB = sTok[row0 + 8];
-        const int bA = sRowB[row0], bB = sRowB[row0 + 8];
+        const int tokA = sTk[row0], tokB = sTk[row0 + 8];
+        const int bA = sRb[row0], bB = sRb[row0 + 8];
         const float sA = scale ? scale[bA] : 1.f, sB = scale ? scale[bB] : 1.f;
+        const uint32_t aEp = smem_u32(sPu);
 #pragma unroll
         for (int np = 0; np < 4; ++np) {
           __syncwarp();
           uint32_t b0, b1, b2, b3;
-          ldsm_x4_trans(aStg + ((warp * 16 + (lane & 15)) * STG_LD + np * 16 + (lane >> 4) * 8) * 2, b0, b1, b2,
+          ldsm_x4_trans(aEp + ((warp * 16 + (lane & 15)) * STG_LD + np * 16 + (lane >> 4) * 8) * 2, b0, b1, b2,
                         b3);
           float cc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
           mma16816<BF16>(cc[0], fa[2], b0, b1);
@@ -479,14 +573,15 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const float* __restrict__ rstd, 
 #pragma unroll
           for (int nb = 0; nb < 2; ++nb) {
             const int k = hf * 64 + np * 16 + nb * 8 + 2 * t4;
+            const float g0 = sG[k], g1 = sG[k + 1];
 #pragma unroll
             for (int hr = 0; hr < 2; ++hr) {
               const int tok = hr ? tokB : tokA;
               if (tok < 0) continue;
               const int64_t row = (int64_t)(hr ? bB : bA) * p.N + tok;
               const float sc = hr ? sB : sA;
-              float d0 = cc[nb][2 * hr] * ggq[k] * sc;
-              float d1 = cc[nb][2 * hr + 1] * ggq[k + 1] * sc;
+              float d0 = cc[nb][2 * hr] * g0 * sc;
+              float d1 = cc[nb][2 * hr + 1] * g1 * sc;
               if (cont) {
                 const int64_t off = row * p.C + ch0 + k;
                 if (residual) {
@@ -502,7 +597,7 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const float* __restrict__ rstd, 
               } else {
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
-                  const int ch = sCh[k + e];
+                  const int ch = sChs[k + e];
                   if (ch >= p.C) continue;
                   const int64_t off = row * p.C + ch;
                   float dv = e ? d1 : d0;

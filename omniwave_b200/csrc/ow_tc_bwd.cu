@@ -66,8 +66,8 @@ struct BCfg {
   static constexpr int OFF_PU = 0, OFF_PV = P_BYTES, OFF_X1 = 2 * P_BYTES;
   // DGRAD
   static constexpr int D_S = 3 * P_BYTES;                    // dU | dV (chunk)
-  static constexpr int D_W = D_S + 2 * Z_BYTES;              // g1 (3 sub) | g2 (2 sub)
-  static constexpr int D_END = D_W + 5 * BU_BYTES;
+  static constexpr int D_W = D_S + 2 * Z_BYTES;              // 2 stages x (Bu | Bv | BoT)
+  static constexpr int D_END = D_W + 6 * BU_BYTES;
   // UV
   static constexpr int U_S = 3 * P_BYTES;                    // dU_h | dV_h (128 features each)
   static constexpr int U_W = U_S + 4 * Z_BYTES;
@@ -78,8 +78,8 @@ struct BCfg {
   static constexpr int O_W = O_ZO + 2 * Z_BYTES;             // Bu | Bv | Bo
   static constexpr int O_END = O_W + 3 * BU_BYTES;
   static constexpr int MAX_END = D_END > U_END ? (D_END > O_END ? D_END : O_END) : (U_END > O_END ? U_END : O_END);
-  static constexpr int OFF_META = MAX_END;
-  static constexpr int META_BYTES = (2 * BM + D) * 4;
+  static constexpr int OFF_META = MAX_END;                   // row[BM], ch[D], cont
+  static constexpr int META_BYTES = (BM + D + 4) * 4;
   static constexpr int OFF_BAR = OFF_META + META_BYTES;
   static constexpr int BAR_BYTES = 16 * 8 + 16;
   static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024;
@@ -97,13 +97,14 @@ struct BCfg {
 template <int D>
 struct BPlan {
   int nD, nUVq, nOq, nH, grid;
-  size_t img, amat, gg, nw, contig, pdA, pdAo, puv, po, dxn, total;
+  size_t img, amat, gg, nw, contig, pdA, pdAo, puv, po, mo, dxn, total;
   BPlan(const Prob& p, bool block, int sms) {
     using C = BCfg<D>;
     nH = C::NH;
-    // Split one wave of CTAs by the roles' relative tensor work per item:
-    // DGRAD 5, UV 2.5 per half (5 for d=64's single half), O 4.
-    const double wD = 5.0, wU = (D == 64 ? 5.0 : 2.5) * nH, wO = 4.0, tot = wD + wU + wO;
+    // Split one wave of CTAs across the roles.  Every role gathers and mixes
+    // each of its items, so per-item time is similar across roles; weigh
+    // them by items to process (a UV half item has fewer chunks).
+    const double wD = 1.0, wU = (D == 64 ? 1.0 : 0.8) * nH, wO = 1.0, tot = wD + wU + wO;
     const int64_t nMB = (p.BQ() + 7) / 8;
     nUVq = std::max(1, (int)(sms * (wU / nH) / tot) / p.Qc);
     nOq = std::max(1, (int)(sms * wO / tot) / p.Qc);
@@ -123,6 +124,7 @@ struct BPlan {
     pdAo = take((size_t)p.Qc * nOq * NCOMP_WARPS * 256 * 4);
     puv = take((size_t)nH * p.Qc * nUVq * 2 * 128 * D * 4);
     po = take((size_t)p.Qc * nOq * C::RD * D * 4);
+    mo = take((size_t)p.Qc * C::RD * D * 4);
     dxn = block ? take((size_t)p.B * p.N * p.C * 4) : 0;
     total = o;
   }
@@ -231,8 +233,7 @@ __device__ __forceinline__ void load8v(const T* __restrict__ src, float (&v)[8])
 }
 
 struct GatherCtx {
-  const int* tok;   // [BM] token or -1
-  const int* rowb;  // [BM] batch
+  const int* row;   // [BM] b * N + token, or -1 for a pad row
   const int* ch;    // [D] channel indices
   int N, C;
   bool cont;
@@ -258,9 +259,9 @@ __device__ __forceinline__ void gather_half(const GatherCtx& gc, const TS* __res
       const int r = unit >> 3, cj = unit & 7;
       const int k = hf * 64 + cj * 8;
       float v[8];
-      const int tok = gc.tok[r];
-      if (tok >= 0) {
-        const int64_t row = (int64_t)gc.rowb[r] * gc.N + tok;
+      const int rw = gc.row[r];
+      if (rw >= 0) {
+        const int64_t row = rw;
         const int ch = ch0 + k;
         load8v<TS>(src + row * gc.C + ch, v);
         if (rstd) {
@@ -271,7 +272,7 @@ __device__ __forceinline__ void gather_half(const GatherCtx& gc, const TS* __res
             v[e] = round_through(t * nw[ch + e], x_dt);
           }
         }
-        const float s = scale ? scale[gc.rowb[r]] : 1.f;
+        const float s = scale ? scale[rw / gc.N] : 1.f;
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[e] *= s * (ggq ? ggq[k + e] : 1.f);
       } else {
@@ -288,20 +289,110 @@ __device__ __forceinline__ void gather_half(const GatherCtx& gc, const TS* __res
   } else {
     for (int e = tid; e < BM * 64; e += NCOMP) {
       const int r = e >> 6, k = hf * 64 + (e & 63);
-      const int tok = gc.tok[r], ch = gc.ch[k];
+      const int rw = gc.row[r], ch = gc.ch[k];
       float v = 0.f;
-      if (tok >= 0 && ch < gc.C) {
-        const int64_t row = (int64_t)gc.rowb[r] * gc.N + tok;
+      if (rw >= 0 && ch < gc.C) {
+        const int64_t row = rw;
         v = load_as<float>(src, row * gc.C + ch);
         if (rstd) {
           v = round_through(v * rstd[row], x_dt);
           v = round_through(v * nw[ch], x_dt);
         }
-        v *= (scale ? scale[gc.rowb[r]] : 1.f) * (ggq ? ggq[k] : 1.f);
+        v *= (scale ? scale[rw / gc.N] : 1.f) * (ggq ? ggq[k] : 1.f);
       }
       const uint32_t pk = pack2<BF16>(v, 0.f);
       *reinterpret_cast<uint16_t*>(dst + offs(r, k)) = (uint16_t)(pk & 0xFFFF);
     }
+  }
+}
+
+// Register-staged gather of NHF 64-channel halves (contiguous channel runs):
+// rows_issue() starts every load of the M-block at once; rows_store() later
+// converts one half and writes it out, so one memory round trip covers the
+// whole item.
+template <typename TS, int NHF>
+struct RowRegs {
+  static constexpr int VW = sizeof(TS) == 2 ? 1 : 2;  // 16-byte vectors per 8 elements
+  uint4 v[NHF][4][VW];
+  float rs[4];  // per-unit row factor: rstd (x) or drop-path scale (dOut)
+};
+
+template <typename TS, int NHF>
+__device__ __forceinline__ void rows_issue(RowRegs<TS, NHF>& R, const GatherCtx& gc, const TS* __restrict__ src,
+                                           int hf0, const float* __restrict__ rstd, const float* __restrict__ scale,
+                                           int tid) {
+  const int ch0 = gc.ch[0];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int unit = tid + u * NCOMP;
+    const int r = unit >> 3, cj = unit & 7;
+    const int rw = gc.row[r];
+    R.rs[u] = 1.f;
+    if (rw >= 0) {
+#pragma unroll
+      for (int h = 0; h < NHF; ++h) {
+        const uint4* p = reinterpret_cast<const uint4*>(src + (int64_t)rw * gc.C + ch0 + (hf0 + h) * 64 + cj * 8);
+#pragma unroll
+        for (int vv = 0; vv < RowRegs<TS, NHF>::VW; ++vv) R.v[h][u][vv] = __ldg(p + vv);
+      }
+      if (rstd) R.rs[u] = rstd[rw];
+      else if (scale) R.rs[u] = scale[rw / gc.N];
+    } else {
+#pragma unroll
+      for (int h = 0; h < NHF; ++h)
+#pragma unroll
+        for (int vv = 0; vv < RowRegs<TS, NHF>::VW; ++vv) R.v[h][u][vv] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+}
+
+// x mode (nw != null or rstd given): round(round(v * rstd) * nw[ch]); gradient
+// mode: v * scale * ggq[k].  ``hf`` is the absolute half (channel offset).
+template <typename TS, int NHF, bool BF16>
+__device__ __forceinline__ void rows_store(const RowRegs<TS, NHF>& R, int h, int hf, const GatherCtx& gc,
+                                           unsigned char* dst, bool sw, bool xnorm, const float* __restrict__ nw,
+                                           const float* __restrict__ ggq, int x_dt, int tid) {
+  const int ch0 = gc.ch[0];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int unit = tid + u * NCOMP;
+    const int r = unit >> 3, cj = unit & 7;
+    const int k = hf * 64 + cj * 8;
+    float v[8];
+    if constexpr (sizeof(TS) == 2) {
+      const uint32_t w[4] = {R.v[h][u][0].x, R.v[h][u][0].y, R.v[h][u][0].z, R.v[h][u][0].w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float2 f = unpack2<std::is_same_v<TS, __nv_bfloat16>>(w[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+      }
+    } else {
+#pragma unroll
+      for (int vv = 0; vv < 2; ++vv) {
+        v[4 * vv + 0] = __uint_as_float(R.v[h][u][vv].x);
+        v[4 * vv + 1] = __uint_as_float(R.v[h][u][vv].y);
+        v[4 * vv + 2] = __uint_as_float(R.v[h][u][vv].z);
+        v[4 * vv + 3] = __uint_as_float(R.v[h][u][vv].w);
+      }
+    }
+    if (xnorm) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float t = round_through(v[e] * R.rs[u], x_dt);
+        v[e] = round_through(t * nw[ch0 + k + e], x_dt);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] *= R.rs[u] * (ggq ? ggq[k + e] : 1.f);
+    }
+    uint4 w;
+    w.x = pack2<BF16>(v[0], v[1]);
+    w.y = pack2<BF16>(v[2], v[3]);
+    w.z = pack2<BF16>(v[4], v[5]);
+    w.w = pack2<BF16>(v[6], v[7]);
+    const uint32_t off = sw ? sw128_off(r, k, BM) : (uint32_t)((r * STG_LD + cj * 8) * 2);
+    *reinterpret_cast<uint4*>(dst + off) = w;
   }
 }
 
@@ -379,9 +470,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
   unsigned char* sPu = sm + C::OFF_PU;
   unsigned char* sPv = sm + C::OFF_PV;
   unsigned char* sX1 = sm + C::OFF_X1;
-  int* sTok = reinterpret_cast<int*>(sm + C::OFF_META);
-  int* sRowB = sTok + BM;
-  int* sCh = sRowB + BM;
+  int* sRow = reinterpret_cast<int*>(sm + C::OFF_META);
+  int* sCh = sRow + BM;
+  volatile int* sCont = sCh + D;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
   uint64_t* bar_p = bars + 0;
   uint64_t* bar_a = bars + 1;
@@ -390,7 +481,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
   uint64_t* bar_w = bars + 4;
   uint64_t* bar_zo = bars + 5;
   uint64_t* bar_g1 = bars + 6;
-  uint64_t* bar_g2 = bars + 7;
+  uint64_t* bar_g2 = bars + 7;   // DGRAD: second weight stage
+  uint64_t* bar_e0 = bars + 8;   // DGRAD: weight stage 0 free
+  uint64_t* bar_e1 = bars + 9;   // DGRAD: weight stage 1 free
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
 
@@ -445,6 +538,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
     mbar_init(bar_zo, NCOMP);
     mbar_init(bar_g1, 1);
     mbar_init(bar_g2, 1);
+    mbar_init(bar_e0, 1);
+    mbar_init(bar_e1, 1);
     *sAbort = 0;
     fence_mbar_init();
   }
@@ -459,7 +554,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
   int g1_off = 0, g1_bytes = 0, g2_off = 0, g2_bytes = 0;
   unsigned char* sW = nullptr;
   if (role == R_DGRAD) {
-    sW = sm + C::D_W; g1_off = 0; g1_bytes = 3 * C::BU_BYTES; g2_off = 3 * C::BU_BYTES; g2_bytes = 2 * C::BU_BYTES;
+    // Two stages of one group; dP reads B_u / B_v from the same images.
+    sW = sm + C::D_W; g1_off = 0; g1_bytes = 3 * C::BU_BYTES;
   } else if (role == R_UV) {
     sW = sm + C::U_W; g1_off = 0; g1_bytes = 3 * C::BU_BYTES;
   } else {
@@ -485,12 +581,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
         mbar_arrive_expect_tx(bar_g2, g2_bytes);
         bulk_g2s(sW2, chunk_img(c) + g2_off, g2_bytes, bar_g2);
       };
-      load1(0);
-      if (g2_bytes) load2(0);
-      for (int c = 0; c + 1 < total_chunks; ++c) {
-        if (mbar_wait(bar_a, c & 1, sAbort)) load1(c + 1);
-        if (g2_bytes && mbar_wait(bar_b, c & 1, sAbort)) load2(c + 1);
-        if (*sAbort) break;
+      if (role == R_DGRAD) {
+        auto loadst = [&](int c) {
+          uint64_t* bar = (c & 1) ? bar_g2 : bar_g1;
+          mbar_arrive_expect_tx(bar, g1_bytes);
+          bulk_g2s(sW + (c & 1) * g1_bytes, chunk_img(c), g1_bytes, bar);
+        };
+        loadst(0);
+        if (total_chunks > 1) loadst(1);
+        for (int c = 0; c + 2 < total_chunks; ++c) {
+          if (mbar_wait((c & 1) ? bar_e1 : bar_e0, (c >> 1) & 1, sAbort)) loadst(c + 2);
+          if (*sAbort) break;
+        }
+      } else {
+        load1(0);
+        if (g2_bytes) load2(0);
+        for (int c = 0; c + 1 < total_chunks; ++c) {
+          if (mbar_wait(bar_a, c & 1, sAbort)) load1(c + 1);
+          if (g2_bytes && mbar_wait(bar_b, c & 1, sAbort)) load2(c + 1);
+          if (*sAbort) break;
+        }
       }
     }
   } else if (warp == MMA_WARP) {
@@ -499,6 +609,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
       constexpr uint32_t ID_N64 = idesc_f16(BM, NC, BF16);
       constexpr uint32_t ID_ND = idesc_f16(BM, D, BF16);
       constexpr uint32_t ID_MN = idesc_f16_mn(BM, D, BF16);
+      constexpr uint32_t ID_BMN = idesc_f16(BM, D, BF16) | (1u << 16);  // A K-major, B MN-major
       const uint32_t aPu = smem_u32(sPu), aPv = smem_u32(sPv), aX1 = smem_u32(sX1);
       const uint32_t aW = smem_u32(sW);
       auto kmma = [&](uint32_t tcol, uint32_t aA, int arows, uint32_t aB, int brows, int ksteps, uint32_t id,
@@ -517,25 +628,37 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
         mbar_wait(bar_p, it & 1, sAbort);
         tc_fence_after();
         for (int j = 0; j < nchunks; ++j, ++c) {
-          mbar_wait(bar_g1, c & 1, sAbort);
+          uint32_t aWc = aW;
+          if (role == R_DGRAD) {
+            aWc = aW + (c & 1) * 3 * C::BU_BYTES;
+            mbar_wait((c & 1) ? bar_g2 : bar_g1, (c >> 1) & 1, sAbort);
+          } else {
+            mbar_wait(bar_g1, c & 1, sAbort);
+          }
           tc_fence_after();
           if (!*sAbort) {
-            kmma(C::T_U, aPu, BM, aW, NC, D / 16, ID_N64, false);
-            kmma(C::T_V, aPv, BM, aW + C::BU_BYTES, NC, D / 16, ID_N64, false);
-            if (role != R_O) kmma(C::T_DZ, aX1, BM, aW + 2 * C::BU_BYTES, NC, D / 16, ID_N64, false);
+            kmma(C::T_U, aPu, BM, aWc, NC, D / 16, ID_N64, false);
+            kmma(C::T_V, aPv, BM, aWc + C::BU_BYTES, NC, D / 16, ID_N64, false);
+            if (role != R_O) kmma(C::T_DZ, aX1, BM, aWc + 2 * C::BU_BYTES, NC, D / 16, ID_N64, false);
           }
           umma_commit(bar_a);
           mbar_wait(bar_du, c & 1, sAbort);
           tc_fence_after();
           if (role == R_DGRAD) {
-            mbar_wait(bar_g2, c & 1, sAbort);
-            tc_fence_after();
             if (!*sAbort) {
+              // dP_u += dU_q B_u[:, q]^T: B is the B_u chunk image read MN-major
+              // (N = channels in 64-wide atoms NC*128 bytes apart, K = features).
               const uint32_t aS = smem_u32(sm + C::D_S);
-              kmma(C::T_DPU, aS, BM, aW + 3 * C::BU_BYTES, D, NC / 16, ID_ND, j > 0);
-              kmma(C::T_DPV, aS + C::Z_BYTES, BM, aW + 4 * C::BU_BYTES, D, NC / 16, ID_ND, j > 0);
+              for (int kk = 0; kk < NC / 16; ++kk) {
+                umma_f16(tbase + C::T_DPU, sdesc_sw128(sw128_kstep(aS, kk, BM)),
+                         sdesc_sw128_mn(aWc + kk * 2048, NC * 128), ID_BMN, (j > 0 || kk > 0) ? 1u : 0u);
+                umma_f16(tbase + C::T_DPV, sdesc_sw128(sw128_kstep(aS + C::Z_BYTES, kk, BM)),
+                         sdesc_sw128_mn(aWc + C::BU_BYTES + kk * 2048, NC * 128), ID_BMN,
+                         (j > 0 || kk > 0) ? 1u : 0u);
+              }
             }
             umma_commit(bar_b);
+            umma_commit((c & 1) ? bar_e1 : bar_e0);
           } else if (role == R_O) {
             mbar_wait(bar_g2, c & 1, sAbort);
             tc_fence_after();
@@ -568,23 +691,38 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
     const int lq = warp & 3, cb = (warp >> 2) * 32;
     const int r = lq * 32 + lane;
     const uint32_t trow = tbase + ((uint32_t)(lq * 32) << 16);
-    uint32_t fAoT[4], fAuT[4], fAvT[4], fAo[4];
-    load_afrag(a.amat + 512, true, g, t4, fAoT);
-    load_afrag(a.amat + 0, true, g, t4, fAuT);
-    load_afrag(a.amat + 256, true, g, t4, fAvT);
-    load_afrag(a.amat + 512, false, g, t4, fAo);
-    uint32_t fAu[4], fAv[4];
-    load_afrag(a.amat + 0, false, g, t4, fAu);
-    load_afrag(a.amat + 256, false, g, t4, fAv);
+    // Token-mix fragments are (re)loaded right before each use (L1-resident)
+    // to keep them out of the long-lived register set.
+    auto frag = [&](int m, bool tr, uint32_t (&f)[4]) { load_afrag(a.amat + m * 256, tr, g, t4, f); };
     float accA[2][2][4] = {};  // DGRAD: dA_u, dA_v ; O: dA_o in accA[0]
     const TX* x = (const TX*)a.x;
     const TO* dout = (const TO*)a.dout;
     int c = 0, pc = 0;
     unsigned char* stg_a = role == R_O ? sm + C::O_Z : sm + C::D_S;  // phase-A staging
-    for (int it = 0; it < (int)n_items; ++it) {
+    // Metadata of an item (packed row b*N+token per M-block row, channel per
+    // group column, contiguity flag), loaded into registers one item ahead.
+    struct MetaReg { int row, ch, cont; };
+    auto meta_issue = [&](int it) {
+      MetaReg m{-1, 0, 0};
       const int64_t item = it0 + (int64_t)it * it_step;
       const int qc = (int)(item / nMB), mb = (int)(item - (int64_t)qc * nMB);
-      GatherCtx gc{sTok, sRowB, sCh, p.N, p.C, a.vec_ok && a.contig[qc] != 0};
+      if (tid < BM) {
+        const int64_t t = (int64_t)mb * 8 + (tid >> 4);
+        if (t < BQ) {
+          const int b = (int)(t / p.Qs);
+          const int tok = p.tok[(t - (int64_t)b * p.Qs) * 16 + (tid & 15)];
+          m.row = tok < p.N ? b * p.N + tok : -1;
+        }
+      }
+      if (tid < D) m.ch = p.ch[qc * D + tid];
+      if (tid == 0) m.cont = a.vec_ok && a.contig[qc] != 0;
+      return m;
+    };
+    MetaReg mreg{-1, 0, 0};
+    if (n_items > 0) mreg = meta_issue(0);
+    for (int it = 0; it < (int)n_items; ++it) {
+      const int64_t item = it0 + (int64_t)it * it_step;
+      const int qc = (int)(item / nMB);
       const float* ggq = a.gg + (int64_t)qc * D;
       // UV: the previous item's weight-gradient products read P and dU/dV.
       if (role == R_UV && it > 0) {
@@ -595,36 +733,80 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
         mbar_wait(bar_w, (pc - 1) & 1, sAbort);
         __syncwarp();
       }
+      comp_sync();  // previous item is done with metadata and staging
+      if (tid < BM) sRow[tid] = mreg.row;
+      if (tid < D) sCh[tid] = mreg.ch;
+      if (tid == 0) *sCont = mreg.cont;
       comp_sync();
-      for (int rr = tid; rr < BM; rr += NCOMP) {
-        const int64_t t = (int64_t)mb * 8 + (rr >> 4);
-        int tok = p.N, b = 0;
-        if (t < BQ) {
-          b = (int)(t / p.Qs);
-          tok = p.tok[(t - (int64_t)b * p.Qs) * 16 + (rr & 15)];
-        }
-        sTok[rr] = tok < p.N ? tok : -1;
-        sRowB[rr] = b;
-      }
-      for (int k = tid; k < D; k += NCOMP) sCh[k] = p.ch[qc * D + k];
-      comp_sync();
+      if (it + 1 < (int)n_items) mreg = meta_issue(it + 1);
+      GatherCtx gc{sRow, sCh, p.N, p.C, *sCont != 0};
       // ---- phase A: P_u, P_v from x; dY' (or G') from dOut
       const uint32_t aStg = smem_u32(stg_a);
-      for (int hf = 0; hf < D / 64; ++hf) {
-        gather_half<TX, BF16>(gc, x, hf, a.rstd, a.nw, a.x_dt, nullptr, nullptr, stg_a, false, tid);
-        comp_sync();
-        __syncwarp();
-        mix_half<BF16>(aStg, fAu, sPu, hf, warp, lane);
-        mix_half<BF16>(aStg, fAv, sPv, hf, warp, lane);
-        comp_sync();
-        if (role == R_O) {
-          gather_half<TO, BF16>(gc, dout, hf, nullptr, nullptr, 0, a.scale, nullptr, sX1, true, tid);
-        } else {
-          gather_half<TO, BF16>(gc, dout, hf, nullptr, nullptr, 0, a.scale, ggq, stg_a, false, tid);
+      const bool xnorm = a.rstd != nullptr;
+      if (gc.cont) {
+        constexpr int NHF = D / 64;
+        constexpr bool both16 = sizeof(TX) == 2 && sizeof(TO) == 2;
+        RowRegs<TX, NHF> rx;
+        RowRegs<TO, NHF> rg;
+        rows_issue<TX, NHF>(rx, gc, x, 0, a.rstd, nullptr, tid);
+        if constexpr (both16) rows_issue<TO, NHF>(rg, gc, dout, 0, nullptr, a.scale, tid);
+#pragma unroll
+        for (int hf = 0; hf < NHF; ++hf) {
+          rows_store<TX, NHF, BF16>(rx, hf, hf, gc, stg_a, false, xnorm, a.nw, nullptr, a.x_dt, tid);
           comp_sync();
           __syncwarp();
-          mix_half<BF16>(aStg, fAoT, sX1, hf, warp, lane);
+          {
+            uint32_t f[4];
+            frag(0, false, f);
+            mix_half<BF16>(aStg, f, sPu, hf, warp, lane);
+            frag(1, false, f);
+            mix_half<BF16>(aStg, f, sPv, hf, warp, lane);
+          }
           comp_sync();
+        }
+        if constexpr (!both16) rows_issue<TO, NHF>(rg, gc, dout, 0, nullptr, a.scale, tid);
+#pragma unroll
+        for (int hf = 0; hf < NHF; ++hf) {
+          if (role == R_O) {
+            rows_store<TO, NHF, BF16>(rg, hf, hf, gc, sX1, true, false, nullptr, nullptr, 0, tid);
+          } else {
+            rows_store<TO, NHF, BF16>(rg, hf, hf, gc, stg_a, false, false, nullptr, ggq, 0, tid);
+            comp_sync();
+            __syncwarp();
+            {
+              uint32_t f[4];
+              frag(2, true, f);
+              mix_half<BF16>(aStg, f, sX1, hf, warp, lane);
+            }
+            comp_sync();
+          }
+        }
+      } else {
+        for (int hf = 0; hf < D / 64; ++hf) {
+          gather_half<TX, BF16>(gc, x, hf, a.rstd, a.nw, a.x_dt, nullptr, nullptr, stg_a, false, tid);
+          comp_sync();
+          __syncwarp();
+          {
+            uint32_t f[4];
+            frag(0, false, f);
+            mix_half<BF16>(aStg, f, sPu, hf, warp, lane);
+            frag(1, false, f);
+            mix_half<BF16>(aStg, f, sPv, hf, warp, lane);
+          }
+          comp_sync();
+          if (role == R_O) {
+            gather_half<TO, BF16>(gc, dout, hf, nullptr, nullptr, 0, a.scale, nullptr, sX1, true, tid);
+          } else {
+            gather_half<TO, BF16>(gc, dout, hf, nullptr, nullptr, 0, a.scale, ggq, stg_a, false, tid);
+            comp_sync();
+            __syncwarp();
+            {
+              uint32_t f[4];
+              frag(2, true, f);
+              mix_half<BF16>(aStg, f, sX1, hf, warp, lane);
+            }
+            comp_sync();
+          }
         }
       }
       fence_proxy_async_smem();
@@ -719,6 +901,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
             uint32_t b0, b1, b2, b3;
             ldsm_x4_trans(smem_u32(sz + sw128_off(rowr, colr, BM)), b0, b1, b2, b3);
             float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+            uint32_t fAo[4];
+            frag(2, false, fAo);
             mma16816<BF16>(c0, fAo, b0, b1);
             mma16816<BF16>(c1, fAo, b2, b3);
             const int r0 = warp * 16 + g, k0 = (j & 1) * 64 + np * 16 + 2 * t4;
@@ -746,6 +930,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
         unsigned char* stC = sm + 2 * STG_BYTES;  // T half
         const uint32_t aA = smem_u32(stA), aB = smem_u32(stB), aC = smem_u32(stC);
         for (int hf = 0; hf < D / 64; ++hf) {
+          // Start the re-gather of T (for dA_u, dA_v) before the TMEM reads.
+          RowRegs<TX, 1> rt;
+          if (gc.cont) rows_issue<TX, 1>(rt, gc, x, hf, a.rstd, nullptr, tid);
           uint32_t pr[32], qr[32];
           tmem_ld32(trow + C::T_DPU + hf * 64 + cb, pr);
           tmem_ld32(trow + C::T_DPV + hf * 64 + cb, qr);
@@ -764,7 +951,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
             *reinterpret_cast<uint4*>(stA + (r * STG_LD + cb + jj * 8) * 2) = w1;
             *reinterpret_cast<uint4*>(stB + (r * STG_LD + cb + jj * 8) * 2) = w2;
           }
-          gather_half<TX, BF16>(gc, x, hf, a.rstd, a.nw, a.x_dt, nullptr, nullptr, stC, false, tid);
+          if (gc.cont) rows_store<TX, 1, BF16>(rt, 0, hf, gc, stC, false, xnorm, a.nw, nullptr, a.x_dt, tid);
+          else gather_half<TX, BF16>(gc, x, hf, a.rstd, a.nw, a.x_dt, nullptr, nullptr, stC, false, tid);
           comp_sync();
           __syncwarp();
           // dA_u += dP_u T^T, dA_v += dP_v T^T (tile ``warp``)
@@ -775,8 +963,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           gram16<BF16>(accA[1], rowB, rowC, lane);
           // dT = A_u^T dP_u + A_v^T dP_v, scattered to dX / dxn
           const int row0 = warp * 16 + g;
-          const int tokA = sTok[row0], tokB = sTok[row0 + 8];
-          const int bA = sRowB[row0], bB = sRowB[row0 + 8];
+          const int rwA = sRow[row0], rwB = sRow[row0 + 8];
 #pragma unroll
           for (int np = 0; np < 4; ++np) {
             __syncwarp();
@@ -784,18 +971,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
             ldsm_x4_trans(aA + ((warp * 16 + (lane & 15)) * STG_LD + np * 16 + (lane >> 4) * 8) * 2, b0, b1, b2, b3);
             ldsm_x4_trans(aB + ((warp * 16 + (lane & 15)) * STG_LD + np * 16 + (lane >> 4) * 8) * 2, e0, e1, e2, e3);
             float cc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-            mma16816<BF16>(cc[0], fAuT, b0, b1);
-            mma16816<BF16>(cc[1], fAuT, b2, b3);
-            mma16816<BF16>(cc[0], fAvT, e0, e1);
-            mma16816<BF16>(cc[1], fAvT, e2, e3);
+            uint32_t fT[4];
+            frag(0, true, fT);
+            mma16816<BF16>(cc[0], fT, b0, b1);
+            mma16816<BF16>(cc[1], fT, b2, b3);
+            frag(1, true, fT);
+            mma16816<BF16>(cc[0], fT, e0, e1);
+            mma16816<BF16>(cc[1], fT, e2, e3);
 #pragma unroll
             for (int nb = 0; nb < 2; ++nb) {
               const int k = hf * 64 + np * 16 + nb * 8 + 2 * t4;
 #pragma unroll
               for (int hr = 0; hr < 2; ++hr) {
-                const int tok = hr ? tokB : tokA;
-                if (tok < 0) continue;
-                const int64_t row = (int64_t)(hr ? bB : bA) * p.N + tok;
+                const int rw = hr ? rwB : rwA;
+                if (rw < 0) continue;
+                const int64_t row = rw;
                 const float d0 = cc[nb][2 * hr], d1 = cc[nb][2 * hr + 1];
                 if (gc.cont) {
                   const int64_t off = row * p.C + sCh[0] + k;
@@ -933,62 +1123,76 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// Reduction of the per-CTA partials into the gradient outputs (fixed order).
+// Reduction of the per-CTA partials into the gradient outputs.  Every sum is
+// taken in a fixed order (per-thread loops over partial slots, then a fixed
+// shuffle tree), so results are bitwise reproducible.
 // ---------------------------------------------------------------------------
+// dB_u, dB_v [qc][c][e] and M_o -> dB_o [qc][e][c]: one thread per output,
+// consecutive threads on consecutive c so the partial reads coalesce.
 template <int D, typename TW>
-__global__ void tc_bwd_reduce_kernel(Prob p, BwdArgs a, const TW* __restrict__ bo, TW* __restrict__ da_u,
-                                     TW* __restrict__ da_v, TW* __restrict__ da_o, TW* __restrict__ db_u,
-                                     TW* __restrict__ db_v, TW* __restrict__ db_o, TW* __restrict__ dgamma) {
+__global__ void tc_bwd_reduce_b_kernel(Prob p, BwdArgs a, TW* __restrict__ db_u, TW* __restrict__ db_v,
+                                       TW* __restrict__ db_o, float* __restrict__ mo) {
   using C = BCfg<D>;
   const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int64_t nB = (int64_t)p.Qc * D * C::RD;
-  // dB_u, dB_v : [qc][c][e]; partial layout [h][qc][j][m][e%128][c]
-  for (int64_t i = tid; i < 2 * nB; i += stride) {
+  for (int64_t i = tid; i < 3 * nB; i += stride) {
     const int m = (int)(i / nB);
     const int64_t rem = i - m * nB;
-    const int qc = (int)(rem / (D * C::RD));
-    const int c = (int)((rem / C::RD) % D), e = (int)(rem % C::RD);
-    const int hh = e / 128, el = e % 128;
-    float s = 0.f;
-    for (int j = 0; j < a.nUVq; ++j)
-      s += a.puv[((((int64_t)(hh * p.Qc + qc) * a.nUVq + j) * 2 + m) * 128 + el) * D + c];
-    (m ? db_v : db_u)[rem] = Elem<TW>::from(s);
-  }
-  // dB_o = gamma * M_o : [qc][e][c]
-  for (int64_t i = tid; i < nB; i += stride) {
-    const int qc = (int)(i / (C::RD * D));
-    const int64_t rem = i - (int64_t)qc * C::RD * D;
-    float s = 0.f;
-    for (int j = 0; j < a.nOq; ++j) s += a.po[((int64_t)qc * a.nOq + j) * C::RD * D + rem];
-    const int cidx = (int)(rem % D);
-    db_o[i] = Elem<TW>::from(s * a.gg[(int64_t)qc * D + cidx]);
-  }
-  // dgamma[ch[qc][c]] = sum_e B_o[qc][e][c] * M_o[qc][e][c]
-  for (int64_t i = tid; i < (int64_t)p.Qc * D; i += stride) {
-    const int qc = (int)(i / D), cidx = (int)(i % D);
-    const int ch = p.ch[i];
-    if (ch >= p.C) continue;
-    float s = 0.f;
-    for (int e = 0; e < C::RD; ++e) {
-      float m = 0.f;
-      for (int j = 0; j < a.nOq; ++j) m += a.po[(((int64_t)qc * a.nOq + j) * C::RD + e) * D + cidx];
-      s += load_as<float>(bo, ((int64_t)qc * C::RD + e) * D + cidx) * m;
-    }
-    dgamma[ch] = Elem<TW>::from(s);
-  }
-  // token-mix gradients
-  for (int64_t i = tid; i < 3 * 256; i += stride) {
-    const int m = (int)(i / 256), e = (int)(i % 256);
+    const int qc = (int)(rem / (C::RD * D));
+    const int e = (int)((rem / D) % C::RD), c = (int)(rem % D);
     float s = 0.f;
     if (m < 2) {
-      for (int b = 0; b < a.nD; ++b)
-        for (int w = 0; w < NCOMP_WARPS; ++w) s += a.pdA[((int64_t)b * NCOMP_WARPS + w) * 512 + m * 256 + e];
+      const int hh = e / 128, el = e % 128;
+      for (int j = 0; j < a.nUVq; ++j)
+        s += a.puv[((((int64_t)(hh * p.Qc + qc) * a.nUVq + j) * 2 + m) * 128 + el) * D + c];
+      (m ? db_v : db_u)[((int64_t)qc * D + c) * C::RD + e] = Elem<TW>::from(s);
     } else {
-      const int64_t n = (int64_t)p.Qc * a.nOq * NCOMP_WARPS;
-      for (int64_t b = 0; b < n; ++b) s += a.pdAo[b * 256 + e];
+      for (int j = 0; j < a.nOq; ++j) s += a.po[((int64_t)qc * a.nOq + j) * C::RD * D + (int64_t)e * D + c];
+      mo[rem] = s;
+      db_o[rem] = Elem<TW>::from(s * a.gg[(int64_t)qc * D + c]);
     }
-    (m == 0 ? da_u : (m == 1 ? da_v : da_o))[e] = Elem<TW>::from(s);
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// dgamma[ch[qc][c]] = sum_e B_o[qc][e][c] * M_o[qc][e][c]  (one warp per (qc, c)),
+// and the token-mix gradients (one warp per element).
+template <int D, typename TW>
+__global__ void tc_bwd_reduce_small_kernel(Prob p, BwdArgs a, const TW* __restrict__ bo,
+                                           const float* __restrict__ mo, TW* __restrict__ dgamma,
+                                           TW* __restrict__ da_u, TW* __restrict__ da_v, TW* __restrict__ da_o) {
+  using C = BCfg<D>;
+  const int lane = threadIdx.x & 31;
+  const int64_t gw = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t n_gamma = (int64_t)p.Qc * D;
+  for (int64_t w = gw; w < n_gamma + 3 * 256; w += nw) {
+    float s = 0.f;
+    if (w < n_gamma) {
+      const int qc = (int)(w / D), c = (int)(w % D);
+      for (int e = lane; e < C::RD; e += 32)
+        s += load_as<float>(bo, ((int64_t)qc * C::RD + e) * D + c) * mo[((int64_t)qc * C::RD + e) * D + c];
+      s = warp_sum(s);
+      const int ch = p.ch[w];
+      if (lane == 0 && ch < p.C) dgamma[ch] = Elem<TW>::from(s);
+    } else {
+      const int m = (int)((w - n_gamma) / 256), e = (int)((w - n_gamma) % 256);
+      if (m < 2) {
+        const int64_t n = (int64_t)a.nD * NCOMP_WARPS;
+        for (int64_t b = lane; b < n; b += 32) s += a.pdA[b * 512 + m * 256 + e];
+      } else {
+        const int64_t n = (int64_t)p.Qc * a.nOq * NCOMP_WARPS;
+        for (int64_t b = lane; b < n; b += 32) s += a.pdAo[b * 256 + e];
+      }
+      s = warp_sum(s);
+      if (lane == 0) (m == 0 ? da_u : (m == 1 ? da_v : da_o))[e] = Elem<TW>::from(s);
+    }
   }
 }
 
@@ -1090,8 +1294,11 @@ int tc_backward_t(const ow_bigemm_args_t* ar, const ow_bigemm_grads_t* gr, const
 
   auto red = [&](auto* tw) {
     using TW = std::remove_pointer_t<decltype(tw)>;
-    launch(tc_bwd_reduce_kernel<D, TW>, 148 * 4, 256, 0, st, p, a, (const TW*)ar->b_o, (TW*)gr->da_u,
-           (TW*)gr->da_v, (TW*)gr->da_o, (TW*)gr->db_u, (TW*)gr->db_v, (TW*)gr->db_o, (TW*)gr->dgamma);
+    float* mo = (float*)(base + pl.mo);
+    launch(tc_bwd_reduce_b_kernel<D, TW>, 148 * 8, 256, 0, st, p, a, (TW*)gr->db_u, (TW*)gr->db_v,
+           (TW*)gr->db_o, mo);
+    launch(tc_bwd_reduce_small_kernel<D, TW>, 148, 256, 0, st, p, a, (const TW*)ar->b_o, (const float*)mo,
+           (TW*)gr->dgamma, (TW*)gr->da_u, (TW*)gr->da_v, (TW*)gr->da_o);
   };
   switch (ar->w_dtype) {
     case OW_DTYPE_F32: red((float*)nullptr); break;
