@@ -22,6 +22,13 @@ workload.  Under torchrun only rank 0 runs it.
 
 Multi-GPU: one process per GPU; the batch is sharded (each rank runs its own
 B=128 sweep, no data-path collective), so scaling is weak.
+
+The same line carries ``omniweave_t``: OmniWeave-T (random init broadcast
+from rank 0, synthetic N(0,1) images, per-rank seeds) measured as BASELINE
+configs 3-5 -- bf16 inference at 256 images per GPU, batch-sharded with no
+communication, and the DDP training step at 128 images per GPU (bf16
+autocast, cross-entropy on uniform labels, NCCL gradient all-reduce, AdamW
+lr 1e-3 wd 0.05).  Images/s are whole-job totals over max-over-ranks time.
 """
 
 from __future__ import annotations
@@ -203,12 +210,12 @@ def run_ours(args) -> None:
         torch.distributed.barrier()
     torch.cuda.synchronize()
     launches0 = lib.ow_launch_count()
-    with _Clocks(dev.index) as clk:
-        t0.record()
-        for s in range(args.steps):
-            step(evs[s])
-        t1.record()
-        torch.cuda.synchronize()
+    clk = _Clocks(dev.index).__enter__()  # sampled over every timed region below
+    t0.record()
+    for s in range(args.steps):
+        step(evs[s])
+    t1.record()
+    torch.cuda.synchronize()
     launches = lib.ow_launch_count() - launches0
     if world > 1:
         torch.distributed.barrier()
@@ -237,6 +244,13 @@ def run_ours(args) -> None:
 
     # --- end-to-end through the public API with host buffers -----------------
     e2e = _e2e(args, cases, names, dev, world)
+    del cases
+    torch.cuda.empty_cache()
+
+    model_line = None
+    if not args.no_model:
+        model_line = _model_bench(args, dev, world, rank, lib)
+    clk.__exit__(None, None, None)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -282,6 +296,8 @@ def run_ours(args) -> None:
             "gpu_launches": int(launches),
             "clocks": clk.summary(),
         }
+        if model_line is not None:
+            line["omniweave_t"] = model_line
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -335,6 +351,76 @@ def _e2e(args, cases, names, dev, world):
     val = step_flops(BATCH) * steps * world / (float(ms.item()) * 1e-3) / 1e12
     return {"value": round(val, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d // steps,
             "d2h_bytes_per_step": d2h // steps}
+
+
+MODEL_FWD_GFLOP_PER_IMG = 3.757  # OmniWeave-T at 224x224: 2.895 BiGEMM + 0.863 Linear
+
+
+def _timed(fn, steps, warmup, dev, world):
+    """Max-over-ranks device time (ms) of ``steps`` calls after ``warmup``."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+    return float(ms.item())
+
+
+def _model_bench(args, dev, world, rank, lib):
+    from omniwave_b200 import create_model
+    from omniwave_b200.train import TrainStep, broadcast_parameters
+
+    out = {"model": "omniweave_t", "input": "224x224", "data": "synthetic N(0,1), per-rank seeds"}
+    # ---- inference (configs 3/4): bf16 weights, 256 images per GPU
+    torch.manual_seed(0)
+    model = create_model("omniweave_t").to(dev)
+    broadcast_parameters(model)
+    model = model.to(torch.bfloat16).eval()
+    bi = 256
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    imgs = torch.randn(bi, 3, 224, 224, device=dev, generator=g, dtype=torch.bfloat16)
+
+    @torch.no_grad()
+    def infer():
+        model(imgs)
+
+    ms = _timed(infer, args.model_steps, args.warmup, dev, world)
+    out["infer_batch_per_gpu"] = bi
+    out["infer_img_per_s"] = round(bi * world * args.model_steps / (ms * 1e-3), 1)
+    out["infer_ms_per_step"] = round(ms / args.model_steps, 3)
+    del model, imgs
+    torch.cuda.empty_cache()
+    # ---- training step (config 5): DDP, AdamW, bf16 autocast, 128 per GPU
+    torch.manual_seed(0)
+    model = create_model("omniweave_t").to(dev)
+    ts = TrainStep(model, lr=1e-3, weight_decay=0.05, amp_dtype=torch.bfloat16)
+    bt = 128
+    x = torch.randn(bt, 3, 224, 224, device=dev, generator=g)
+    y = torch.randint(0, 1000, (bt,), device=dev, generator=g)
+    launches0 = lib.ow_launch_count()
+    ms = _timed(lambda: ts.step(x, y), args.model_steps, args.warmup, dev, world)
+    ts.check_finite()
+    img_s = bt * world * args.model_steps / (ms * 1e-3)
+    out["train_batch_per_gpu"] = bt
+    out["train_img_per_s"] = round(img_s, 1)
+    out["train_ms_per_step"] = round(ms / args.model_steps, 3)
+    out["train_tflops"] = round(img_s * 3 * MODEL_FWD_GFLOP_PER_IMG * 1e9 / 1e12, 2)
+    out["train_parallelism"] = f"DDP x{world} (NCCL bucketed all-reduce)" if world > 1 else "single GPU"
+    out["bigemm_launches_in_train_region"] = int(lib.ow_launch_count() - launches0)
+    del ts, model, x, y
+    torch.cuda.empty_cache()
+    return out
 
 
 def _peaks():
@@ -459,6 +545,8 @@ def main(argv=None) -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-model", action="store_true", help="skip the OmniWeave-T measurements")
+    ap.add_argument("--model-steps", type=int, default=5)
     args = ap.parse_args(argv)
     if args.impl == "reference":
         run_reference(args)
