@@ -173,14 +173,21 @@ def run_ours(args) -> None:
     lib = _lib.load()
     names = ("x", "a_u", "a_v", "a_o", "b_u", "b_v", "b_o", "gamma")
 
+    batch = args.batch
+    only = set(args.cases.split(",")) if args.cases else None
     cases = []
     for si, (h, w, c, d) in enumerate(SHAPES):
         for ri, (route, lvl) in enumerate(ROUTES):
-            tensors, dout = _make_case(h, w, c, d, BATCH, dev, seed=1 + 1000 * rank + 10 * si + ri)
+            if only is not None and f"{h}x{w}x{c}/{route}{lvl}" not in only:
+                continue
+            tensors, dout = _make_case(h, w, c, d, batch, dev, seed=1 + 1000 * rank + 10 * si + ri)
             plan = build_route_plan(h, w, c, G, d, route, lvl)
             leaves = {k: v.detach().requires_grad_(True) for k, v in tensors.items()}
             cases.append(dict(shape=(h, w, c, d), route=f"{route}{lvl}", plan=plan,
                               leaves=leaves, dout=dout))
+    if not cases:
+        raise SystemExit(f"--cases {args.cases!r} selects nothing")
+    sweep_flops = sum(3.0 * fwd_flops(batch, *cs["shape"]) for cs in cases)
 
     def one_case(cs, ev=None):
         if ev is not None:
@@ -224,7 +231,7 @@ def run_ours(args) -> None:
     if world > 1:
         torch.distributed.all_reduce(ms_t, op=torch.distributed.ReduceOp.MAX)
     ms_max = float(ms_t.item())
-    flops = step_flops(BATCH) * args.steps * world
+    flops = sweep_flops * args.steps * world
     value = flops / (ms_max * 1e-3) / 1e12
 
     # Per-call breakdown (fwd / bwd of each case) from the in-region events.
@@ -238,12 +245,12 @@ def run_ours(args) -> None:
     (h, w, c, d), route = dom_key
     dom_phase = "bwd" if dom_b >= dom_f else "fwd"
     dom_ms = max(dom_f, dom_b)
-    dom_flops = (2.0 if dom_phase == "bwd" else 1.0) * fwd_flops(BATCH, h, w, c, d)
+    dom_flops = (2.0 if dom_phase == "bwd" else 1.0) * fwd_flops(batch, h, w, c, d)
     peaks = _peaks()
     achieved = dom_flops / (dom_ms * 1e-3) / 1e12
 
     # --- end-to-end through the public API with host buffers -----------------
-    e2e = _e2e(args, cases, names, dev, world)
+    e2e = None if args.no_e2e else _e2e(args, cases, names, dev, world, sweep_flops)
     del cases
     torch.cuda.empty_cache()
 
@@ -272,13 +279,15 @@ def run_ours(args) -> None:
             "data": "synthetic (seeded N(0,1) inputs and upstream grads, default-init weights)",
             "config": {
                 "workload": "bigemm_sweep_fwd_bwd",
-                "batch_per_gpu": BATCH,
-                "global_batch": BATCH * world,
+                "batch_per_gpu": batch,
+                "global_batch": batch * world,
                 "shapes": [f"{h}x{w}x{c}/d{d}" for (h, w, c, d) in SHAPES],
                 "routes": [f"{r}{l}" for r, l in ROUTES],
+                "cases": sorted({f"{cs['shape'][0]}x{cs['shape'][1]}x{cs['shape'][2]}/{cs['route']}"
+                                 for cs in cases}) if only is not None else "all",
                 "parallelism": f"batch-shard x{world}",
                 "l2": "per-step working set ~1 GB > 126 MB L2 (inputs larger than L2)",
-                "flops_per_step_per_gpu": step_flops(BATCH),
+                "flops_per_step_per_gpu": sweep_flops,
             },
             "roofline": {
                 "bound": "tensor",
@@ -305,7 +314,7 @@ def run_ours(args) -> None:
         torch.distributed.destroy_process_group()
 
 
-def _e2e(args, cases, names, dev, world):
+def _e2e(args, cases, names, dev, world, sweep_flops):
     """Same metric through ``bigemm`` with pinned host inputs/outputs."""
     from omniwave_b200 import bigemm
 
@@ -348,7 +357,7 @@ def _e2e(args, cases, names, dev, world):
     ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
     if world > 1:
         torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
-    val = step_flops(BATCH) * steps * world / (float(ms.item()) * 1e-3) / 1e12
+    val = sweep_flops * steps * world / (float(ms.item()) * 1e-3) / 1e12
     return {"value": round(val, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d // steps,
             "d2h_bytes_per_step": d2h // steps}
 
@@ -547,6 +556,10 @@ def main(argv=None) -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-model", action="store_true", help="skip the OmniWeave-T measurements")
     ap.add_argument("--model-steps", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=BATCH, help="operator-sweep batch per GPU")
+    ap.add_argument("--cases", default="",
+                    help="comma-separated subset of the sweep, e.g. 56x56x128/local0 (profiling runs)")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     args = ap.parse_args(argv)
     if args.impl == "reference":
         run_reference(args)

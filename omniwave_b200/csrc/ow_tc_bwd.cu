@@ -14,18 +14,27 @@
 //
 // The weight gradients sum over every tile of a channel group; their f32
 // accumulators (3 x d x rd) do not fit one SM's 512 TMEM columns next to the
-// working set at d = 128, so one persistent launch runs three CTA roles that
-// each recompute the forward operands they need from x and dOut:
+// working set at d = 128, so the work runs as three CTA roles:
 //
 //   DGRAD  (any item)      U, V, dZ -> dU, dV -> dP_u, dP_v (TMEM)   -> dX, dA_u, dA_v
 //   UV(h)  (one group)     U, V, dZ on rd half h -> dU, dV -> TMEM += dU^T P_u, dV^T P_v
 //   O      (one group)     U, V -> Z -> A_o Z; TMEM Y += Z B_o, M_o += (A_o Z)^T G'  -> dA_o
 //
+// Every role needs the same per-item operands (P_u, P_v, dY', G', T).  A
+// pack kernel with many CTAs per SM gathers x and dOut through the route
+// tables once per item and writes those five operands as pre-swizzled
+// images; the persistent role kernel then streams them (and the weight
+// chunk images) into shared memory with bulk copies issued by one producer
+// warp, so its compute warps only run the per-chunk elementwise work and the
+// per-item epilogue while the tensor work of the next item proceeds.
+//
 // The UV and O weight-gradient products read the token-major tiles already
-// in shared memory through MN-major UMMA descriptors.  Each CTA writes f32
-// partials; a reduction kernel sums them in a fixed order (bitwise
-// reproducible).  Per-role thread layout is the forward's: 8 compute warps,
-// one MMA-issuing warp that owns TMEM, one warp streaming weight chunks.
+// in shared memory through MN-major UMMA descriptors; the DGRAD epilogue
+// reads dP straight out of TMEM in the mma.sync fragment layout
+// (tcgen05.ld 16x256b) for the 16x16 token-mix gradients.  Each CTA writes
+// f32 partials; a reduction kernel sums them in a fixed order (bitwise
+// reproducible).  Per-role thread layout: 8 compute warps, one MMA-issuing
+// warp that owns TMEM, one producer warp issuing the bulk copies.
 
 #include <algorithm>
 #include <type_traits>
@@ -62,11 +71,17 @@ struct BCfg {
   static constexpr int Z_BYTES = BM * NC * 2;   // 16 KB
   static constexpr int BU_BYTES = NC * D * 2;   // one weight sub-image
   static constexpr int IMG_BYTES = 6 * BU_BYTES;  // Bu | Bv | BoT | BuT | BvT | Bo
+  // Packed per-item operand images written by the pack kernel, each an SW128
+  // K-major [BM x D] image: P_u | P_v | dY' | G' | T.
+  static constexpr int PK_DY = 2, PK_G = 3, PK_T = 4;
+  static constexpr int ITEM_BYTES = 5 * P_BYTES;
   // Shared-memory plans (bytes).  Common: P_u at 0, P_v at P, X1 at 2P.
   static constexpr int OFF_PU = 0, OFF_PV = P_BYTES, OFF_X1 = 2 * P_BYTES;
-  // DGRAD
-  static constexpr int D_S = 3 * P_BYTES;                    // dU | dV (chunk)
-  static constexpr int D_W = D_S + 2 * Z_BYTES;              // 2 stages x (Bu | Bv | BoT)
+  static constexpr int ALIGN1K(int v) { return (v + 1023) / 1024 * 1024; }
+  // DGRAD: dU | dV of one chunk, reused for the T image in the epilogue.
+  static constexpr int D_S = 3 * P_BYTES;
+  static constexpr int D_SBYTES = 2 * Z_BYTES > P_BYTES ? 2 * Z_BYTES : P_BYTES;
+  static constexpr int D_W = D_S + D_SBYTES;                 // 2 stages x (Bu | Bv | BoT)
   static constexpr int D_END = D_W + 6 * BU_BYTES;
   // UV
   static constexpr int U_S = 3 * P_BYTES;                    // dU_h | dV_h (128 features each)
@@ -75,7 +90,8 @@ struct BCfg {
   // O
   static constexpr int O_Z = 3 * P_BYTES;
   static constexpr int O_ZO = O_Z + Z_BYTES;                 // pair of chunks (128 features)
-  static constexpr int O_W = O_ZO + 2 * Z_BYTES;             // Bu | Bv | Bo
+  static constexpr int O_STG = O_ZO + 2 * Z_BYTES;           // Y staging for dA_o
+  static constexpr int O_W = ALIGN1K(O_STG + STG_BYTES);     // Bu | Bv | Bo
   static constexpr int O_END = O_W + 3 * BU_BYTES;
   static constexpr int MAX_END = D_END > U_END ? (D_END > O_END ? D_END : O_END) : (U_END > O_END ? U_END : O_END);
   static constexpr int OFF_META = MAX_END;                   // row[BM], ch[D], cont
@@ -84,7 +100,6 @@ struct BCfg {
   static constexpr int BAR_BYTES = 16 * 8 + 16;
   static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024;
   static_assert(SMEM <= 232448, "shared memory budget");
-  static_assert(3 * STG_BYTES <= 3 * P_BYTES + 2 * Z_BYTES, "epilogue staging alias");
   // TMEM columns.
   static constexpr int T_U = 0, T_V = 64, T_DZ = 128;
   static constexpr int T_DPU = 256, T_DPV = 256 + D;          // DGRAD
@@ -97,13 +112,12 @@ struct BCfg {
 template <int D>
 struct BPlan {
   int nD, nUVq, nOq, nH, grid;
-  size_t img, amat, gg, nw, contig, pdA, pdAo, puv, po, mo, dxn, total;
+  size_t img, amat, gg, nw, contig, pdA, pdAo, puv, po, mo, dxn, packed, total;
   BPlan(const Prob& p, bool block, int sms) {
     using C = BCfg<D>;
     nH = C::NH;
-    // Split one wave of CTAs across the roles.  Every role gathers and mixes
-    // each of its items, so per-item time is similar across roles; weigh
-    // them by items to process (a UV half item has fewer chunks).
+    // Split one wave of CTAs across the roles, weighed by the work each
+    // role has per item (a UV half item has half the chunks).
     const double wD = 1.0, wU = (D == 64 ? 1.0 : 0.8) * nH, wO = 1.0, tot = wD + wU + wO;
     const int64_t nMB = (p.BQ() + 7) / 8;
     nUVq = std::max(1, (int)(sms * (wU / nH) / tot) / p.Qc);
@@ -126,6 +140,7 @@ struct BPlan {
     po = take((size_t)p.Qc * nOq * C::RD * D * 4);
     mo = take((size_t)p.Qc * C::RD * D * 4);
     dxn = block ? take((size_t)p.B * p.N * p.C * 4) : 0;
+    packed = take((size_t)p.Qc * nMB * C::ITEM_BYTES);
     total = o;
   }
 };
@@ -400,7 +415,7 @@ __device__ __forceinline__ void rows_store(const RowRegs<TS, NHF>& R, int h, int
 // written in SW128 K-major layout at channel offset hf*64.
 template <bool BF16>
 __device__ __forceinline__ void mix_half(uint32_t aStg, const uint32_t (&fa)[4], unsigned char* dst, int hf,
-                                         int warp, int lane) {
+                                         int warp, int lane, const float* colscale = nullptr) {
   const int g = lane >> 2, t4 = lane & 3;
 #pragma unroll
   for (int np = 0; np < 4; ++np) {
@@ -410,6 +425,11 @@ __device__ __forceinline__ void mix_half(uint32_t aStg, const uint32_t (&fa)[4],
     mma16816<BF16>(c0, fa, b0, b1);
     mma16816<BF16>(c1, fa, b2, b3);
     const int r0 = warp * 16 + g, k0 = hf * 64 + np * 16 + 2 * t4;
+    if (colscale) {
+      const float s0 = colscale[k0], s1 = colscale[k0 + 1], s2 = colscale[k0 + 8], s3 = colscale[k0 + 9];
+      c0[0] *= s0; c0[1] *= s1; c0[2] *= s0; c0[3] *= s1;
+      c1[0] *= s2; c1[1] *= s3; c1[2] *= s2; c1[3] *= s3;
+    }
     *reinterpret_cast<uint32_t*>(dst + sw128_off(r0, k0, BM)) = pack2<BF16>(c0[0], c0[1]);
     *reinterpret_cast<uint32_t*>(dst + sw128_off(r0 + 8, k0, BM)) = pack2<BF16>(c0[2], c0[3]);
     *reinterpret_cast<uint32_t*>(dst + sw128_off(r0, k0 + 8, BM)) = pack2<BF16>(c1[0], c1[1]);
@@ -452,6 +472,7 @@ struct BwdArgs {
   const float* nw;
   const int* contig;
   int vec_ok;
+  unsigned char* packed;  // [items][5][BM x D] SW128 operand images
   void* dx;       // operator mode: x dtype
   float* dxn;     // block mode
   float* pdA;     // [nD][8][2][256]
@@ -461,6 +482,118 @@ struct BwdArgs {
   int nD, nUVq, nOq, nH;
 };
 
+// ---------------------------------------------------------------------------
+// Pack kernel: gathers one M-block (128 token rows) of x (RMS-normalised in
+// block mode) and of dOut through the route tables and writes the operand
+// images the backward roles consume, once per item:
+//   P_u = A_u T, P_v = A_v T, dY' = A_o^T (G' gamma), G', T
+// (G' = mask * drop-path scale * dOut).  Many small CTAs per SM hide the
+// gather latency that a single persistent CTA could not.
+// ---------------------------------------------------------------------------
+template <int D, bool BF16, typename TX, typename TO>
+__global__ void __launch_bounds__(NCOMP) tc_pack_kernel(BwdArgs a) {
+  using C = BCfg<D>;
+  const Prob& p = a.p;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
+  unsigned char* stg = sm;
+  int* sRow = reinterpret_cast<int*>(sm + STG_BYTES);
+  int* sCh = sRow + BM;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int64_t BQ = (int64_t)p.B * p.Qs;
+  const int nMB = (int)((BQ + 7) / 8);
+  const int64_t item = blockIdx.x;
+  const int qc = (int)(item / nMB), mb = (int)(item - (int64_t)qc * nMB);
+  for (int r = tid; r < BM; r += NCOMP) {
+    const int64_t t = (int64_t)mb * 8 + (r >> 4);
+    int rw = -1;
+    if (t < BQ) {
+      const int b = (int)(t / p.Qs);
+      const int tok = p.tok[(t - (int64_t)b * p.Qs) * 16 + (r & 15)];
+      rw = tok < p.N ? b * p.N + tok : -1;
+    }
+    sRow[r] = rw;
+  }
+  for (int k = tid; k < D; k += NCOMP) sCh[k] = p.ch[qc * D + k];
+  __syncthreads();
+  GatherCtx gc{sRow, sCh, p.N, p.C, a.vec_ok && a.contig[qc] != 0};
+  const float* ggq = a.gg + (int64_t)qc * D;
+  unsigned char* out = a.packed + item * C::ITEM_BYTES;
+  const uint32_t aStg = smem_u32(stg);
+  const TX* x = (const TX*)a.x;
+  const TO* dout = (const TO*)a.dout;
+  // staging (row-major) -> SW128 image in global memory
+  auto copy_out = [&](unsigned char* img, int hf) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int unit = tid + u * NCOMP;
+      const int r = unit >> 3, cj = unit & 7;
+      const uint4 v = *reinterpret_cast<const uint4*>(stg + (r * STG_LD + cj * 8) * 2);
+      *reinterpret_cast<uint4*>(img + sw128_off(r, hf * 64 + cj * 8, BM)) = v;
+    }
+  };
+  for (int hf = 0; hf < D / 64; ++hf) {
+    if (gc.cont) {
+      RowRegs<TX, 1> rx;
+      RowRegs<TO, 1> rg;
+      rows_issue<TX, 1>(rx, gc, x, hf, a.rstd, nullptr, tid);
+      rows_issue<TO, 1>(rg, gc, dout, hf, nullptr, a.scale, tid);
+      rows_store<TX, 1, BF16>(rx, 0, hf, gc, stg, false, a.rstd != nullptr, a.nw, nullptr, a.x_dt, tid);
+      __syncthreads();
+      copy_out(out + C::PK_T * C::P_BYTES, hf);
+      {
+        uint32_t f[4];
+        load_afrag(a.amat, false, g, t4, f);
+        mix_half<BF16>(aStg, f, out, hf, warp, lane);
+        load_afrag(a.amat + 256, false, g, t4, f);
+        mix_half<BF16>(aStg, f, out + C::P_BYTES, hf, warp, lane);
+      }
+      __syncthreads();
+      rows_store<TO, 1, BF16>(rg, 0, hf, gc, stg, false, false, nullptr, nullptr, 0, tid);
+    } else {
+      gather_half<TX, BF16>(gc, x, hf, a.rstd, a.nw, a.x_dt, nullptr, nullptr, stg, false, tid);
+      __syncthreads();
+      copy_out(out + C::PK_T * C::P_BYTES, hf);
+      {
+        uint32_t f[4];
+        load_afrag(a.amat, false, g, t4, f);
+        mix_half<BF16>(aStg, f, out, hf, warp, lane);
+        load_afrag(a.amat + 256, false, g, t4, f);
+        mix_half<BF16>(aStg, f, out + C::P_BYTES, hf, warp, lane);
+      }
+      __syncthreads();
+      gather_half<TO, BF16>(gc, dout, hf, nullptr, nullptr, 0, a.scale, nullptr, stg, false, tid);
+    }
+    __syncthreads();
+    copy_out(out + C::PK_G * C::P_BYTES, hf);
+    {
+      uint32_t f[4];
+      load_afrag(a.amat + 512, true, g, t4, f);
+      mix_half<BF16>(aStg, f, out + C::PK_DY * C::P_BYTES, hf, warp, lane, ggq);
+    }
+    __syncthreads();
+  }
+}
+
+__device__ __forceinline__ void tmem_ld16x256_x2(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
+__device__ __forceinline__ uint32_t movm_trans(uint32_t v) {
+  uint32_t o;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(o) : "r"(v));
+  return o;
+}
+
+// ---------------------------------------------------------------------------
+// Role kernel (see the file header).  Operands of every item arrive from the
+// pack kernel through one bulk copy issued by the producer warp, so the
+// compute warps only run the chunk loop and the epilogue, and the next
+// item's tensor work overlaps the current epilogue.
+// ---------------------------------------------------------------------------
 template <int D, bool BF16, typename TX, typename TO>
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
   using C = BCfg<D>;
@@ -474,16 +607,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
   int* sCh = sRow + BM;
   volatile int* sCont = sCh + D;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
-  uint64_t* bar_p = bars + 0;
-  uint64_t* bar_a = bars + 1;
-  uint64_t* bar_du = bars + 2;
-  uint64_t* bar_b = bars + 3;
-  uint64_t* bar_w = bars + 4;
-  uint64_t* bar_zo = bars + 5;
-  uint64_t* bar_g1 = bars + 6;
-  uint64_t* bar_g2 = bars + 7;   // DGRAD: second weight stage
+  uint64_t* bar_p = bars + 0;    // item operands loaded (tx)
+  uint64_t* bar_a = bars + 1;    // U, V (, dZ) of a chunk done (commit)
+  uint64_t* bar_du = bars + 2;   // chunk's elementwise outputs written, TMEM working set read
+  uint64_t* bar_b = bars + 3;    // DGRAD: dP of a chunk done; O: Y of a chunk done
+  uint64_t* bar_w = bars + 4;    // UV: weight-gradient products of an item done; O: M_o pair done
+  uint64_t* bar_zo = bars + 5;   // O: A_o Z pair written
+  uint64_t* bar_g1 = bars + 6;   // weights (stage 0 / first group) loaded
+  uint64_t* bar_g2 = bars + 7;   // weights (stage 1 / second group) loaded
   uint64_t* bar_e0 = bars + 8;   // DGRAD: weight stage 0 free
   uint64_t* bar_e1 = bars + 9;   // DGRAD: weight stage 1 free
+  uint64_t* bar_pf = bars + 10;  // item operands no longer read (DGRAD, O)
+  uint64_t* bar_tf = bars + 11;  // DGRAD: last dP done (dU/dV region free for T)
+  uint64_t* bar_t = bars + 12;   // DGRAD: T image loaded
+  uint64_t* bar_epd = bars + 13; // epilogue done with TMEM accumulators (and G' for O)
+  uint64_t* bar_gl = bars + 14;  // O: G' loaded
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
 
@@ -492,7 +630,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
   const int nMB = (int)((BQ + 7) / 8);
 
   // ---- role of this CTA and its item range
-  int role, qc_fix = 0, h = 0, wslot = 0;
+  int role, h = 0, wslot = 0;
   int64_t it0 = 0, it_step = 1, n_items = 0;
   {
     const int b = blockIdx.x;
@@ -518,7 +656,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
         nq = a.nOq;
         wslot = local;
       }
-      qc_fix = local / nq;
+      const int qc_fix = local / nq;
       const int j = local % nq;
       const int64_t m0 = (int64_t)nMB * j / nq, m1 = (int64_t)nMB * (j + 1) / nq;
       it0 = (int64_t)qc_fix * nMB + m0;
@@ -528,9 +666,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
   }
   const int nchunks = role == R_UV ? C::NQH : C::NQ;
   const int q_base = role == R_UV ? h * C::NQH : 0;
+  const int nit = (int)n_items;
 
   if (threadIdx.x == 0) {
-    mbar_init(bar_p, NCOMP);
+    mbar_init(bar_p, 1);
     mbar_init(bar_a, 1);
     mbar_init(bar_du, NCOMP);
     mbar_init(bar_b, 1);
@@ -540,6 +679,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
     mbar_init(bar_g2, 1);
     mbar_init(bar_e0, 1);
     mbar_init(bar_e1, 1);
+    mbar_init(bar_pf, 1);
+    mbar_init(bar_tf, 1);
+    mbar_init(bar_t, 1);
+    mbar_init(bar_epd, NCOMP);
+    mbar_init(bar_gl, 1);
     *sAbort = 0;
     fence_mbar_init();
   }
@@ -549,57 +693,92 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
   tc_fence_after();
   const uint32_t tbase = *sTmem;
 
-  // Weight sub-image groups per role: g1 = first group (bytes from the chunk
-  // image start), g2 = second group.
-  int g1_off = 0, g1_bytes = 0, g2_off = 0, g2_bytes = 0;
-  unsigned char* sW = nullptr;
-  if (role == R_DGRAD) {
-    // Two stages of one group; dP reads B_u / B_v from the same images.
-    sW = sm + C::D_W; g1_off = 0; g1_bytes = 3 * C::BU_BYTES;
-  } else if (role == R_UV) {
-    sW = sm + C::U_W; g1_off = 0; g1_bytes = 3 * C::BU_BYTES;
-  } else {
-    sW = sm + C::O_W; g1_off = 0; g1_bytes = 2 * C::BU_BYTES; g2_off = 5 * C::BU_BYTES; g2_bytes = C::BU_BYTES;
-  }
-  unsigned char* sW2 = sW + g1_bytes;
-  const int total_chunks = (int)n_items * nchunks;
+  unsigned char* sW = sm + (role == R_DGRAD ? C::D_W : (role == R_UV ? C::U_W : C::O_W));
+  const int total_chunks = nit * nchunks;
+  auto item_of = [&](int it) { return it0 + (int64_t)it * it_step; };
   auto chunk_img = [&](int c) {
     const int it = c / nchunks, j = c - it * nchunks;
-    const int64_t item = it0 + (int64_t)it * it_step;
-    const int qc = (int)(item / nMB);
+    const int qc = (int)(item_of(it) / nMB);
     return a.img + ((int64_t)qc * C::NQ + q_base + j) * C::IMG_BYTES;
   };
+  auto item_src = [&](int it) { return a.packed + item_of(it) * C::ITEM_BYTES; };
 
   if (warp == PROD_WARP) {
-    // ------------------------------------------------ weight producer
-    if (lane == 0 && total_chunks > 0) {
-      auto load1 = [&](int c) {
-        mbar_arrive_expect_tx(bar_g1, g1_bytes);
-        bulk_g2s(sW, chunk_img(c) + g1_off, g1_bytes, bar_g1);
+    // ------------------------------------------------ producer (bulk copies)
+    if (lane == 0 && nit > 0) {
+      auto load_item = [&](int it) {
+        if (role == R_O) {
+          mbar_arrive_expect_tx(bar_p, 2 * C::P_BYTES);
+          bulk_g2s(sPu, item_src(it), 2 * C::P_BYTES, bar_p);
+        } else {
+          mbar_arrive_expect_tx(bar_p, 3 * C::P_BYTES);
+          bulk_g2s(sPu, item_src(it), 3 * C::P_BYTES, bar_p);
+        }
       };
-      auto load2 = [&](int c) {
-        mbar_arrive_expect_tx(bar_g2, g2_bytes);
-        bulk_g2s(sW2, chunk_img(c) + g2_off, g2_bytes, bar_g2);
+      auto load_g = [&](int it) {  // O: G' into X1
+        mbar_arrive_expect_tx(bar_gl, C::P_BYTES);
+        bulk_g2s(sX1, item_src(it) + C::PK_G * C::P_BYTES, C::P_BYTES, bar_gl);
+      };
+      auto load_t = [&](int it) {  // DGRAD: T into the dU/dV region
+        mbar_arrive_expect_tx(bar_t, C::P_BYTES);
+        bulk_g2s(sm + C::D_S, item_src(it) + C::PK_T * C::P_BYTES, C::P_BYTES, bar_t);
       };
       if (role == R_DGRAD) {
-        auto loadst = [&](int c) {
+        auto load_w = [&](int c) {
           uint64_t* bar = (c & 1) ? bar_g2 : bar_g1;
-          mbar_arrive_expect_tx(bar, g1_bytes);
-          bulk_g2s(sW + (c & 1) * g1_bytes, chunk_img(c), g1_bytes, bar);
+          mbar_arrive_expect_tx(bar, 3 * C::BU_BYTES);
+          bulk_g2s(sW + (c & 1) * 3 * C::BU_BYTES, chunk_img(c), 3 * C::BU_BYTES, bar);
         };
-        loadst(0);
-        if (total_chunks > 1) loadst(1);
-        for (int c = 0; c + 2 < total_chunks; ++c) {
-          if (mbar_wait((c & 1) ? bar_e1 : bar_e0, (c >> 1) & 1, sAbort)) loadst(c + 2);
-          if (*sAbort) break;
+        load_item(0);
+        load_w(0);
+        if (total_chunks > 1) load_w(1);
+        for (int it = 0; it < nit && !*sAbort; ++it) {
+          for (int j = 0; j < nchunks; ++j) {
+            const int c = it * nchunks + j;
+            if (j == nchunks - 1 && it + 1 < nit && mbar_wait(bar_pf, it & 1, sAbort)) load_item(it + 1);
+            if (c + 2 < total_chunks && mbar_wait((c & 1) ? bar_e1 : bar_e0, (c >> 1) & 1, sAbort)) load_w(c + 2);
+          }
+          if (mbar_wait(bar_tf, it & 1, sAbort)) load_t(it);
+        }
+      } else if (role == R_UV) {
+        auto load_w = [&](int c) {
+          mbar_arrive_expect_tx(bar_g1, 3 * C::BU_BYTES);
+          bulk_g2s(sW, chunk_img(c), 3 * C::BU_BYTES, bar_g1);
+        };
+        load_item(0);
+        load_w(0);
+        for (int it = 0; it < nit && !*sAbort; ++it) {
+          for (int j = 0; j < nchunks; ++j) {
+            const int c = it * nchunks + j;
+            if (c + 1 < total_chunks && mbar_wait(bar_a, c & 1, sAbort)) load_w(c + 1);
+          }
+          if (it + 1 < nit && mbar_wait(bar_w, it & 1, sAbort)) load_item(it + 1);
         }
       } else {
-        load1(0);
-        if (g2_bytes) load2(0);
-        for (int c = 0; c + 1 < total_chunks; ++c) {
-          if (mbar_wait(bar_a, c & 1, sAbort)) load1(c + 1);
-          if (g2_bytes && mbar_wait(bar_b, c & 1, sAbort)) load2(c + 1);
-          if (*sAbort) break;
+        auto load_w1 = [&](int c) {
+          mbar_arrive_expect_tx(bar_g1, 2 * C::BU_BYTES);
+          bulk_g2s(sW, chunk_img(c), 2 * C::BU_BYTES, bar_g1);
+        };
+        auto load_w2 = [&](int c) {
+          mbar_arrive_expect_tx(bar_g2, C::BU_BYTES);
+          bulk_g2s(sW + 2 * C::BU_BYTES, chunk_img(c) + 5 * C::BU_BYTES, C::BU_BYTES, bar_g2);
+        };
+        load_item(0);
+        load_g(0);
+        load_w1(0);
+        load_w2(0);
+        for (int it = 0; it < nit && !*sAbort; ++it) {
+          for (int j = 0; j < nchunks; ++j) {
+            const int c = it * nchunks + j;
+            if (c + 1 < total_chunks) {
+              if (mbar_wait(bar_a, c & 1, sAbort)) load_w1(c + 1);
+              if (mbar_wait(bar_b, c & 1, sAbort)) load_w2(c + 1);
+            }
+          }
+          if (it + 1 < nit) {
+            if (mbar_wait(bar_pf, it & 1, sAbort)) load_item(it + 1);
+            if (mbar_wait(bar_epd, it & 1, sAbort)) load_g(it + 1);
+          }
         }
       }
     }
@@ -624,7 +803,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
                    ID_MN, (acc0 || kk > 0) ? 1u : 0u);
       };
       int c = 0, pc = 0;
-      for (int it = 0; it < (int)n_items; ++it) {
+      for (int it = 0; it < nit; ++it) {
         mbar_wait(bar_p, it & 1, sAbort);
         tc_fence_after();
         for (int j = 0; j < nchunks; ++j, ++c) {
@@ -642,12 +821,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
             if (role != R_O) kmma(C::T_DZ, aX1, BM, aWc + 2 * C::BU_BYTES, NC, D / 16, ID_N64, false);
           }
           umma_commit(bar_a);
+          if (j == nchunks - 1 && role == R_DGRAD) umma_commit(bar_pf);
           mbar_wait(bar_du, c & 1, sAbort);
           tc_fence_after();
           if (role == R_DGRAD) {
+            if (j == 0 && it > 0) {  // previous epilogue has read dP out of TMEM
+              mbar_wait(bar_epd, (it - 1) & 1, sAbort);
+              tc_fence_after();
+            }
             if (!*sAbort) {
-              // dP_u += dU_q B_u[:, q]^T: B is the B_u chunk image read MN-major
-              // (N = channels in 64-wide atoms NC*128 bytes apart, K = features).
+              // dP += dU_q B_u[:, q]^T with B_u's chunk image read MN-major.
               const uint32_t aS = smem_u32(sm + C::D_S);
               for (int kk = 0; kk < NC / 16; ++kk) {
                 umma_f16(tbase + C::T_DPU, sdesc_sw128(sw128_kstep(aS, kk, BM)),
@@ -659,19 +842,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
             }
             umma_commit(bar_b);
             umma_commit((c & 1) ? bar_e1 : bar_e0);
+            if (j == nchunks - 1) umma_commit(bar_tf);
           } else if (role == R_O) {
             mbar_wait(bar_g2, c & 1, sAbort);
+            if (j == 0 && it > 0) mbar_wait(bar_epd, (it - 1) & 1, sAbort);  // Y read out
             tc_fence_after();
-            if (!*sAbort) kmma(C::T_Y, smem_u32(sm + C::O_Z), BM, smem_u32(sW2), D, NC / 16, ID_ND, j > 0);
+            if (!*sAbort) kmma(C::T_Y, smem_u32(sm + C::O_Z), BM, aW + 2 * C::BU_BYTES, D, NC / 16, ID_ND, j > 0);
             umma_commit(bar_b);
             if (j & 1) {
+              if (j == 1) mbar_wait(bar_gl, it & 1, sAbort);
               mbar_wait(bar_zo, pc & 1, sAbort);
               tc_fence_after();
-              if (!*sAbort)
-                mnmma(C::T_ACCO + (j >> 1) * D, smem_u32(sm + C::O_ZO), aX1, it > 0);
+              if (!*sAbort) mnmma(C::T_ACCO + (j >> 1) * D, smem_u32(sm + C::O_ZO), aX1, it > 0);
               umma_commit(bar_w);
               ++pc;
             }
+            if (j == nchunks - 1) umma_commit(bar_pf);
           }
         }
         if (role == R_UV) {
@@ -691,20 +877,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
     const int lq = warp & 3, cb = (warp >> 2) * 32;
     const int r = lq * 32 + lane;
     const uint32_t trow = tbase + ((uint32_t)(lq * 32) << 16);
-    // Token-mix fragments are (re)loaded right before each use (L1-resident)
-    // to keep them out of the long-lived register set.
     auto frag = [&](int m, bool tr, uint32_t (&f)[4]) { load_afrag(a.amat + m * 256, tr, g, t4, f); };
     float accA[2][2][4] = {};  // DGRAD: dA_u, dA_v ; O: dA_o in accA[0]
-    const TX* x = (const TX*)a.x;
-    const TO* dout = (const TO*)a.dout;
     int c = 0, pc = 0;
-    unsigned char* stg_a = role == R_O ? sm + C::O_Z : sm + C::D_S;  // phase-A staging
-    // Metadata of an item (packed row b*N+token per M-block row, channel per
-    // group column, contiguity flag), loaded into registers one item ahead.
+    // DGRAD epilogue metadata, loaded into registers one item ahead.
     struct MetaReg { int row, ch, cont; };
     auto meta_issue = [&](int it) {
       MetaReg m{-1, 0, 0};
-      const int64_t item = it0 + (int64_t)it * it_step;
+      const int64_t item = item_of(it);
       const int qc = (int)(item / nMB), mb = (int)(item - (int64_t)qc * nMB);
       if (tid < BM) {
         const int64_t t = (int64_t)mb * 8 + (tid >> 4);
@@ -719,98 +899,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
       return m;
     };
     MetaReg mreg{-1, 0, 0};
-    if (n_items > 0) mreg = meta_issue(0);
-    for (int it = 0; it < (int)n_items; ++it) {
-      const int64_t item = it0 + (int64_t)it * it_step;
+    if (role == R_DGRAD && nit > 0) mreg = meta_issue(0);
+    for (int it = 0; it < nit; ++it) {
+      const int64_t item = item_of(it);
       const int qc = (int)(item / nMB);
       const float* ggq = a.gg + (int64_t)qc * D;
-      // UV: the previous item's weight-gradient products read P and dU/dV.
-      if (role == R_UV && it > 0) {
-        mbar_wait(bar_w, (it - 1) & 1, sAbort);
-        __syncwarp();
-      }
-      if (role == R_O && it > 0) {
-        mbar_wait(bar_w, (pc - 1) & 1, sAbort);
-        __syncwarp();
-      }
-      comp_sync();  // previous item is done with metadata and staging
-      if (tid < BM) sRow[tid] = mreg.row;
-      if (tid < D) sCh[tid] = mreg.ch;
-      if (tid == 0) *sCont = mreg.cont;
-      comp_sync();
-      if (it + 1 < (int)n_items) mreg = meta_issue(it + 1);
-      GatherCtx gc{sRow, sCh, p.N, p.C, *sCont != 0};
-      // ---- phase A: P_u, P_v from x; dY' (or G') from dOut
-      const uint32_t aStg = smem_u32(stg_a);
-      const bool xnorm = a.rstd != nullptr;
-      if (gc.cont) {
-        constexpr int NHF = D / 64;
-        constexpr bool both16 = sizeof(TX) == 2 && sizeof(TO) == 2;
-        RowRegs<TX, NHF> rx;
-        RowRegs<TO, NHF> rg;
-        rows_issue<TX, NHF>(rx, gc, x, 0, a.rstd, nullptr, tid);
-        if constexpr (both16) rows_issue<TO, NHF>(rg, gc, dout, 0, nullptr, a.scale, tid);
-#pragma unroll
-        for (int hf = 0; hf < NHF; ++hf) {
-          rows_store<TX, NHF, BF16>(rx, hf, hf, gc, stg_a, false, xnorm, a.nw, nullptr, a.x_dt, tid);
-          comp_sync();
-          __syncwarp();
-          {
-            uint32_t f[4];
-            frag(0, false, f);
-            mix_half<BF16>(aStg, f, sPu, hf, warp, lane);
-            frag(1, false, f);
-            mix_half<BF16>(aStg, f, sPv, hf, warp, lane);
-          }
-          comp_sync();
-        }
-        if constexpr (!both16) rows_issue<TO, NHF>(rg, gc, dout, 0, nullptr, a.scale, tid);
-#pragma unroll
-        for (int hf = 0; hf < NHF; ++hf) {
-          if (role == R_O) {
-            rows_store<TO, NHF, BF16>(rg, hf, hf, gc, sX1, true, false, nullptr, nullptr, 0, tid);
-          } else {
-            rows_store<TO, NHF, BF16>(rg, hf, hf, gc, stg_a, false, false, nullptr, ggq, 0, tid);
-            comp_sync();
-            __syncwarp();
-            {
-              uint32_t f[4];
-              frag(2, true, f);
-              mix_half<BF16>(aStg, f, sX1, hf, warp, lane);
-            }
-            comp_sync();
-          }
-        }
-      } else {
-        for (int hf = 0; hf < D / 64; ++hf) {
-          gather_half<TX, BF16>(gc, x, hf, a.rstd, a.nw, a.x_dt, nullptr, nullptr, stg_a, false, tid);
-          comp_sync();
-          __syncwarp();
-          {
-            uint32_t f[4];
-            frag(0, false, f);
-            mix_half<BF16>(aStg, f, sPu, hf, warp, lane);
-            frag(1, false, f);
-            mix_half<BF16>(aStg, f, sPv, hf, warp, lane);
-          }
-          comp_sync();
-          if (role == R_O) {
-            gather_half<TO, BF16>(gc, dout, hf, nullptr, nullptr, 0, a.scale, nullptr, sX1, true, tid);
-          } else {
-            gather_half<TO, BF16>(gc, dout, hf, nullptr, nullptr, 0, a.scale, ggq, stg_a, false, tid);
-            comp_sync();
-            __syncwarp();
-            {
-              uint32_t f[4];
-              frag(2, true, f);
-              mix_half<BF16>(aStg, f, sX1, hf, warp, lane);
-            }
-            comp_sync();
-          }
-        }
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(bar_p);
 
       // ---- chunk loop
       for (int j = 0; j < nchunks; ++j, ++c) {
@@ -847,6 +940,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
             *reinterpret_cast<uint4*>(sdu + C::Z_BYTES + off) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
           }
         } else if (role == R_UV) {
+          if (j == 0 && it > 0) mbar_wait(bar_w, (it - 1) & 1, sAbort);  // previous products read dU/dV
           unsigned char* sdu = sm + C::U_S;
 #pragma unroll
           for (int jj = 0; jj < 4; ++jj) {
@@ -895,14 +989,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           __syncwarp();
           const unsigned char* sz = sm + C::O_Z;
           unsigned char* szo = sm + C::O_ZO;
+          uint32_t fAo[4];
+          frag(2, false, fAo);
 #pragma unroll
           for (int np = 0; np < 4; ++np) {
             const int rowr = warp * 16 + (lane & 15), colr = np * 16 + (lane >> 4) * 8;
             uint32_t b0, b1, b2, b3;
             ldsm_x4_trans(smem_u32(sz + sw128_off(rowr, colr, BM)), b0, b1, b2, b3);
             float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
-            uint32_t fAo[4];
-            frag(2, false, fAo);
             mma16816<BF16>(c0, fAo, b0, b1);
             mma16816<BF16>(c1, fAo, b2, b3);
             const int r0 = warp * 16 + g, k0 = (j & 1) * 64 + np * 16 + 2 * t4;
@@ -922,72 +1016,70 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
 
       // ---- per-item epilogue
       if (role == R_DGRAD) {
-        mbar_wait(bar_b, (c - 1) & 1, sAbort);
+        // Metadata of this item for the dX scatter.
+        if (tid < BM) sRow[tid] = mreg.row;
+        if (tid < D) sCh[tid] = mreg.ch;
+        if (tid == 0) *sCont = mreg.cont;
+        comp_sync();
+        if (it + 1 < nit) mreg = meta_issue(it + 1);
+        const bool cont = *sCont != 0;
+        mbar_wait(bar_b, (c - 1) & 1, sAbort);  // last dP done
+        mbar_wait(bar_t, it & 1, sAbort);       // T image of this item loaded
         __syncwarp();
         tc_fence_after();
-        unsigned char* stA = sm;                  // dP_u half
-        unsigned char* stB = sm + STG_BYTES;      // dP_v half
-        unsigned char* stC = sm + 2 * STG_BYTES;  // T half
-        const uint32_t aA = smem_u32(stA), aB = smem_u32(stB), aC = smem_u32(stC);
-        for (int hf = 0; hf < D / 64; ++hf) {
-          // Start the re-gather of T (for dA_u, dA_v) before the TMEM reads.
-          RowRegs<TX, 1> rt;
-          if (gc.cont) rows_issue<TX, 1>(rt, gc, x, hf, a.rstd, nullptr, tid);
-          uint32_t pr[32], qr[32];
-          tmem_ld32(trow + C::T_DPU + hf * 64 + cb, pr);
-          tmem_ld32(trow + C::T_DPV + hf * 64 + cb, qr);
-          tmem_ld_wait();
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
-            uint4 w1, w2;
-            w1.x = pack2<BF16>(__uint_as_float(pr[jj * 8 + 0]), __uint_as_float(pr[jj * 8 + 1]));
-            w1.y = pack2<BF16>(__uint_as_float(pr[jj * 8 + 2]), __uint_as_float(pr[jj * 8 + 3]));
-            w1.z = pack2<BF16>(__uint_as_float(pr[jj * 8 + 4]), __uint_as_float(pr[jj * 8 + 5]));
-            w1.w = pack2<BF16>(__uint_as_float(pr[jj * 8 + 6]), __uint_as_float(pr[jj * 8 + 7]));
-            w2.x = pack2<BF16>(__uint_as_float(qr[jj * 8 + 0]), __uint_as_float(qr[jj * 8 + 1]));
-            w2.y = pack2<BF16>(__uint_as_float(qr[jj * 8 + 2]), __uint_as_float(qr[jj * 8 + 3]));
-            w2.z = pack2<BF16>(__uint_as_float(qr[jj * 8 + 4]), __uint_as_float(qr[jj * 8 + 5]));
-            w2.w = pack2<BF16>(__uint_as_float(qr[jj * 8 + 6]), __uint_as_float(qr[jj * 8 + 7]));
-            *reinterpret_cast<uint4*>(stA + (r * STG_LD + cb + jj * 8) * 2) = w1;
-            *reinterpret_cast<uint4*>(stB + (r * STG_LD + cb + jj * 8) * 2) = w2;
-          }
-          if (gc.cont) rows_store<TX, 1, BF16>(rt, 0, hf, gc, stC, false, xnorm, a.nw, nullptr, a.x_dt, tid);
-          else gather_half<TX, BF16>(gc, x, hf, a.rstd, a.nw, a.x_dt, nullptr, nullptr, stC, false, tid);
-          comp_sync();
-          __syncwarp();
-          // dA_u += dP_u T^T, dA_v += dP_v T^T (tile ``warp``)
-          auto rowA = [&](int rr, int k) { return aA + ((warp * 16 + rr) * STG_LD + k) * 2; };
-          auto rowB = [&](int rr, int k) { return aB + ((warp * 16 + rr) * STG_LD + k) * 2; };
-          auto rowC = [&](int rr, int k) { return aC + ((warp * 16 + rr) * STG_LD + k) * 2; };
-          gram16<BF16>(accA[0], rowA, rowC, lane);
-          gram16<BF16>(accA[1], rowB, rowC, lane);
-          // dT = A_u^T dP_u + A_v^T dP_v, scattered to dX / dxn
-          const int row0 = warp * 16 + g;
-          const int rwA = sRow[row0], rwB = sRow[row0 + 8];
-#pragma unroll
-          for (int np = 0; np < 4; ++np) {
-            __syncwarp();
-            uint32_t b0, b1, b2, b3, e0, e1, e2, e3;
-            ldsm_x4_trans(aA + ((warp * 16 + (lane & 15)) * STG_LD + np * 16 + (lane >> 4) * 8) * 2, b0, b1, b2, b3);
-            ldsm_x4_trans(aB + ((warp * 16 + (lane & 15)) * STG_LD + np * 16 + (lane >> 4) * 8) * 2, e0, e1, e2, e3);
-            float cc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-            uint32_t fT[4];
-            frag(0, true, fT);
-            mma16816<BF16>(cc[0], fT, b0, b1);
-            mma16816<BF16>(cc[1], fT, b2, b3);
-            frag(1, true, fT);
-            mma16816<BF16>(cc[0], fT, e0, e1);
-            mma16816<BF16>(cc[1], fT, e2, e3);
+        // Warp (lq, hw): tiles 2lq, 2lq+1 (TMEM lanes 32lq..32lq+31), channels
+        // [hw*D/2, (hw+1)*D/2).  dP arrives in the mma C-fragment layout.
+        const int hw = warp >> 2;
+        const uint32_t aT = smem_u32(sm + C::D_S);
+        uint32_t fuT[4], fvT[4];
+        frag(0, true, fuT);
+        frag(1, true, fvT);
+#pragma unroll 1
+        for (int tl = 0; tl < 2; ++tl) {
+          const int tile = 2 * lq + tl;
+          const int rwA = sRow[tile * 16 + g], rwB = sRow[tile * 16 + g + 8];
+          const uint32_t tl_addr = tbase + ((uint32_t)(tile * 16) << 16);
+#pragma unroll 1
+          for (int np = 0; np < D / 32; ++np) {
+            const int k0 = hw * (D / 2) + np * 16;
+            uint32_t pu[8], pv[8];
+            tmem_ld16x256_x2(tl_addr + C::T_DPU + k0, pu);
+            tmem_ld16x256_x2(tl_addr + C::T_DPV + k0, pv);
+            tmem_ld_wait();
+            // A fragments (rows = tokens, k = channels k0..k0+15) of dP_u, dP_v
+            uint32_t au[4], av[4];
+            au[0] = pack2<BF16>(__uint_as_float(pu[0]), __uint_as_float(pu[1]));
+            au[1] = pack2<BF16>(__uint_as_float(pu[2]), __uint_as_float(pu[3]));
+            au[2] = pack2<BF16>(__uint_as_float(pu[4]), __uint_as_float(pu[5]));
+            au[3] = pack2<BF16>(__uint_as_float(pu[6]), __uint_as_float(pu[7]));
+            av[0] = pack2<BF16>(__uint_as_float(pv[0]), __uint_as_float(pv[1]));
+            av[1] = pack2<BF16>(__uint_as_float(pv[2]), __uint_as_float(pv[3]));
+            av[2] = pack2<BF16>(__uint_as_float(pv[4]), __uint_as_float(pv[5]));
+            av[3] = pack2<BF16>(__uint_as_float(pv[6]), __uint_as_float(pv[7]));
+            // dA += dP T^T : B[k = channel][n = token j] = T[j][k] (T image, SW128)
+            uint32_t tb[4];
+            ldsm_x4(aT + sw128_off(tile * 16 + (lane & 7) + (lane >> 4) * 8, k0 + ((lane >> 3) & 1) * 8, BM),
+                    tb[0], tb[1], tb[2], tb[3]);
+            mma16816<BF16>(accA[0][0], au, tb[0], tb[1]);
+            mma16816<BF16>(accA[0][1], au, tb[2], tb[3]);
+            mma16816<BF16>(accA[1][0], av, tb[0], tb[1]);
+            mma16816<BF16>(accA[1][1], av, tb[2], tb[3]);
+            // dT = A_u^T dP_u + A_v^T dP_v : B fragments = transposed 8x8 blocks
 #pragma unroll
             for (int nb = 0; nb < 2; ++nb) {
-              const int k = hf * 64 + np * 16 + nb * 8 + 2 * t4;
+              const uint32_t bu0 = movm_trans(au[2 * nb]), bu1 = movm_trans(au[2 * nb + 1]);
+              const uint32_t bv0 = movm_trans(av[2 * nb]), bv1 = movm_trans(av[2 * nb + 1]);
+              float cc[4] = {0.f, 0.f, 0.f, 0.f};
+              mma16816<BF16>(cc, fuT, bu0, bu1);
+              mma16816<BF16>(cc, fvT, bv0, bv1);
+              const int k = k0 + nb * 8 + 2 * t4;
 #pragma unroll
               for (int hr = 0; hr < 2; ++hr) {
                 const int rw = hr ? rwB : rwA;
                 if (rw < 0) continue;
                 const int64_t row = rw;
-                const float d0 = cc[nb][2 * hr], d1 = cc[nb][2 * hr + 1];
-                if (gc.cont) {
+                const float d0 = cc[2 * hr], d1 = cc[2 * hr + 1];
+                if (cont) {
                   const int64_t off = row * p.C + sCh[0] + k;
                   if (a.dxn) {
                     *reinterpret_cast<float2*>(a.dxn + off) = make_float2(d0, d1);
@@ -1010,15 +1102,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
               }
             }
           }
-          comp_sync();
         }
         tc_fence_before();
+        mbar_arrive(bar_epd);
+        comp_sync();  // T (in the dU/dV region) and the metadata are read out
       } else if (role == R_O) {
         mbar_wait(bar_b, (c - 1) & 1, sAbort);   // Y complete
-        mbar_wait(bar_w, (pc - 1) & 1, sAbort);  // M_o done with the pair buffer
+        mbar_wait(bar_gl, it & 1, sAbort);      // G' of this item present
         __syncwarp();
         tc_fence_after();
-        unsigned char* stY = sm + C::O_Z;
+        unsigned char* stY = sm + C::O_STG;
         const uint32_t aY = smem_u32(stY), aG = smem_u32(sX1);
         for (int hf = 0; hf < D / 64; ++hf) {
           uint32_t yr[32];
@@ -1042,6 +1135,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           comp_sync();
         }
         tc_fence_before();
+        mbar_arrive(bar_epd);
       }
     }
 
@@ -1059,7 +1153,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           dst[m * 256 + (g + 8) * 16 + col + 1] = accA[m][nb][3];
         }
     } else if (n_items > 0) {
-      if (role == R_UV) mbar_wait(bar_w, ((int)n_items - 1) & 1, sAbort);
+      if (role == R_UV) mbar_wait(bar_w, (nit - 1) & 1, sAbort);
+      else mbar_wait(bar_w, (pc - 1) & 1, sAbort);
       __syncwarp();
       tc_fence_after();
       if (role == R_UV) {
@@ -1100,7 +1195,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
       }
       tc_fence_before();
     } else if (role == R_O) {
-      // No items: zero partials so the reduction stays well defined.
       float* da = a.pdAo + ((int64_t)wslot * NCOMP_WARPS + warp) * 256;
       for (int i = lane; i < 256; i += 32) da[i] = 0.f;
       float* dst = a.po + (int64_t)wslot * C::RD * D;
@@ -1238,6 +1332,7 @@ int tc_backward_t(const ow_bigemm_args_t* ar, const ow_bigemm_grads_t* gr, const
   a.pdAo = (float*)(base + pl.pdAo);
   a.puv = (float*)(base + pl.puv);
   a.po = (float*)(base + pl.po);
+  a.packed = base + pl.packed;
   a.nD = pl.nD;
   a.nUVq = pl.nUVq;
   a.nOq = pl.nOq;
@@ -1268,6 +1363,12 @@ int tc_backward_t(const ow_bigemm_args_t* ar, const ow_bigemm_grads_t* gr, const
   auto go = [&](auto* tx, auto* to) -> int {
     using TX = std::remove_pointer_t<decltype(tx)>;
     using TO = std::remove_pointer_t<decltype(to)>;
+    const int64_t items = (int64_t)p.Qc * ((p.BQ() + 7) / 8);
+    if (items > 0) {
+      constexpr int pack_smem = STG_BYTES + (BM + D) * 4 + 128;
+      launch(tc_pack_kernel<D, BF16, TX, TO>, (int)items, NCOMP, pack_smem, st, a);
+      OW_CHECK_LAUNCH("tc_pack_kernel");
+    }
     auto kern = tc_bwd_kernel<D, BF16, TX, TO>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, BCfg<D>::SMEM);
     if (e != cudaSuccess) {
