@@ -34,6 +34,7 @@ lr 1e-3 wd 0.05).  Images/s are whole-job totals over max-over-ranks time.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import math
 import os
@@ -60,6 +61,27 @@ def fwd_flops(b: int, h: int, w: int, c: int, d: int) -> float:
     qc = math.ceil(c / d)
     rd = 2 * d
     return float(b * qs * qc * (4 * G * G * d + 2 * G * G * rd + 6 * G * d * rd))
+
+
+def _kernel_flops(name: str, b: int, h: int, w: int, c: int, d: int) -> float:
+    """Algorithmic FLOPs one launch of ``name`` accounts for.  The backward's
+    algorithmic work (2x forward) is split between the pack kernel, which
+    does the three 16x16 token mixes of the operands (P_u, P_v, dY'), and the
+    role kernel, which does everything else."""
+    tiles = b * math.ceil(h * w / G) * math.ceil(c / d)
+    mixes = tiles * 3 * 2 * G * G * d
+    if name == "tc_fwd_kernel":
+        return fwd_flops(b, h, w, c, d)
+    if name == "tc_pack_kernel":
+        return float(mixes)
+    return 2.0 * fwd_flops(b, h, w, c, d) - mixes
+
+
+# DRAM bytes (read + write) per launch from the committed ncu captures,
+# keyed by (kernel, case, batch): value and the profile summary it comes from.
+_TRAFFIC = {
+    ("tc_bwd_kernel", "56x56x128/local0", 128): (854.8e6, "profiles/tc_bwd_kernel_56x56x128_local0.md"),
+}
 
 
 def fwd_bytes(b, h, w, c, elem=2) -> float:
@@ -188,9 +210,15 @@ def run_ours(args) -> None:
     if not cases:
         raise SystemExit(f"--cases {args.cases!r} selects nothing")
     sweep_flops = sum(3.0 * fwd_flops(batch, *cs["shape"]) for cs in cases)
+    case_names = sorted(f"{cs['shape'][0]}x{cs['shape'][1]}x{cs['shape'][2]}/{cs['route']}" for cs in cases)
 
     def one_case(cs, ev=None):
+        # ev: call boundaries [0..2] and, through ow_profile_events, the
+        # forward kernel [3, 4], the pack kernel [5, 6] and the backward role
+        # kernel [7, 8] on the same stream.
         if ev is not None:
+            for k, i in ((0, 3), (1, 5), (2, 7)):
+                lib.ow_profile_events(k, ctypes.c_void_p(ev[i].cuda_event), ctypes.c_void_p(ev[i + 1].cuda_event))
             ev[0].record()
         out = bigemm(plan=cs["plan"], backend="cuda", **cs["leaves"])
         if ev is not None:
@@ -198,6 +226,8 @@ def run_ours(args) -> None:
         grads = torch.autograd.grad(out, [cs["leaves"][k] for k in names], cs["dout"])
         if ev is not None:
             ev[2].record()
+            for k in range(3):
+                lib.ow_profile_events(k, None, None)
         return out, grads
 
     def step(evs=None):
@@ -209,8 +239,10 @@ def run_ours(args) -> None:
     torch.cuda.synchronize()
 
     # --- device-timed region -------------------------------------------------
-    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in cases]
+    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(9)] for _ in cases]
            for _ in range(args.steps)]
+    for e in (e for st in evs for ce in st for e in ce):
+        e.record()  # torch creates the CUDA event on first record; the library needs the handle
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     if world > 1:
@@ -234,20 +266,24 @@ def run_ours(args) -> None:
     flops = sweep_flops * args.steps * world
     value = flops / (ms_max * 1e-3) / 1e12
 
-    # Per-call breakdown (fwd / bwd of each case) from the in-region events.
-    per = {}
+    # Per-call breakdown (fwd / bwd of each case) and per-kernel launch times
+    # from the in-region events.
+    def mean_ms(i, a, b):
+        return statistics.mean(evs[s][i][a].elapsed_time(evs[s][i][b]) for s in range(args.steps))
+
+    per, kern = {}, {}
     for i, cs in enumerate(cases):
-        f = statistics.mean(evs[s][i][0].elapsed_time(evs[s][i][1]) for s in range(args.steps))
-        b = statistics.mean(evs[s][i][1].elapsed_time(evs[s][i][2]) for s in range(args.steps))
-        per[(cs["shape"], cs["route"])] = (f, b)
-    # Dominant call: the largest total time.
-    dom_key, (dom_f, dom_b) = max(per.items(), key=lambda kv: kv[1][0] + kv[1][1])
+        per[(cs["shape"], cs["route"])] = (mean_ms(i, 0, 1), mean_ms(i, 1, 2))
+        kern[(cs["shape"], cs["route"])] = {"tc_fwd_kernel": mean_ms(i, 3, 4), "tc_pack_kernel": mean_ms(i, 5, 6),
+                                            "tc_bwd_kernel": mean_ms(i, 7, 8)}
+    # Dominant kernel: the single launch with the largest device time.
+    dom_key, dom_name, dom_ms = max(((k, n, t) for k, v in kern.items() for n, t in v.items()),
+                                    key=lambda x: x[2])
     (h, w, c, d), route = dom_key
-    dom_phase = "bwd" if dom_b >= dom_f else "fwd"
-    dom_ms = max(dom_f, dom_b)
-    dom_flops = (2.0 if dom_phase == "bwd" else 1.0) * fwd_flops(batch, h, w, c, d)
+    dom_flops = _kernel_flops(dom_name, batch, h, w, c, d)
     peaks = _peaks()
     achieved = dom_flops / (dom_ms * 1e-3) / 1e12
+    traffic = _TRAFFIC.get((dom_name, f"{h}x{w}x{c}/{route}", batch))
 
     # --- end-to-end through the public API with host buffers -----------------
     e2e = None if args.no_e2e else _e2e(args, cases, names, dev, world, sweep_flops)
@@ -283,24 +319,28 @@ def run_ours(args) -> None:
                 "global_batch": batch * world,
                 "shapes": [f"{h}x{w}x{c}/d{d}" for (h, w, c, d) in SHAPES],
                 "routes": [f"{r}{l}" for r, l in ROUTES],
-                "cases": sorted({f"{cs['shape'][0]}x{cs['shape'][1]}x{cs['shape'][2]}/{cs['route']}"
-                                 for cs in cases}) if only is not None else "all",
+                "cases": case_names if only is not None else "all",
                 "parallelism": f"batch-shard x{world}",
                 "l2": "per-step working set ~1 GB > 126 MB L2 (inputs larger than L2)",
                 "flops_per_step_per_gpu": sweep_flops,
             },
             "roofline": {
                 "bound": "tensor",
-                "kernel": f"bigemm {dom_phase} {h}x{w}x{c}/d{d} {route}",
+                "kernel": f"{dom_name} {h}x{w}x{c}/d{d} {route} B={batch}",
                 "achieved": round(achieved, 3),
                 "peak": peaks["bf16_tflops"],
                 "unit": "TFLOP/s",
                 "frac": round(achieved / peaks["bf16_tflops"], 4),
                 "peak_source": peaks["source"],
-                "traffic": None,
+                "launch_ms": round(dom_ms, 4),
+                "algorithmic_flops_per_launch": dom_flops,
+                "traffic": None if traffic is None else traffic[0],
+                "traffic_source": None if traffic is None else traffic[1],
             },
             "per_call_ms": {f"{k[0][0]}x{k[0][1]}x{k[0][2]}/{k[1]}": [round(v[0], 4), round(v[1], 4)]
                             for k, v in per.items()},
+            "per_kernel_ms": {f"{k[0][0]}x{k[0][1]}x{k[0][2]}/{k[1]}": {n: round(t, 4) for n, t in v.items()}
+                              for k, v in kern.items()},
             "e2e": e2e,
             "gpu_launches": int(launches),
             "clocks": clk.summary(),

@@ -131,6 +131,23 @@ typedef struct ow_bigemm_grads_t {
  */
 OW_API uint64_t ow_launch_count(void);
 
+/*
+ * Kernel timing for measurement tools.  While set, every call in this
+ * process (any host thread) records the caller's CUDA events (cudaEvent_t
+ * cast to void*) on the call's stream immediately before and after one of
+ * its kernels:
+ *   OW_PROF_FWD  the tensor-core forward kernel,
+ *   OW_PROF_PACK the backward pack kernel (operand images),
+ *   OW_PROF_BWD  the backward role kernel.
+ * Passing NULL for both events stops recording for that kernel.  Returns
+ * OW_ERR_INVALID for an unknown ``kernel``.  No counterpart in the reference
+ * (it is a measurement aid, not part of the operator).
+ */
+#define OW_PROF_FWD 0
+#define OW_PROF_PACK 1
+#define OW_PROF_BWD 2
+OW_API int ow_profile_events(int kernel, void* start, void* stop);
+
 /* ABI version compiled into the library (OW_ABI_VERSION). */
 OW_API int ow_abi_version(void);
 

@@ -67,7 +67,7 @@ EXPORTS = (
     "ow_abi_version", "ow_last_error", "ow_device_supported", "ow_device_fault",
     "ow_launch_count", "ow_bigemm_workspace_size",
     "ow_rmsnorm_rstd", "ow_bigemm_fwd", "ow_bigemm_bwd", "ow_bigemm_fwd_noalloc",
-    "ow_noalloc_scratch_limit",
+    "ow_noalloc_scratch_limit", "ow_profile_events",
 )
 
 _lock = threading.Lock()
@@ -98,6 +98,8 @@ def load() -> ctypes.CDLL:
         lib.ow_device_fault.argtypes = [ctypes.c_int, ctypes.c_int]
         lib.ow_device_fault.restype = ctypes.c_int
         lib.ow_launch_count.restype = ctypes.c_uint64
+        lib.ow_profile_events.argtypes = [ctypes.c_int, _vp, _vp]
+        lib.ow_profile_events.restype = ctypes.c_int
         lib.ow_bigemm_workspace_size.argtypes = [ctypes.POINTER(Args), ctypes.c_int]
         lib.ow_bigemm_workspace_size.restype = ctypes.c_size_t
         lib.ow_rmsnorm_rstd.argtypes = [_vp, _c_i32, _c_i32, ctypes.c_int64, _c_i32,

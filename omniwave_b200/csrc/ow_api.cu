@@ -20,6 +20,14 @@ static std::atomic<uint64_t> g_launches{0};
 
 void count_launches(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
 
+// Process-wide (autograd runs backward calls on its own device threads).
+static std::atomic<void*> g_prof[3][2] = {};
+
+void profile_mark(int kernel, bool after, cudaStream_t st) {
+  void* e = g_prof[kernel][after ? 1 : 0].load(std::memory_order_acquire);
+  if (e) cudaEventRecord((cudaEvent_t)e, st);
+}
+
 void set_error(const char* fmt, ...) {
   va_list ap;
   va_start(ap, fmt);
@@ -99,6 +107,16 @@ extern "C" {
 int ow_abi_version(void) { return OW_ABI_VERSION; }
 
 uint64_t ow_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int ow_profile_events(int kernel, void* start, void* stop) {
+  if (kernel < OW_PROF_FWD || kernel > OW_PROF_BWD) {
+    set_error("ow_profile_events: unknown kernel %d", kernel);
+    return OW_ERR_INVALID;
+  }
+  g_prof[kernel][0].store(start, std::memory_order_release);
+  g_prof[kernel][1].store(stop, std::memory_order_release);
+  return OW_OK;
+}
 
 const char* ow_last_error(void) { return g_err; }
 

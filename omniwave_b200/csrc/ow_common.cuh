@@ -31,6 +31,10 @@ void clear_error();
 
 void count_launches(int n);
 
+// Records the caller's profiling event (ow_profile_events) for ``kernel``
+// before (after == false) or after its launch on ``st``; no-op when unset.
+void profile_mark(int kernel, bool after, cudaStream_t st);
+
 #define OW_CHECK_LAUNCH(what)                                                   \
   do {                                                                          \
     cudaError_t e_ = cudaGetLastError();                                        \

@@ -24,6 +24,26 @@ static __device__ int g_fault = 0;
 
 constexpr int kFaultWait = 1;
 
+// Optional timeline tracing (builds with -DOW_TRACE only): OW_TR(slot, ev)
+// records %globaltimer into a per-translation-unit table indexed by
+// (CTA, slot, event) for the first kTraceCtas CTAs.  Compiles to nothing in
+// the product build.
+#ifdef OW_TRACE
+constexpr int kTraceEvents = 96, kTraceSlots = 3, kTraceCtas = 160;
+static __device__ unsigned long long g_trace[kTraceCtas * kTraceSlots * kTraceEvents];
+#define OW_TR(slot, ev)                                                                             \
+  do {                                                                                              \
+    if ((ev) < ::ow::sm100::kTraceEvents && blockIdx.x < ::ow::sm100::kTraceCtas) {                 \
+      unsigned long long t_;                                                                        \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                        \
+      ::ow::sm100::g_trace[(blockIdx.x * ::ow::sm100::kTraceSlots + (slot)) * ::ow::sm100::kTraceEvents + \
+                           (ev)] = t_;                                                              \
+    }                                                                                               \
+  } while (0)
+#else
+#define OW_TR(slot, ev) ((void)0)
+#endif
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

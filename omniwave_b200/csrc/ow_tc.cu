@@ -684,10 +684,12 @@ int tc_forward_t(const ow_bigemm_args_t* a, const Prob& p, cudaStream_t st, Carv
       set_error("tc forward: cannot reserve %d bytes of shared memory: %s", Cfg<D>::SMEM, cudaGetErrorString(e));
       return OW_ERR_CUDA;
     }
+    profile_mark(OW_PROF_FWD, false, st);
     launch(kern, grid, TC_THREADS, Cfg<D>::SMEM, st, p, (const TX*)a->x, (const float*)a->rstd, a->x_dtype,
            (const unsigned char*)(base + w.img), (const uint16_t*)(base + w.amat),
            (const float*)(base + w.gg), (const float*)(base + w.nw), (const int*)(base + w.contig),
            a->sample_scale, a->residual, (TO*)a->out, vec_ok);
+    profile_mark(OW_PROF_FWD, true, st);
     OW_CHECK_LAUNCH("tc_fwd_kernel");
     return OW_OK;
   };

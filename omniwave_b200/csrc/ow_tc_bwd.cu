@@ -725,6 +725,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
       };
       if (role == R_DGRAD) {
         auto load_w = [&](int c) {
+          { const int it_ = c / nchunks, j_ = c % nchunks; if (it_ < 3 && j_ < 4) OW_TR(2, it_ * 32 + 26 + j_); }
           uint64_t* bar = (c & 1) ? bar_g2 : bar_g1;
           mbar_arrive_expect_tx(bar, 3 * C::BU_BYTES);
           bulk_g2s(sW + (c & 1) * 3 * C::BU_BYTES, chunk_img(c), 3 * C::BU_BYTES, bar);
@@ -735,13 +736,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
         for (int it = 0; it < nit && !*sAbort; ++it) {
           for (int j = 0; j < nchunks; ++j) {
             const int c = it * nchunks + j;
-            if (j == nchunks - 1 && it + 1 < nit && mbar_wait(bar_pf, it & 1, sAbort)) load_item(it + 1);
+            if (j == nchunks - 1 && it + 1 < nit && mbar_wait(bar_pf, it & 1, sAbort)) {
+              if (it < 3) OW_TR(2, it * 32 + 24);
+              load_item(it + 1);
+            }
             if (c + 2 < total_chunks && mbar_wait((c & 1) ? bar_e1 : bar_e0, (c >> 1) & 1, sAbort)) load_w(c + 2);
           }
-          if (mbar_wait(bar_tf, it & 1, sAbort)) load_t(it);
+          if (mbar_wait(bar_tf, it & 1, sAbort)) {
+            if (it < 3) OW_TR(2, it * 32 + 25);
+            load_t(it);
+          }
         }
       } else if (role == R_UV) {
         auto load_w = [&](int c) {
+          { const int it_ = c / nchunks, j_ = c % nchunks; if (it_ < 3 && j_ < 4) OW_TR(2, it_ * 32 + 26 + j_); }
           mbar_arrive_expect_tx(bar_g1, 3 * C::BU_BYTES);
           bulk_g2s(sW, chunk_img(c), 3 * C::BU_BYTES, bar_g1);
         };
@@ -752,7 +760,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
             const int c = it * nchunks + j;
             if (c + 1 < total_chunks && mbar_wait(bar_a, c & 1, sAbort)) load_w(c + 1);
           }
-          if (it + 1 < nit && mbar_wait(bar_w, it & 1, sAbort)) load_item(it + 1);
+          if (it + 1 < nit && mbar_wait(bar_w, it & 1, sAbort)) {
+            if (it < 3) OW_TR(2, it * 32 + 24);
+            load_item(it + 1);
+          }
         }
       } else {
         auto load_w1 = [&](int c) {
@@ -776,8 +787,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
             }
           }
           if (it + 1 < nit) {
-            if (mbar_wait(bar_pf, it & 1, sAbort)) load_item(it + 1);
-            if (mbar_wait(bar_epd, it & 1, sAbort)) load_g(it + 1);
+            if (mbar_wait(bar_pf, it & 1, sAbort)) {
+              if (it < 3) OW_TR(2, it * 32 + 24);
+              load_item(it + 1);
+            }
+            if (mbar_wait(bar_epd, it & 1, sAbort)) {
+              if (it < 3) OW_TR(2, it * 32 + 25);
+              load_g(it + 1);
+            }
           }
         }
       }
@@ -805,6 +822,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
       int c = 0, pc = 0;
       for (int it = 0; it < nit; ++it) {
         mbar_wait(bar_p, it & 1, sAbort);
+        if (it < 3) OW_TR(1, it * 32 + 12);
         tc_fence_after();
         for (int j = 0; j < nchunks; ++j, ++c) {
           uint32_t aWc = aW;
@@ -814,6 +832,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           } else {
             mbar_wait(bar_g1, c & 1, sAbort);
           }
+          if (it < 3 && j < 4) OW_TR(1, it * 32 + 13 + j);
           tc_fence_after();
           if (!*sAbort) {
             kmma(C::T_U, aPu, BM, aWc, NC, D / 16, ID_N64, false);
@@ -823,6 +842,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           umma_commit(bar_a);
           if (j == nchunks - 1 && role == R_DGRAD) umma_commit(bar_pf);
           mbar_wait(bar_du, c & 1, sAbort);
+          if (it < 3 && j < 4) OW_TR(1, it * 32 + 17 + j);
           tc_fence_after();
           if (role == R_DGRAD) {
             if (j == 0 && it > 0) {  // previous epilogue has read dP out of TMEM
@@ -908,6 +928,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
       // ---- chunk loop
       for (int j = 0; j < nchunks; ++j, ++c) {
         mbar_wait(bar_a, c & 1, sAbort);
+        if (tid == 0 && it < 3 && j < 4) OW_TR(0, it * 32 + 2 * j);
         __syncwarp();
         tc_fence_after();
         uint32_t ur[32], vr[32], zr[32];
@@ -981,6 +1002,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
         }
         fence_proxy_async_smem();
         tc_fence_before();
+        if (tid == 0 && it < 3 && j < 4) OW_TR(0, it * 32 + 2 * j + 1);
         mbar_arrive(bar_du);
         if (role == R_O) {
           // Zo chunk = A_o Z into the pair buffer (atom j & 1).
@@ -1015,6 +1037,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
       }
 
       // ---- per-item epilogue
+      if (tid == 0 && it < 3) OW_TR(0, it * 32 + 8);
       if (role == R_DGRAD) {
         // Metadata of this item for the dX scatter.
         if (tid < BM) sRow[tid] = mreg.row;
@@ -1025,6 +1048,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
         const bool cont = *sCont != 0;
         mbar_wait(bar_b, (c - 1) & 1, sAbort);  // last dP done
         mbar_wait(bar_t, it & 1, sAbort);       // T image of this item loaded
+        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 9);
         __syncwarp();
         tc_fence_after();
         // Warp (lq, hw): tiles 2lq, 2lq+1 (TMEM lanes 32lq..32lq+31), channels
@@ -1103,12 +1127,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
             }
           }
         }
+        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 10);
         tc_fence_before();
         mbar_arrive(bar_epd);
         comp_sync();  // T (in the dU/dV region) and the metadata are read out
       } else if (role == R_O) {
         mbar_wait(bar_b, (c - 1) & 1, sAbort);   // Y complete
         mbar_wait(bar_gl, it & 1, sAbort);      // G' of this item present
+        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 9);
         __syncwarp();
         tc_fence_after();
         unsigned char* stY = sm + C::O_STG;
@@ -1134,6 +1160,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           gram16<BF16>(accA[0], rowG, rowY, lane);
           comp_sync();
         }
+        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 10);
         tc_fence_before();
         mbar_arrive(bar_epd);
       }
@@ -1366,7 +1393,9 @@ int tc_backward_t(const ow_bigemm_args_t* ar, const ow_bigemm_grads_t* gr, const
     const int64_t items = (int64_t)p.Qc * ((p.BQ() + 7) / 8);
     if (items > 0) {
       constexpr int pack_smem = STG_BYTES + (BM + D) * 4 + 128;
+      profile_mark(OW_PROF_PACK, false, st);
       launch(tc_pack_kernel<D, BF16, TX, TO>, (int)items, NCOMP, pack_smem, st, a);
+      profile_mark(OW_PROF_PACK, true, st);
       OW_CHECK_LAUNCH("tc_pack_kernel");
     }
     auto kern = tc_bwd_kernel<D, BF16, TX, TO>;
@@ -1375,7 +1404,9 @@ int tc_backward_t(const ow_bigemm_args_t* ar, const ow_bigemm_grads_t* gr, const
       set_error("tc backward: cannot reserve %d bytes of shared memory: %s", BCfg<D>::SMEM, cudaGetErrorString(e));
       return OW_ERR_CUDA;
     }
+    profile_mark(OW_PROF_BWD, false, st);
     launch(kern, pl.grid, TC_THREADS, BCfg<D>::SMEM, st, a);
+    profile_mark(OW_PROF_BWD, true, st);
     OW_CHECK_LAUNCH("tc_bwd_kernel");
     return OW_OK;
   };
@@ -1426,3 +1457,14 @@ int tc_backward(const ow_bigemm_args_t* a, const ow_bigemm_grads_t* gr, const Pr
 }
 
 }  // namespace ow
+
+#ifdef OW_TRACE
+extern "C" __attribute__((visibility("default"))) int ow_trace_bwd(void* host, size_t bytes, int clear) {
+  if (clear) {
+    void* dev = nullptr;
+    cudaGetSymbolAddress(&dev, ow::sm100::g_trace);
+    return (int)cudaMemset(dev, 0, sizeof(ow::sm100::g_trace));
+  }
+  return (int)cudaMemcpyFromSymbol(host, ow::sm100::g_trace, bytes);
+}
+#endif

@@ -43,6 +43,14 @@ def test_abi_version_and_counters():
     assert lib.ow_launch_count() >= 0
 
 
+def test_profile_events_checks_kernel_id():
+    lib = _lib.load()
+    assert lib.ow_profile_events(7, None, None) == 1  # OW_ERR_INVALID
+    assert "unknown kernel" in lib.ow_last_error().decode()
+    for k in (0, 1, 2):  # NULL events: recording off, nothing touches CUDA
+        assert lib.ow_profile_events(k, None, None) == 0
+
+
 def _args(**over):
     r = _lib.Route(2, 14, 14, 512, 13, 4, 16, 128, 256, 1, 1)
     a = _lib.Args(r, 1, 2, 2, None, None, 1, 1, 1, 1, 1, 1, 1, 0, None, 0, 1, 2, None, 0)
