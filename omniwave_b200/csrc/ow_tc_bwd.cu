@@ -4,13 +4,16 @@
 // The gradient of the forward (reference.py:147-171, taken by autograd in the
 // reference) is, per tile with G' = mask * scale * dOut and G = G' * gamma:
 //
-//   dY' = A_o^T G             dZ = dY' B_o^T          (Z = silu(U) * V)
+//   H   = A_o^T G'            dZ = (H * gamma) B_o^T  (Z = silu(U) * V)
 //   dU  = dZ * V * silu'(U)   dV = dZ * silu(U)
 //   dP_u = dU B_u^T           dP_v = dV B_v^T
 //   dT  = A_u^T dP_u + A_v^T dP_v                          -> dX (scattered)
 //   dA_u = sum dP_u T^T,  dA_v = sum dP_v T^T,  dA_o = sum G (Z B_o)^T
 //   dB_u = sum P_u^T dU,  dB_v = sum P_v^T dV
-//   M_o  = sum (A_o Z)^T G'  ->  dB_o = M_o * gamma,  dgamma = sum_e B_o * M_o
+//   M_o  = sum (A_o Z)^T G' = sum Z^T H  ->  dB_o = M_o * gamma,  dgamma = sum_e B_o * M_o
+//
+// gamma is folded into the B_o^T weight stages (dZ = H (B_o diag(gamma))^T),
+// so H serves both dZ and M_o and no token mix of Z is needed.
 //
 // The weight gradients sum over every tile of a channel group; their f32
 // accumulators (3 x d x rd) do not fit one SM's 512 TMEM columns next to the
@@ -18,9 +21,9 @@
 //
 //   DGRAD  (any item)      U, V, dZ -> dU, dV -> dP_u, dP_v (TMEM)   -> dX, dA_u, dA_v
 //   UV(h)  (one group)     U, V, dZ on rd half h -> dU, dV -> TMEM += dU^T P_u, dV^T P_v
-//   O      (one group)     U, V -> Z -> A_o Z; TMEM Y += Z B_o, M_o += (A_o Z)^T G'  -> dA_o
+//   O      (one group)     U, V -> Z; TMEM Y += Z B_o, M_o += Z^T H  -> dA_o
 //
-// Every role needs the same per-item operands (P_u, P_v, dY', G', T).  A
+// Every role needs the same per-item operands (P_u, P_v, H, G', T).  A
 // pack kernel with many CTAs per SM gathers x and dOut through the route
 // tables once per item and writes those five operands as pre-swizzled
 // images; the persistent role kernel then streams them (and the weight
@@ -49,7 +52,6 @@ namespace {
 using namespace sm100;
 
 constexpr int BM = 128;
-constexpr int NC = 64;
 constexpr int NCOMP_WARPS = 8;
 constexpr int NCOMP = NCOMP_WARPS * 32;
 constexpr int MMA_WARP = NCOMP_WARPS;
@@ -64,48 +66,76 @@ enum Role { R_DGRAD = 0, R_UV = 1, R_O = 2 };
 template <int D>
 struct BCfg {
   static constexpr int RD = 2 * D;
-  static constexpr int NQ = RD / NC;
-  static constexpr int NQH = 2;                 // chunks per 128-feature half
-  static constexpr int NH = RD / 128;           // halves
+  static constexpr int NH = RD / 128;           // 128-feature halves
+  // Pipeline step: SC features per sub-chunk.  The U/V/dZ accumulators of two
+  // sub-chunks are live in TMEM at once (one being read by the compute warps
+  // while the tensor pipe fills the other), which at d = 128 leaves room for
+  // 32 features per sub-chunk next to the d x 2d f32 accumulators.
+  static constexpr int SC = D == 64 ? 64 : 32;
+  static constexpr int NSUB = RD / SC;          // sub-chunks per item (DGRAD, O)
+  static constexpr int NSUB_UV = 128 / SC;      // sub-chunks per UV half
+  static constexpr int SPC = 64 / SC;           // sub-chunks per 64-feature chunk
   static constexpr int P_BYTES = BM * D * 2;
-  static constexpr int Z_BYTES = BM * NC * 2;   // 16 KB
-  static constexpr int BU_BYTES = NC * D * 2;   // one weight sub-image
-  static constexpr int IMG_BYTES = 6 * BU_BYTES;  // Bu | Bv | BoT | BuT | BvT | Bo
+  static constexpr int Z_BYTES = BM * 64 * 2;   // one 64-column SW128 atom of 128 rows (16 KB)
+  // Weight images per channel group: for every sub-chunk s one contiguous
+  // stage [B_u | B_v | B_o^T] of SC features x D channels (K-major, SC rows),
+  // then for every 64-feature chunk k the slice B_o[k] as D rows x 64 features.
+  static constexpr int SUB_BYTES = SC * D * 2;
+  static constexpr int A_BYTES = 3 * SUB_BYTES;
+  static constexpr int BO_BYTES = D * 64 * 2;
+  static constexpr int QC_IMG = NSUB * A_BYTES + (RD / 64) * BO_BYTES;
   // Packed per-item operand images written by the pack kernel, each an SW128
-  // K-major [BM x D] image: P_u | P_v | dY' | G' | T.
-  static constexpr int PK_DY = 2, PK_G = 3, PK_T = 4;
+  // K-major [BM x D] image: P_u | P_v | H = A_o^T G' | G' | T.
+  static constexpr int PK_H = 2, PK_G = 3, PK_T = 4;
   static constexpr int ITEM_BYTES = 5 * P_BYTES;
   // Shared-memory plans (bytes).  Common: P_u at 0, P_v at P, X1 at 2P.
   static constexpr int OFF_PU = 0, OFF_PV = P_BYTES, OFF_X1 = 2 * P_BYTES;
-  static constexpr int ALIGN1K(int v) { return (v + 1023) / 1024 * 1024; }
-  // DGRAD: dU | dV of one chunk, reused for the T image in the epilogue.
+  // DGRAD: two dU/dV buffers (SC = 64: one atom each; SC = 32: the two column
+  // halves of one atom), reused for the T image in the epilogue; three
+  // weight stages.
   static constexpr int D_S = 3 * P_BYTES;
-  static constexpr int D_SBYTES = 2 * Z_BYTES > P_BYTES ? 2 * Z_BYTES : P_BYTES;
-  static constexpr int D_W = D_S + D_SBYTES;                 // 2 stages x (Bu | Bv | BoT)
-  static constexpr int D_END = D_W + 6 * BU_BYTES;
-  // UV
-  static constexpr int U_S = 3 * P_BYTES;                    // dU_h | dV_h (128 features each)
+  static constexpr int DS_BYTES = 4 * BM * SC * 2 > P_BYTES ? 4 * BM * SC * 2 : P_BYTES;
+  static constexpr int D_NST = 3;
+  // At d = 64 a channel group's weights (48 KB per role) stay resident in
+  // shared memory, one slot per sub-chunk, and are loaded again only when a
+  // CTA moves to another channel group; DGRAD then also has a T region of its
+  // own so that T is loaded ahead of the epilogue.
+  static constexpr bool RES = D == 64;
+  static constexpr int D_W = D_S + DS_BYTES;
+  static constexpr int D_T = D_W + (RES ? NSUB : D_NST) * A_BYTES;
+  static constexpr int D_END = D_T + (RES ? P_BYTES : 0);
+  static constexpr int D_TT = RES ? D_T : D_S;              // where the epilogue reads T
+  // UV: item buffers (two at d = 64), dU_h | dV_h for 128 features, two stages.
+  static constexpr int U_NB = D == 64 ? 2 : 1;
+  static constexpr int U_S = U_NB * 3 * P_BYTES;
   static constexpr int U_W = U_S + 4 * Z_BYTES;
-  static constexpr int U_END = U_W + 3 * BU_BYTES;
-  // O
+  static constexpr int U_END = U_W + 2 * A_BYTES;
+  // O: P_u | P_v | G', two Z buffers, the (A_o Z) buffer of 128 features
+  // (reused for Y staging in the epilogue), two [B_u | B_v] stages, two B_o stages.
   static constexpr int O_Z = 3 * P_BYTES;
-  static constexpr int O_ZO = O_Z + Z_BYTES;                 // pair of chunks (128 features)
-  static constexpr int O_STG = O_ZO + 2 * Z_BYTES;           // Y staging for dA_o
-  static constexpr int O_W = ALIGN1K(O_STG + STG_BYTES);     // Bu | Bv | Bo
-  static constexpr int O_END = O_W + 3 * BU_BYTES;
+  static constexpr int ZB_BYTES = 2 * BM * SC * 2;
+  static constexpr int O_ZO = O_Z + ZB_BYTES;
+  static constexpr int O_W1 = O_ZO + 2 * Z_BYTES;
+  static constexpr int O_BO = O_W1 + 4 * SUB_BYTES;
+  static constexpr int O_END = O_BO + 2 * BO_BYTES;
   static constexpr int MAX_END = D_END > U_END ? (D_END > O_END ? D_END : O_END) : (U_END > O_END ? U_END : O_END);
   static constexpr int OFF_META = MAX_END;                   // row[BM], ch[D], cont
   static constexpr int META_BYTES = (BM + D + 4) * 4;
   static constexpr int OFF_BAR = OFF_META + META_BYTES;
-  static constexpr int BAR_BYTES = 16 * 8 + 16;
+  static constexpr int NBARS = 28;
+  static constexpr int BAR_BYTES = NBARS * 8 + 16;
   static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024;
   static_assert(SMEM <= 232448, "shared memory budget");
-  // TMEM columns.
-  static constexpr int T_U = 0, T_V = 64, T_DZ = 128;
-  static constexpr int T_DPU = 256, T_DPV = 256 + D;          // DGRAD
-  static constexpr int T_ACCU = 256, T_ACCV = 256 + D;        // UV
-  static constexpr int T_Y = 128, T_ACCO = 256;               // O (NH blocks of D)
-  static_assert(T_DPV + D <= TMEM_COLS && T_ACCO + NH * D <= TMEM_COLS, "TMEM budget");
+  static_assert(STG_BYTES <= 2 * Z_BYTES, "Y staging fits the (A_o Z) buffer");
+  static_assert(!RES || (NSUB <= 2 && NSUB_UV <= 2 && RD / 64 <= 2), "resident weights fit the slots");
+  // TMEM columns.  DGRAD / UV: U/V/dZ buffer b at b * 3SC; O: U/V buffer b at
+  // b * 2SC, Y at 4SC.
+  static constexpr int T_BUF3 = 3 * SC, T_BUF2 = 2 * SC;
+  static constexpr int T_DPU = TMEM_COLS - 2 * D, T_DPV = TMEM_COLS - D;    // DGRAD
+  static constexpr int T_ACCU = TMEM_COLS - 2 * D, T_ACCV = TMEM_COLS - D;  // UV
+  static constexpr int T_Y = 4 * SC, T_ACCO = TMEM_COLS - NH * D;           // O
+  static_assert(2 * T_BUF3 <= T_DPU, "TMEM budget (DGRAD / UV)");
+  static_assert(T_Y + D <= T_ACCO, "TMEM budget (O)");
 };
 
 // Grid plan and workspace layout (bytes).
@@ -129,7 +159,7 @@ struct BPlan {
     grid = nD + nH * p.Qc * nUVq + p.Qc * nOq;
     size_t o = 0;
     auto take = [&](size_t n) { size_t r = o; o = (o + n + 255) / 256 * 256; return r; };
-    img = take((size_t)p.Qc * C::NQ * C::IMG_BYTES);
+    img = take((size_t)p.Qc * C::QC_IMG);
     amat = take(3 * 256 * 2);
     gg = take((size_t)p.Qc * D * 4);
     nw = take((size_t)p.C * 4);
@@ -157,33 +187,38 @@ __global__ void tc_bwd_prep_kernel(Prob p, const TW* __restrict__ au, const TW* 
                                    float* __restrict__ gg, float* __restrict__ nw, int* __restrict__ contig) {
   using C = BCfg<D>;
   using T16 = std::conditional_t<BF16, __nv_bfloat16, __half>;
-  const int64_t per_sub = (int64_t)NC * D;
-  const int64_t per_chunk = 6 * per_sub;
-  const int64_t n_img = (int64_t)p.Qc * C::NQ * per_chunk;
+  constexpr int64_t per_a = 3LL * C::SC * D;           // one sub-chunk stage
+  constexpr int64_t per_qc = C::NSUB * per_a + (int64_t)C::RD * D;
+  const int64_t n_img = (int64_t)p.Qc * per_qc;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   for (int64_t i = tid; i < n_img; i += stride) {
-    const int64_t chunk = i / per_chunk;
-    const int e = (int)(i - chunk * per_chunk);
-    const int sub = (int)(e / per_sub), r = (int)(e - sub * per_sub);
-    const int qc = (int)(chunk / C::NQ), q = (int)(chunk - (int64_t)qc * C::NQ);
-    const int f0 = q * NC;
+    const int qc = (int)(i / per_qc);
+    const int64_t e = i - (int64_t)qc * per_qc;
+    unsigned char* base = img + (int64_t)qc * C::QC_IMG;
     float v;
     uint32_t off;
-    if (sub < 3) {  // rows = 64 features n, K = D channels k
-      const int n = r / D, k = r - n * D;
-      if (sub == 0) v = load_as<float>(bu, ((int64_t)qc * D + k) * C::RD + f0 + n);
-      else if (sub == 1) v = load_as<float>(bv, ((int64_t)qc * D + k) * C::RD + f0 + n);
-      else v = load_as<float>(bo, ((int64_t)qc * C::RD + f0 + n) * D + k);
-      off = sub * C::BU_BYTES + sw128_off(n, k, NC);
-    } else {  // rows = D channels n, K = 64 features k
-      const int n = r / NC, k = r - n * NC;
-      if (sub == 3) v = load_as<float>(bu, ((int64_t)qc * D + n) * C::RD + f0 + k);
-      else if (sub == 4) v = load_as<float>(bv, ((int64_t)qc * D + n) * C::RD + f0 + k);
-      else v = load_as<float>(bo, ((int64_t)qc * C::RD + f0 + k) * D + n);
-      off = sub * C::BU_BYTES + sw128_off(n, k, D);
+    if (e < C::NSUB * per_a) {  // stage s: [B_u | B_v | B_o^T], rows = SC features n, K = D channels k
+      const int s = (int)(e / per_a);
+      const int r = (int)(e - s * per_a);
+      const int sub = r / (C::SC * D), rr = r - sub * (C::SC * D);
+      const int n = rr / D, k = rr - n * D;
+      const int f = s * C::SC + n;
+      if (sub == 0) v = load_as<float>(bu, ((int64_t)qc * D + k) * C::RD + f);
+      else if (sub == 1) v = load_as<float>(bv, ((int64_t)qc * D + k) * C::RD + f);
+      else {  // B_o^T scaled by the group's LayerScale gamma
+        const int ch = p.ch[qc * D + k];
+        v = ch < p.C ? load_as<float>(bo, ((int64_t)qc * C::RD + f) * D + k) * load_as<float>(gamma, ch) : 0.f;
+      }
+      off = (uint32_t)(s * C::A_BYTES + sub * C::SUB_BYTES) + sw128_off(n, k, C::SC);
+    } else {  // chunk k: B_o rows = D channels c, K = 64 features of the chunk
+      const int r = (int)(e - C::NSUB * per_a);
+      const int kc = r / (64 * D), rr = r - kc * 64 * D;
+      const int c = rr / 64, kf = rr - c * 64;
+      v = load_as<float>(bo, ((int64_t)qc * C::RD + kc * 64 + kf) * D + c);
+      off = (uint32_t)(C::NSUB * C::A_BYTES + kc * C::BO_BYTES) + sw128_off(c, kf, D);
     }
-    *reinterpret_cast<T16*>(img + chunk * C::IMG_BYTES + off) = Elem<T16>::from(v);
+    *reinterpret_cast<T16*>(base + off) = Elem<T16>::from(v);
   }
   for (int64_t i = tid; i < 3 * 256; i += stride) {
     const TW* src = i < 256 ? au : (i < 512 ? av : ao);
@@ -486,18 +521,24 @@ struct BwdArgs {
 // Pack kernel: gathers one M-block (128 token rows) of x (RMS-normalised in
 // block mode) and of dOut through the route tables and writes the operand
 // images the backward roles consume, once per item:
-//   P_u = A_u T, P_v = A_v T, dY' = A_o^T (G' gamma), G', T
+//   P_u = A_u T, P_v = A_v T, H = A_o^T G', G', T
 // (G' = mask * drop-path scale * dOut).  Many small CTAs per SM hide the
-// gather latency that a single persistent CTA could not.
+// gather latency that a single persistent CTA could not.  Each 64-channel
+// half of an image is one 16 KB SW128 atom; it is built in shared memory and
+// written with one bulk copy, so the global writes are full lines.
 // ---------------------------------------------------------------------------
 template <int D, bool BF16, typename TX, typename TO>
 __global__ void __launch_bounds__(NCOMP) tc_pack_kernel(BwdArgs a) {
   using C = BCfg<D>;
+  constexpr int ATOM = BM * 128;  // one 64-channel half of an operand image
   const Prob& p = a.p;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
-  unsigned char* stg = sm;
-  int* sRow = reinterpret_cast<int*>(sm + STG_BYTES);
+  unsigned char* atom0 = sm;             // T, then G'
+  unsigned char* atom1 = sm + ATOM;      // P_u, then H
+  unsigned char* atom2 = sm + 2 * ATOM;  // P_v
+  unsigned char* stg = sm + 3 * ATOM;    // gathered half, row-major
+  int* sRow = reinterpret_cast<int*>(stg + STG_BYTES);
   int* sCh = sRow + BM;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t4 = lane & 3;
@@ -518,62 +559,72 @@ __global__ void __launch_bounds__(NCOMP) tc_pack_kernel(BwdArgs a) {
   for (int k = tid; k < D; k += NCOMP) sCh[k] = p.ch[qc * D + k];
   __syncthreads();
   GatherCtx gc{sRow, sCh, p.N, p.C, a.vec_ok && a.contig[qc] != 0};
-  const float* ggq = a.gg + (int64_t)qc * D;
   unsigned char* out = a.packed + item * C::ITEM_BYTES;
   const uint32_t aStg = smem_u32(stg);
   const TX* x = (const TX*)a.x;
   const TO* dout = (const TO*)a.dout;
-  // staging (row-major) -> SW128 image in global memory
-  auto copy_out = [&](unsigned char* img, int hf) {
+  // staging (row-major) -> SW128 atom in shared memory
+  auto to_atom = [&](unsigned char* atom) {
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int unit = tid + u * NCOMP;
       const int r = unit >> 3, cj = unit & 7;
       const uint4 v = *reinterpret_cast<const uint4*>(stg + (r * STG_LD + cj * 8) * 2);
-      *reinterpret_cast<uint4*>(img + sw128_off(r, hf * 64 + cj * 8, BM)) = v;
+      *reinterpret_cast<uint4*>(atom + sw128_off(r, cj * 8, BM)) = v;
     }
   };
+  // Atoms are byte-identical to the global image halves: one bulk store each.
+  auto atoms_ready = [&]() {
+    fence_proxy_async_smem();
+    __syncthreads();
+  };
+  auto atoms_free = [&]() {
+    if (tid == 0) bulk_wait_read();
+    __syncthreads();
+  };
   for (int hf = 0; hf < D / 64; ++hf) {
+    RowRegs<TO, 1> rg;
     if (gc.cont) {
       RowRegs<TX, 1> rx;
-      RowRegs<TO, 1> rg;
       rows_issue<TX, 1>(rx, gc, x, hf, a.rstd, nullptr, tid);
       rows_issue<TO, 1>(rg, gc, dout, hf, nullptr, a.scale, tid);
       rows_store<TX, 1, BF16>(rx, 0, hf, gc, stg, false, a.rstd != nullptr, a.nw, nullptr, a.x_dt, tid);
-      __syncthreads();
-      copy_out(out + C::PK_T * C::P_BYTES, hf);
-      {
-        uint32_t f[4];
-        load_afrag(a.amat, false, g, t4, f);
-        mix_half<BF16>(aStg, f, out, hf, warp, lane);
-        load_afrag(a.amat + 256, false, g, t4, f);
-        mix_half<BF16>(aStg, f, out + C::P_BYTES, hf, warp, lane);
-      }
-      __syncthreads();
-      rows_store<TO, 1, BF16>(rg, 0, hf, gc, stg, false, false, nullptr, nullptr, 0, tid);
     } else {
       gather_half<TX, BF16>(gc, x, hf, a.rstd, a.nw, a.x_dt, nullptr, nullptr, stg, false, tid);
-      __syncthreads();
-      copy_out(out + C::PK_T * C::P_BYTES, hf);
-      {
-        uint32_t f[4];
-        load_afrag(a.amat, false, g, t4, f);
-        mix_half<BF16>(aStg, f, out, hf, warp, lane);
-        load_afrag(a.amat + 256, false, g, t4, f);
-        mix_half<BF16>(aStg, f, out + C::P_BYTES, hf, warp, lane);
-      }
-      __syncthreads();
-      gather_half<TO, BF16>(gc, dout, hf, nullptr, nullptr, 0, a.scale, nullptr, stg, false, tid);
     }
-    __syncthreads();
-    copy_out(out + C::PK_G * C::P_BYTES, hf);
+    atoms_free();  // also publishes stg
+    to_atom(atom0);
+    {
+      uint32_t f[4];
+      load_afrag(a.amat, false, g, t4, f);
+      mix_half<BF16>(aStg, f, atom1, 0, warp, lane);
+      load_afrag(a.amat + 256, false, g, t4, f);
+      mix_half<BF16>(aStg, f, atom2, 0, warp, lane);
+    }
+    atoms_ready();
+    if (tid == 0) {
+      bulk_s2g(out + C::PK_T * C::P_BYTES + hf * ATOM, atom0, ATOM);
+      bulk_s2g(out + hf * ATOM, atom1, ATOM);
+      bulk_s2g(out + C::P_BYTES + hf * ATOM, atom2, ATOM);
+      bulk_commit();
+    }
+    if (gc.cont) rows_store<TO, 1, BF16>(rg, 0, hf, gc, stg, false, false, nullptr, nullptr, 0, tid);
+    else gather_half<TO, BF16>(gc, dout, hf, nullptr, nullptr, 0, a.scale, nullptr, stg, false, tid);
+    atoms_free();
+    to_atom(atom0);
     {
       uint32_t f[4];
       load_afrag(a.amat + 512, true, g, t4, f);
-      mix_half<BF16>(aStg, f, out + C::PK_DY * C::P_BYTES, hf, warp, lane, ggq);
+      mix_half<BF16>(aStg, f, atom1, 0, warp, lane);  // H = A_o^T G'
     }
-    __syncthreads();
+    atoms_ready();
+    if (tid == 0) {
+      bulk_s2g(out + C::PK_G * C::P_BYTES + hf * ATOM, atom0, ATOM);
+      bulk_s2g(out + C::PK_H * C::P_BYTES + hf * ATOM, atom1, ATOM);
+      bulk_commit();
+    }
   }
+  if (tid == 0) bulk_wait_all();
 }
 
 __device__ __forceinline__ void tmem_ld16x256_x2(uint32_t taddr, uint32_t (&r)[8]) {
@@ -589,40 +640,43 @@ __device__ __forceinline__ uint32_t movm_trans(uint32_t v) {
 }
 
 // ---------------------------------------------------------------------------
-// Role kernel (see the file header).  Operands of every item arrive from the
-// pack kernel through one bulk copy issued by the producer warp, so the
-// compute warps only run the chunk loop and the epilogue, and the next
-// item's tensor work overlaps the current epilogue.
+// Role kernel (see the file header).  The feature dimension is walked in
+// sub-chunks of SC features.  The tensor pipe fills one TMEM buffer with the
+// next sub-chunk's U/V(/dZ) while the compute warps turn the other buffer
+// into elementwise outputs; item operands and weight stages arrive by bulk
+// copies issued ahead of use by the producer warp.
 // ---------------------------------------------------------------------------
 template <int D, bool BF16, typename TX, typename TO>
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
   using C = BCfg<D>;
+  constexpr int SC = C::SC;
+  constexpr int HC = SC / 2;            // columns of a sub-chunk per compute thread
+  constexpr bool HALVES = SC == 32;     // two buffers share one 64-column atom
+  constexpr int NB_UV = C::U_NB;
   const Prob& p = a.p;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  unsigned char* sPu = sm + C::OFF_PU;
-  unsigned char* sPv = sm + C::OFF_PV;
-  unsigned char* sX1 = sm + C::OFF_X1;
   int* sRow = reinterpret_cast<int*>(sm + C::OFF_META);
   int* sCh = sRow + BM;
   volatile int* sCont = sCh + D;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
-  uint64_t* bar_p = bars + 0;    // item operands loaded (tx)
-  uint64_t* bar_a = bars + 1;    // U, V (, dZ) of a chunk done (commit)
-  uint64_t* bar_du = bars + 2;   // chunk's elementwise outputs written, TMEM working set read
-  uint64_t* bar_b = bars + 3;    // DGRAD: dP of a chunk done; O: Y of a chunk done
-  uint64_t* bar_w = bars + 4;    // UV: weight-gradient products of an item done; O: M_o pair done
-  uint64_t* bar_zo = bars + 5;   // O: A_o Z pair written
-  uint64_t* bar_g1 = bars + 6;   // weights (stage 0 / first group) loaded
-  uint64_t* bar_g2 = bars + 7;   // weights (stage 1 / second group) loaded
-  uint64_t* bar_e0 = bars + 8;   // DGRAD: weight stage 0 free
-  uint64_t* bar_e1 = bars + 9;   // DGRAD: weight stage 1 free
-  uint64_t* bar_pf = bars + 10;  // item operands no longer read (DGRAD, O)
-  uint64_t* bar_tf = bars + 11;  // DGRAD: last dP done (dU/dV region free for T)
-  uint64_t* bar_t = bars + 12;   // DGRAD: T image loaded
-  uint64_t* bar_epd = bars + 13; // epilogue done with TMEM accumulators (and G' for O)
-  uint64_t* bar_gl = bars + 14;  // O: G' loaded
-  uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* bar_p = bars + 0;     // [2] item operands of item buffer i loaded (tx)
+  uint64_t* bar_a = bars + 2;     // [2] U/V(/dZ) of TMEM buffer b computed (commit)
+  uint64_t* bar_du = bars + 4;    // [2] compute done with TMEM buffer b, its outputs in smem
+  uint64_t* bar_b = bars + 6;     // [2] DGRAD: dP read dU/dV buffer b; O: Y read Z buffer b (commit)
+  uint64_t* bar_wf = bars + 8;    // [3] weight stage loaded (tx)
+  uint64_t* bar_we = bars + 11;   // [3] DGRAD: weight stage no longer read (commit)
+  uint64_t* bar_bo = bars + 14;   // [2] O: B_o stage loaded (tx)
+  uint64_t* bar_boe = bars + 16;  // [2] O: B_o stage no longer read (commit)
+  uint64_t* bar_pf = bars + 18;   // DGRAD, O: item operands no longer read (commit)
+  uint64_t* bar_tf = bars + 19;   // DGRAD: last dP of the item done (commit)
+  uint64_t* bar_t = bars + 20;    // DGRAD: T image loaded (tx)
+  uint64_t* bar_w = bars + 21;    // UV: products of an item done; O: M_o of a pair done (commit)
+  uint64_t* bar_zo = bars + 22;   // O: (A_o Z) of a 128-feature pair written
+  uint64_t* bar_yd = bars + 23;   // O: Y of the item complete (commit)
+  uint64_t* bar_epd = bars + 24;  // O: epilogue done with G' and the staging buffer
+  uint64_t* bar_gl = bars + 25;   // O: G' loaded (tx)
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + C::NBARS);
   volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -664,24 +718,35 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
       n_items = m1 - m0;
     }
   }
-  const int nchunks = role == R_UV ? C::NQH : C::NQ;
-  const int q_base = role == R_UV ? h * C::NQH : 0;
+  const int nsub = role == R_UV ? C::NSUB_UV : C::NSUB;
+  const int q_base = role == R_UV ? h * C::NSUB_UV : 0;  // first sub-chunk of the role's features
+  // Each CTA walks its sub-chunks from a different starting point so that the
+  // CTAs of one role do not all fetch the same weight stage at once (the O
+  // role rotates by whole 128-feature pairs).
+  const int rot = role == R_O ? (int)(blockIdx.x % C::NH) * (128 / C::SC) : (int)(blockIdx.x % nsub);
+  auto sub_of = [&](int j) { return (j + rot) % nsub; };
   const int nit = (int)n_items;
+  const int total = nit * nsub;
 
   if (threadIdx.x == 0) {
-    mbar_init(bar_p, 1);
-    mbar_init(bar_a, 1);
-    mbar_init(bar_du, NCOMP);
-    mbar_init(bar_b, 1);
-    mbar_init(bar_w, 1);
-    mbar_init(bar_zo, NCOMP);
-    mbar_init(bar_g1, 1);
-    mbar_init(bar_g2, 1);
-    mbar_init(bar_e0, 1);
-    mbar_init(bar_e1, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar_p + i, 1);
+      mbar_init(bar_a + i, 1);
+      mbar_init(bar_du + i, NCOMP);
+      mbar_init(bar_b + i, 1);
+      mbar_init(bar_bo + i, 1);
+      mbar_init(bar_boe + i, 1);
+    }
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(bar_wf + i, 1);
+      mbar_init(bar_we + i, 1);
+    }
     mbar_init(bar_pf, 1);
     mbar_init(bar_tf, 1);
     mbar_init(bar_t, 1);
+    mbar_init(bar_w, 1);
+    mbar_init(bar_zo, NCOMP);
+    mbar_init(bar_yd, 1);
     mbar_init(bar_epd, NCOMP);
     mbar_init(bar_gl, 1);
     *sAbort = 0;
@@ -693,108 +758,156 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
   tc_fence_after();
   const uint32_t tbase = *sTmem;
 
-  unsigned char* sW = sm + (role == R_DGRAD ? C::D_W : (role == R_UV ? C::U_W : C::O_W));
-  const int total_chunks = nit * nchunks;
   auto item_of = [&](int it) { return it0 + (int64_t)it * it_step; };
-  auto chunk_img = [&](int c) {
-    const int it = c / nchunks, j = c - it * nchunks;
-    const int qc = (int)(item_of(it) / nMB);
-    return a.img + ((int64_t)qc * C::NQ + q_base + j) * C::IMG_BYTES;
-  };
   auto item_src = [&](int it) { return a.packed + item_of(it) * C::ITEM_BYTES; };
+  auto qimg = [&](int c) { return a.img + (item_of(c / nsub) / nMB) * C::QC_IMG; };
+  auto stage_src = [&](int c) { return qimg(c) + (int64_t)(q_base + sub_of(c % nsub)) * C::A_BYTES; };
+  auto bo_src = [&](int c) {
+    return qimg(c) + (int64_t)C::NSUB * C::A_BYTES + (int64_t)(sub_of(c % nsub) / C::SPC) * C::BO_BYTES;
+  };
+  // Double-buffered 64-row-block operands (dU/dV for DGRAD, Z for O): byte
+  // offset of buffer b's atom and its first column.
+  auto buf_atom = [&](int b, int atoms_per_buf) -> uint32_t {
+    return HALVES ? 0u : (uint32_t)(b * atoms_per_buf * C::Z_BYTES);
+  };
+  auto buf_col = [&](int b) { return HALVES ? b * 32 : 0; };
 
   if (warp == PROD_WARP) {
     // ------------------------------------------------ producer (bulk copies)
     if (lane == 0 && nit > 0) {
-      auto load_item = [&](int it) {
-        if (role == R_O) {
-          mbar_arrive_expect_tx(bar_p, 2 * C::P_BYTES);
-          bulk_g2s(sPu, item_src(it), 2 * C::P_BYTES, bar_p);
-        } else {
-          mbar_arrive_expect_tx(bar_p, 3 * C::P_BYTES);
-          bulk_g2s(sPu, item_src(it), 3 * C::P_BYTES, bar_p);
-        }
-      };
-      auto load_g = [&](int it) {  // O: G' into X1
-        mbar_arrive_expect_tx(bar_gl, C::P_BYTES);
-        bulk_g2s(sX1, item_src(it) + C::PK_G * C::P_BYTES, C::P_BYTES, bar_gl);
-      };
-      auto load_t = [&](int it) {  // DGRAD: T into the dU/dV region
-        mbar_arrive_expect_tx(bar_t, C::P_BYTES);
-        bulk_g2s(sm + C::D_S, item_src(it) + C::PK_T * C::P_BYTES, C::P_BYTES, bar_t);
-      };
       if (role == R_DGRAD) {
+        auto load_item = [&](int it) {
+          mbar_arrive_expect_tx(bar_p, 3 * C::P_BYTES);
+          bulk_g2s(sm, item_src(it), 3 * C::P_BYTES, bar_p);
+        };
         auto load_w = [&](int c) {
-          { const int it_ = c / nchunks, j_ = c % nchunks; if (it_ < 3 && j_ < 4) OW_TR(2, it_ * 32 + 26 + j_); }
-          uint64_t* bar = (c & 1) ? bar_g2 : bar_g1;
-          mbar_arrive_expect_tx(bar, 3 * C::BU_BYTES);
-          bulk_g2s(sW + (c & 1) * 3 * C::BU_BYTES, chunk_img(c), 3 * C::BU_BYTES, bar);
+          { const int i_ = c / nsub, j_ = c % nsub; if (i_ < 3 && j_ < 6) OW_TR(2, i_ * 32 + 26 + j_); }
+          const int st = c % C::D_NST;
+          mbar_arrive_expect_tx(bar_wf + st, C::A_BYTES);
+          bulk_g2s(sm + C::D_W + st * C::A_BYTES, stage_src(c), C::A_BYTES, bar_wf + st);
+        };
+        auto load_t = [&](int it) {
+          mbar_arrive_expect_tx(bar_t, C::P_BYTES);
+          bulk_g2s(sm + C::D_TT, item_src(it) + C::PK_T * C::P_BYTES, C::P_BYTES, bar_t);
         };
         load_item(0);
-        load_w(0);
-        if (total_chunks > 1) load_w(1);
-        for (int it = 0; it < nit && !*sAbort; ++it) {
-          for (int j = 0; j < nchunks; ++j) {
-            const int c = it * nchunks + j;
-            if (j == nchunks - 1 && it + 1 < nit && mbar_wait(bar_pf, it & 1, sAbort)) {
-              if (it < 3) OW_TR(2, it * 32 + 24);
-              load_item(it + 1);
-            }
-            if (c + 2 < total_chunks && mbar_wait((c & 1) ? bar_e1 : bar_e0, (c >> 1) & 1, sAbort)) load_w(c + 2);
-          }
-          if (mbar_wait(bar_tf, it & 1, sAbort)) {
-            if (it < 3) OW_TR(2, it * 32 + 25);
-            load_t(it);
-          }
-        }
-      } else if (role == R_UV) {
-        auto load_w = [&](int c) {
-          { const int it_ = c / nchunks, j_ = c % nchunks; if (it_ < 3 && j_ < 4) OW_TR(2, it_ * 32 + 26 + j_); }
-          mbar_arrive_expect_tx(bar_g1, 3 * C::BU_BYTES);
-          bulk_g2s(sW, chunk_img(c), 3 * C::BU_BYTES, bar_g1);
-        };
-        load_item(0);
-        load_w(0);
-        for (int it = 0; it < nit && !*sAbort; ++it) {
-          for (int j = 0; j < nchunks; ++j) {
-            const int c = it * nchunks + j;
-            if (c + 1 < total_chunks && mbar_wait(bar_a, c & 1, sAbort)) load_w(c + 1);
-          }
-          if (it + 1 < nit && mbar_wait(bar_w, it & 1, sAbort)) {
-            if (it < 3) OW_TR(2, it * 32 + 24);
-            load_item(it + 1);
-          }
-        }
-      } else {
-        auto load_w1 = [&](int c) {
-          mbar_arrive_expect_tx(bar_g1, 2 * C::BU_BYTES);
-          bulk_g2s(sW, chunk_img(c), 2 * C::BU_BYTES, bar_g1);
-        };
-        auto load_w2 = [&](int c) {
-          mbar_arrive_expect_tx(bar_g2, C::BU_BYTES);
-          bulk_g2s(sW + 2 * C::BU_BYTES, chunk_img(c) + 5 * C::BU_BYTES, C::BU_BYTES, bar_g2);
-        };
-        load_item(0);
-        load_g(0);
-        load_w1(0);
-        load_w2(0);
-        for (int it = 0; it < nit && !*sAbort; ++it) {
-          for (int j = 0; j < nchunks; ++j) {
-            const int c = it * nchunks + j;
-            if (c + 1 < total_chunks) {
-              if (mbar_wait(bar_a, c & 1, sAbort)) load_w1(c + 1);
-              if (mbar_wait(bar_b, c & 1, sAbort)) load_w2(c + 1);
-            }
-          }
-          if (it + 1 < nit) {
+        if constexpr (C::RES) {
+          // All sub-chunk stages of the item's channel group, in one copy.
+          auto load_all = [&](int it) {
+            mbar_arrive_expect_tx(bar_wf, C::NSUB * C::A_BYTES);
+            bulk_g2s(sm + C::D_W, qimg(it * nsub), C::NSUB * C::A_BYTES, bar_wf);
+          };
+          load_all(0);
+          load_t(0);
+          int epoch = 0;
+          for (int it = 0; it + 1 < nit && !*sAbort; ++it) {
             if (mbar_wait(bar_pf, it & 1, sAbort)) {
               if (it < 3) OW_TR(2, it * 32 + 24);
               load_item(it + 1);
             }
+            if (item_of(it + 1) / nMB != item_of(it) / nMB && mbar_wait(bar_we, epoch & 1, sAbort)) {
+              ++epoch;
+              load_all(it + 1);
+            }
             if (mbar_wait(bar_epd, it & 1, sAbort)) {
               if (it < 3) OW_TR(2, it * 32 + 25);
-              load_g(it + 1);
+              load_t(it + 1);
             }
+          }
+        } else {
+          for (int c = 0; c < C::D_NST && c < total; ++c) load_w(c);
+          for (int c = 0; c < total && !*sAbort; ++c) {
+            const int it = c / nsub, j = c - it * nsub;
+            if (j == nsub - 1 && it + 1 < nit && mbar_wait(bar_pf, it & 1, sAbort)) {
+              if (it < 3) OW_TR(2, it * 32 + 24);
+              load_item(it + 1);
+            }
+            if (c + C::D_NST < total && mbar_wait(bar_we + c % C::D_NST, (c / C::D_NST) & 1, sAbort))
+              load_w(c + C::D_NST);
+            if (j == nsub - 1 && mbar_wait(bar_tf, it & 1, sAbort)) {
+              if (it < 3) OW_TR(2, it * 32 + 25);
+              load_t(it);
+            }
+          }
+        }
+      } else if (role == R_UV) {
+        auto load_item = [&](int it) {
+          const int bf = it % NB_UV;
+          mbar_arrive_expect_tx(bar_p + bf, 3 * C::P_BYTES);
+          bulk_g2s(sm + bf * 3 * C::P_BYTES, item_src(it), 3 * C::P_BYTES, bar_p + bf);
+        };
+        auto load_w = [&](int c) {
+          { const int i_ = c / nsub, j_ = c % nsub; if (i_ < 3 && j_ < 6) OW_TR(2, i_ * 32 + 26 + j_); }
+          const int st = c & 1;
+          mbar_arrive_expect_tx(bar_wf + st, C::A_BYTES);
+          bulk_g2s(sm + C::U_W + st * C::A_BYTES, stage_src(c), C::A_BYTES, bar_wf + st);
+        };
+        for (int it = 0; it < NB_UV && it < nit; ++it) load_item(it);
+        if constexpr (C::RES) {  // the half's stages, once (the group never changes)
+          mbar_arrive_expect_tx(bar_wf, C::NSUB_UV * C::A_BYTES);
+          bulk_g2s(sm + C::U_W, qimg(0) + (int64_t)q_base * C::A_BYTES, C::NSUB_UV * C::A_BYTES, bar_wf);
+        } else {
+          load_w(0);
+          if (total > 1) load_w(1);
+        }
+        for (int c = 0; c < total && !*sAbort; ++c) {
+          const int it = c / nsub, j = c - it * nsub;
+          if (!C::RES && c + 2 < total && mbar_wait(bar_a + (c & 1), (c >> 1) & 1, sAbort)) load_w(c + 2);
+          if (j == nsub - 1 && it + NB_UV < nit && mbar_wait(bar_w, it & 1, sAbort)) {
+            if (it < 3) OW_TR(2, it * 32 + 24);
+            load_item(it + NB_UV);
+          }
+        }
+      } else {
+        const int nck = total / C::SPC;
+        auto load_p = [&](int it) {
+          mbar_arrive_expect_tx(bar_p, 2 * C::P_BYTES);
+          bulk_g2s(sm, item_src(it), 2 * C::P_BYTES, bar_p);
+        };
+        auto load_g = [&](int it) {
+          mbar_arrive_expect_tx(bar_gl, C::P_BYTES);
+          bulk_g2s(sm + C::OFF_X1, item_src(it) + C::PK_G * C::P_BYTES, C::P_BYTES, bar_gl);
+        };
+        auto load_w1 = [&](int c) {
+          { const int i_ = c / nsub, j_ = c % nsub; if (i_ < 3 && j_ < 6) OW_TR(2, i_ * 32 + 26 + j_); }
+          const int st = c & 1;
+          mbar_arrive_expect_tx(bar_wf + st, 2 * C::SUB_BYTES);
+          bulk_g2s(sm + C::O_W1 + st * 2 * C::SUB_BYTES, stage_src(c), 2 * C::SUB_BYTES, bar_wf + st);
+        };
+        auto load_bo = [&](int kc) {
+          const int st = kc & 1;
+          mbar_arrive_expect_tx(bar_bo + st, C::BO_BYTES);
+          bulk_g2s(sm + C::O_BO + st * C::BO_BYTES, bo_src(kc * C::SPC), C::BO_BYTES, bar_bo + st);
+        };
+        load_p(0);
+        load_g(0);
+        if constexpr (C::RES) {  // [B_u | B_v] of every sub-chunk and all of B_o, once
+          const unsigned char* g0 = qimg(0);
+          mbar_arrive_expect_tx(bar_wf, C::NSUB * 2 * C::SUB_BYTES + (C::RD / 64) * C::BO_BYTES);
+          for (int sj = 0; sj < C::NSUB; ++sj)
+            bulk_g2s(sm + C::O_W1 + sj * 2 * C::SUB_BYTES, g0 + (int64_t)sj * C::A_BYTES, 2 * C::SUB_BYTES, bar_wf);
+          bulk_g2s(sm + C::O_BO, g0 + (int64_t)C::NSUB * C::A_BYTES, (C::RD / 64) * C::BO_BYTES, bar_wf);
+        } else {
+          load_w1(0);
+          if (total > 1) load_w1(1);
+          load_bo(0);
+          if (nck > 1) load_bo(1);
+        }
+        for (int c = 0; c < total && !*sAbort; ++c) {
+          const int it = c / nsub, j = c - it * nsub;
+          if (!C::RES && c + 2 < total && mbar_wait(bar_a + (c & 1), (c >> 1) & 1, sAbort)) load_w1(c + 2);
+          const bool last = j == nsub - 1 && it + 1 < nit;
+          if (last && mbar_wait(bar_pf, it & 1, sAbort)) {
+            if (it < 3) OW_TR(2, it * 32 + 24);
+            load_p(it + 1);
+          }
+          if (!C::RES && c % C::SPC == C::SPC - 1) {
+            const int kc = c / C::SPC;
+            if (kc + 2 < nck && mbar_wait(bar_boe + (kc & 1), (kc >> 1) & 1, sAbort)) load_bo(kc + 2);
+          }
+          if (last && mbar_wait(bar_epd, it & 1, sAbort)) {
+            if (it < 3) OW_TR(2, it * 32 + 25);
+            load_g(it + 1);
           }
         }
       }
@@ -802,101 +915,178 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
   } else if (warp == MMA_WARP) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t ID_N64 = idesc_f16(BM, NC, BF16);
+      constexpr uint32_t ID_N = idesc_f16(BM, SC, BF16);
       constexpr uint32_t ID_ND = idesc_f16(BM, D, BF16);
       constexpr uint32_t ID_MN = idesc_f16_mn(BM, D, BF16);
       constexpr uint32_t ID_BMN = idesc_f16(BM, D, BF16) | (1u << 16);  // A K-major, B MN-major
-      const uint32_t aPu = smem_u32(sPu), aPv = smem_u32(sPv), aX1 = smem_u32(sX1);
-      const uint32_t aW = smem_u32(sW);
-      auto kmma = [&](uint32_t tcol, uint32_t aA, int arows, uint32_t aB, int brows, int ksteps, uint32_t id,
-                      bool acc0) {
+      // D (+)= A * B^T over ksteps 16-element K steps, both SW128 K-major.
+      auto kmma = [&](uint32_t tcol, uint32_t aA, int arows, int ka, uint32_t aB, int brows, int kb, int ksteps,
+                      uint32_t id, bool acc0) {
         for (int kk = 0; kk < ksteps; ++kk)
-          umma_f16(tbase + tcol, sdesc_sw128(sw128_kstep(aA, kk, arows)), sdesc_sw128(sw128_kstep(aB, kk, brows)),
-                   id, (acc0 || kk > 0) ? 1u : 0u);
+          umma_f16(tbase + tcol, sdesc_sw128(sw128_kstep(aA, ka + kk, arows)),
+                   sdesc_sw128(sw128_kstep(aB, kb + kk, brows)), id, (acc0 || kk > 0) ? 1u : 0u);
       };
+      // D (+)= A^T B over the 128 tokens, A and B token-major tiles read MN-major.
       auto mnmma = [&](uint32_t tcol, uint32_t aA, uint32_t aB, bool acc0) {
         for (int kk = 0; kk < BM / 16; ++kk)
           umma_f16(tbase + tcol, sdesc_sw128_mn(aA + kk * 2048, BM * 128), sdesc_sw128_mn(aB + kk * 2048, BM * 128),
                    ID_MN, (acc0 || kk > 0) ? 1u : 0u);
       };
-      int c = 0, pc = 0;
-      for (int it = 0; it < nit; ++it) {
-        mbar_wait(bar_p, it & 1, sAbort);
-        if (it < 3) OW_TR(1, it * 32 + 12);
-        tc_fence_after();
-        for (int j = 0; j < nchunks; ++j, ++c) {
-          uint32_t aWc = aW;
-          if (role == R_DGRAD) {
-            aWc = aW + (c & 1) * 3 * C::BU_BYTES;
-            mbar_wait((c & 1) ? bar_g2 : bar_g1, (c >> 1) & 1, sAbort);
-          } else {
-            mbar_wait(bar_g1, c & 1, sAbort);
-          }
-          if (it < 3 && j < 4) OW_TR(1, it * 32 + 13 + j);
+      const uint32_t s0 = smem_u32(sm);
+      if (role == R_DGRAD) {
+        const uint32_t aPu = s0 + C::OFF_PU, aPv = s0 + C::OFF_PV, aDY = s0 + C::OFF_X1;
+        auto dp = [&](int x) {  // dP_u += dU_x B_u[x]^T, dP_v += dV_x B_v[x]^T
+          const int bx = x & 1, jx = x % nsub;
+          mbar_wait(bar_du + bx, (x >> 1) & 1, sAbort);
           tc_fence_after();
           if (!*sAbort) {
-            kmma(C::T_U, aPu, BM, aWc, NC, D / 16, ID_N64, false);
-            kmma(C::T_V, aPv, BM, aWc + C::BU_BYTES, NC, D / 16, ID_N64, false);
-            if (role != R_O) kmma(C::T_DZ, aX1, BM, aWc + 2 * C::BU_BYTES, NC, D / 16, ID_N64, false);
+            const uint32_t aU = s0 + C::D_S + buf_atom(bx, 2), aV = aU + C::Z_BYTES;
+            const uint32_t aSt = s0 + C::D_W + (C::RES ? sub_of(jx) : x % C::D_NST) * C::A_BYTES;
+            const int k0 = buf_col(bx) / 16;
+            for (int kk = 0; kk < SC / 16; ++kk) {
+              const uint32_t acc = (jx > 0 || kk > 0) ? 1u : 0u;
+              umma_f16(tbase + C::T_DPU, sdesc_sw128(sw128_kstep(aU, k0 + kk, BM)),
+                       sdesc_sw128_mn(aSt + kk * 2048, SC * 128), ID_BMN, acc);
+              umma_f16(tbase + C::T_DPV, sdesc_sw128(sw128_kstep(aV, k0 + kk, BM)),
+                       sdesc_sw128_mn(aSt + C::SUB_BYTES + kk * 2048, SC * 128), ID_BMN, acc);
+            }
           }
-          umma_commit(bar_a);
-          if (j == nchunks - 1 && role == R_DGRAD) umma_commit(bar_pf);
-          mbar_wait(bar_du, c & 1, sAbort);
-          if (it < 3 && j < 4) OW_TR(1, it * 32 + 17 + j);
+          umma_commit(bar_b + bx);
+          if (!C::RES) umma_commit(bar_we + x % C::D_NST);
+          if (jx == nsub - 1) umma_commit(bar_tf);
+        };
+        int c = 0, epoch = 0;
+        for (int it = 0; it < nit; ++it) {
+          if (c > 0) dp(c - 1);  // finish the previous item before waiting for this one's operands
+          if (C::RES) {
+            if (it > 0 && item_of(it) / nMB != item_of(it - 1) / nMB) {
+              umma_commit(bar_we);  // resident weights of the previous group no longer read
+              ++epoch;
+            }
+            if (it == 0 || item_of(it) / nMB != item_of(it - 1) / nMB) mbar_wait(bar_wf, epoch & 1, sAbort);
+          }
+          mbar_wait(bar_p, it & 1, sAbort);
+          if (it < 3) OW_TR(1, it * 32 + 20);
           tc_fence_after();
-          if (role == R_DGRAD) {
-            if (j == 0 && it > 0) {  // previous epilogue has read dP out of TMEM
-              mbar_wait(bar_epd, (it - 1) & 1, sAbort);
-              tc_fence_after();
-            }
-            if (!*sAbort) {
-              // dP += dU_q B_u[:, q]^T with B_u's chunk image read MN-major.
-              const uint32_t aS = smem_u32(sm + C::D_S);
-              for (int kk = 0; kk < NC / 16; ++kk) {
-                umma_f16(tbase + C::T_DPU, sdesc_sw128(sw128_kstep(aS, kk, BM)),
-                         sdesc_sw128_mn(aWc + kk * 2048, NC * 128), ID_BMN, (j > 0 || kk > 0) ? 1u : 0u);
-                umma_f16(tbase + C::T_DPV, sdesc_sw128(sw128_kstep(aS + C::Z_BYTES, kk, BM)),
-                         sdesc_sw128_mn(aWc + C::BU_BYTES + kk * 2048, NC * 128), ID_BMN,
-                         (j > 0 || kk > 0) ? 1u : 0u);
-              }
-            }
-            umma_commit(bar_b);
-            umma_commit((c & 1) ? bar_e1 : bar_e0);
-            if (j == nchunks - 1) umma_commit(bar_tf);
-          } else if (role == R_O) {
-            mbar_wait(bar_g2, c & 1, sAbort);
-            if (j == 0 && it > 0) mbar_wait(bar_epd, (it - 1) & 1, sAbort);  // Y read out
+          for (int j = 0; j < nsub; ++j, ++c) {
+            const int b = c & 1;
+            if (!C::RES) mbar_wait(bar_wf + c % C::D_NST, (c / C::D_NST) & 1, sAbort);
+            if (it < 3 && j < 3) OW_TR(1, it * 32 + 21 + j);
             tc_fence_after();
-            if (!*sAbort) kmma(C::T_Y, smem_u32(sm + C::O_Z), BM, aW + 2 * C::BU_BYTES, D, NC / 16, ID_ND, j > 0);
-            umma_commit(bar_b);
-            if (j & 1) {
-              if (j == 1) mbar_wait(bar_gl, it & 1, sAbort);
-              mbar_wait(bar_zo, pc & 1, sAbort);
-              tc_fence_after();
-              if (!*sAbort) mnmma(C::T_ACCO + (j >> 1) * D, smem_u32(sm + C::O_ZO), aX1, it > 0);
-              umma_commit(bar_w);
-              ++pc;
+            if (!*sAbort) {
+              const uint32_t aSt = s0 + C::D_W + (C::RES ? sub_of(j) : c % C::D_NST) * C::A_BYTES;
+              const uint32_t tb = b * C::T_BUF3;
+              kmma(tb, aPu, BM, 0, aSt, SC, 0, D / 16, ID_N, false);
+              kmma(tb + SC, aPv, BM, 0, aSt + C::SUB_BYTES, SC, 0, D / 16, ID_N, false);
+              kmma(tb + 2 * SC, aDY, BM, 0, aSt + 2 * C::SUB_BYTES, SC, 0, D / 16, ID_N, false);
             }
-            if (j == nchunks - 1) umma_commit(bar_pf);
+            umma_commit(bar_a + b);
+            if (it < 3 && j < 8) OW_TR(1, it * 32 + 8 + j);
+            if (j == nsub - 1) umma_commit(bar_pf);
+            if (j > 0) dp(c - 1);
           }
         }
-        if (role == R_UV) {
+        if (total > 0) dp(total - 1);
+      } else if (role == R_UV) {
+        auto products = [&](int it) {  // dB_u^T[h] += dU_h^T P_u, dB_v^T[h] += dV_h^T P_v
+          const int x = (it + 1) * nsub - 1;
+          mbar_wait(bar_du + (x & 1), (x >> 1) & 1, sAbort);
+          tc_fence_after();
           if (!*sAbort) {
-            const uint32_t aS = smem_u32(sm + C::U_S);
-            mnmma(C::T_ACCU, aS, aPu, it > 0);
-            mnmma(C::T_ACCV, aS + 2 * C::Z_BYTES, aPv, it > 0);
+            const uint32_t aP = s0 + (it % NB_UV) * 3 * C::P_BYTES, aS = s0 + C::U_S;
+            mnmma(C::T_ACCU, aS, aP, it > 0);
+            mnmma(C::T_ACCV, aS + 2 * C::Z_BYTES, aP + C::P_BYTES, it > 0);
           }
           umma_commit(bar_w);
+        };
+        int c = 0;
+        for (int it = 0; it < nit; ++it) {
+          mbar_wait(bar_p + it % NB_UV, (it / NB_UV) & 1, sAbort);
+          if (it < 3) OW_TR(1, it * 32 + 20);
+          tc_fence_after();
+          const uint32_t aP = s0 + (it % NB_UV) * 3 * C::P_BYTES;
+          if (C::RES && it == 0) mbar_wait(bar_wf, 0, sAbort);
+          for (int j = 0; j < nsub; ++j, ++c) {
+            const int b = c & 1;
+            if (c >= 2) mbar_wait(bar_du + b, ((c - 2) >> 1) & 1, sAbort);  // TMEM buffer b read out
+            if (!C::RES) mbar_wait(bar_wf + b, (c >> 1) & 1, sAbort);
+            if (it < 3 && j < 3) OW_TR(1, it * 32 + 21 + j);
+            tc_fence_after();
+            if (!*sAbort) {
+              const uint32_t aSt = s0 + C::U_W + (C::RES ? sub_of(j) : b) * C::A_BYTES;
+              const uint32_t tb = b * C::T_BUF3;
+              kmma(tb, aP, BM, 0, aSt, SC, 0, D / 16, ID_N, false);
+              kmma(tb + SC, aP + C::P_BYTES, BM, 0, aSt + C::SUB_BYTES, SC, 0, D / 16, ID_N, false);
+              kmma(tb + 2 * SC, aP + 2 * C::P_BYTES, BM, 0, aSt + 2 * C::SUB_BYTES, SC, 0, D / 16, ID_N, false);
+            }
+            umma_commit(bar_a + b);
+            if (it < 3 && j < 8) OW_TR(1, it * 32 + 8 + j);
+            if (NB_UV == 2 && j == 0 && it > 0) products(it - 1);
+          }
+          if (NB_UV == 1) products(it);
         }
+        if (NB_UV == 2 && nit > 0) products(nit - 1);
+      } else {
+        const uint32_t aPu = s0 + C::OFF_PU, aPv = s0 + C::OFF_PV, aG = s0 + C::OFF_X1;
+        constexpr int SPP = 128 / SC;  // sub-chunks per 128-feature pair
+        int pc = 0;
+        auto y = [&](int x) {  // Y += Z_x B_o[x]; M_o[pair] += (A_o Z)^T G' once a pair is complete
+          const int bx = x & 1, jx = x % nsub, itx = x / nsub, kx = x / C::SPC;
+          mbar_wait(bar_du + bx, (x >> 1) & 1, sAbort);
+          if (!C::RES && x % C::SPC == 0) mbar_wait(bar_bo + (kx & 1), (kx >> 1) & 1, sAbort);
+          tc_fence_after();
+          if (!*sAbort) {
+            const uint32_t aZ = s0 + C::O_Z + buf_atom(bx, 1);
+            const uint32_t aBo = s0 + C::O_BO + (C::RES ? sub_of(jx) / C::SPC : kx & 1) * C::BO_BYTES;
+            kmma(C::T_Y, aZ, BM, buf_col(bx) / 16, aBo, D, (x % C::SPC) * (SC / 16), SC / 16, ID_ND, jx > 0);
+          }
+          umma_commit(bar_b + bx);
+          if (!C::RES && x % C::SPC == C::SPC - 1) umma_commit(bar_boe + (kx & 1));
+          if (jx == nsub - 1) umma_commit(bar_yd);
+          if (jx % SPP == SPP - 1) {
+            if (jx == SPP - 1) mbar_wait(bar_gl, itx & 1, sAbort);
+            mbar_wait(bar_zo, pc & 1, sAbort);
+            tc_fence_after();
+            if (!*sAbort) mnmma(C::T_ACCO + (sub_of(jx) / SPP) * D, s0 + C::O_ZO, aG, itx > 0);
+            umma_commit(bar_w);
+            ++pc;
+          }
+        };
+        int c = 0;
+        for (int it = 0; it < nit; ++it) {
+          if (c > 0) y(c - 1);  // finish the previous item before waiting for this one's operands
+          if (C::RES && it == 0) mbar_wait(bar_wf, 0, sAbort);
+          mbar_wait(bar_p, it & 1, sAbort);
+          if (it < 3) OW_TR(1, it * 32 + 20);
+          tc_fence_after();
+          for (int j = 0; j < nsub; ++j, ++c) {
+            const int b = c & 1;
+            if (!C::RES) mbar_wait(bar_wf + b, (c >> 1) & 1, sAbort);
+            if (it < 3 && j < 3) OW_TR(1, it * 32 + 21 + j);
+            tc_fence_after();
+            if (!*sAbort) {
+              const uint32_t aSt = s0 + C::O_W1 + (C::RES ? sub_of(j) : b) * 2 * C::SUB_BYTES;
+              const uint32_t tb = b * C::T_BUF2;
+              kmma(tb, aPu, BM, 0, aSt, SC, 0, D / 16, ID_N, false);
+              kmma(tb + SC, aPv, BM, 0, aSt + C::SUB_BYTES, SC, 0, D / 16, ID_N, false);
+            }
+            umma_commit(bar_a + b);
+            if (it < 3 && j < 8) OW_TR(1, it * 32 + 8 + j);
+            if (j == nsub - 1) umma_commit(bar_pf);
+            if (j > 0) y(c - 1);
+          }
+        }
+        if (total > 0) y(total - 1);
       }
     }
   } else {
     // ------------------------------------------------ compute warps
     const int tid = threadIdx.x;
     const int g = lane >> 2, t4 = lane & 3;
-    const int lq = warp & 3, cb = (warp >> 2) * 32;
+    const int lq = warp & 3, chh = warp >> 2;
     const int r = lq * 32 + lane;
     const uint32_t trow = tbase + ((uint32_t)(lq * 32) << 16);
+    const int cb = chh * HC;
     auto frag = [&](int m, bool tr, uint32_t (&f)[4]) { load_afrag(a.amat + m * 256, tr, g, t4, f); };
     float accA[2][2][4] = {};  // DGRAD: dA_u, dA_v ; O: dA_o in accA[0]
     int c = 0, pc = 0;
@@ -925,46 +1115,36 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
       const int qc = (int)(item / nMB);
       const float* ggq = a.gg + (int64_t)qc * D;
 
-      // ---- chunk loop
-      for (int j = 0; j < nchunks; ++j, ++c) {
-        mbar_wait(bar_a, c & 1, sAbort);
-        if (tid == 0 && it < 3 && j < 4) OW_TR(0, it * 32 + 2 * j);
+      // ---- sub-chunk loop
+      for (int j = 0; j < nsub; ++j, ++c) {
+        const int b = c & 1;
+        mbar_wait(bar_a + b, (c >> 1) & 1, sAbort);
+        if (tid == 0 && it < 3 && j < 8) OW_TR(0, it * 32 + j);
         __syncwarp();
         tc_fence_after();
-        uint32_t ur[32], vr[32], zr[32];
-        tmem_ld32(trow + C::T_U + cb, ur);
-        tmem_ld32(trow + C::T_V + cb, vr);
-        if (role != R_O) tmem_ld32(trow + C::T_DZ + cb, zr);
-        tmem_ld_wait();
-        if (role == R_DGRAD) {
-          if (j > 0) mbar_wait(bar_b, (c - 1) & 1, sAbort);  // dP(c-1) done with dU/dV
-          unsigned char* sdu = sm + C::D_S;
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
-            uint32_t wu[4], wv[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              float du[2], dv[2];
-#pragma unroll
-              for (int h2 = 0; h2 < 2; ++h2) {
-                const int i = jj * 8 + 2 * e + h2;
-                const float u = __uint_as_float(ur[i]), v = __uint_as_float(vr[i]), dz = __uint_as_float(zr[i]);
-                const float s = sigm_fast(u);
-                du[h2] = dz * v * s * (1.f + u * (1.f - s));
-                dv[h2] = dz * u * s;
-              }
-              wu[e] = pack2<BF16>(du[0], du[1]);
-              wv[e] = pack2<BF16>(dv[0], dv[1]);
-            }
-            const uint32_t off = sw128_off(r, cb + jj * 8, BM);
-            *reinterpret_cast<uint4*>(sdu + off) = make_uint4(wu[0], wu[1], wu[2], wu[3]);
-            *reinterpret_cast<uint4*>(sdu + C::Z_BYTES + off) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+        if (role != R_O) {
+          uint32_t ur[HC], vr[HC], zr[HC];
+          const uint32_t tcol = b * C::T_BUF3 + cb;
+          tmem_ld_cols<HC>(trow + tcol, ur);
+          tmem_ld_cols<HC>(trow + tcol + SC, vr);
+          tmem_ld_cols<HC>(trow + tcol + 2 * SC, zr);
+          tmem_ld_wait();
+          unsigned char* du_at;
+          int col0;
+          int dv_off;
+          if (role == R_DGRAD) {
+            if (c >= 2) mbar_wait(bar_b + b, ((c - 2) >> 1) & 1, sAbort);  // dP(c-2) read this buffer
+            du_at = sm + C::D_S + buf_atom(b, 2);
+            dv_off = C::Z_BYTES;
+            col0 = buf_col(b);
+          } else {
+            if (j == 0 && it > 0) mbar_wait(bar_w, (it - 1) & 1, sAbort);  // products read dU_h / dV_h
+            du_at = sm + C::U_S;
+            dv_off = 2 * C::Z_BYTES;
+            col0 = sub_of(j) * SC;
           }
-        } else if (role == R_UV) {
-          if (j == 0 && it > 0) mbar_wait(bar_w, (it - 1) & 1, sAbort);  // previous products read dU/dV
-          unsigned char* sdu = sm + C::U_S;
 #pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
+          for (int jj = 0; jj < HC / 8; ++jj) {
             uint32_t wu[4], wv[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
@@ -974,21 +1154,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
                 const int i = jj * 8 + 2 * e + h2;
                 const float u = __uint_as_float(ur[i]), v = __uint_as_float(vr[i]), dz = __uint_as_float(zr[i]);
                 const float s = sigm_fast(u);
-                du[h2] = dz * v * s * (1.f + u * (1.f - s));
-                dv[h2] = dz * u * s;
+                const float ds = dz * s;
+                dv[h2] = ds * u;
+                du[h2] = ds * v * fmaf(-u, s, u + 1.f);
               }
               wu[e] = pack2<BF16>(du[0], du[1]);
               wv[e] = pack2<BF16>(dv[0], dv[1]);
             }
-            const uint32_t off = sw128_off(r, j * 64 + cb + jj * 8, BM);
-            *reinterpret_cast<uint4*>(sdu + off) = make_uint4(wu[0], wu[1], wu[2], wu[3]);
-            *reinterpret_cast<uint4*>(sdu + 2 * C::Z_BYTES + off) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            const uint32_t off = sw128_off(r, col0 + cb + jj * 8, BM);
+            *reinterpret_cast<uint4*>(du_at + off) = make_uint4(wu[0], wu[1], wu[2], wu[3]);
+            *reinterpret_cast<uint4*>(du_at + dv_off + off) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
           }
         } else {  // R_O: Z = silu(U) * V
-          if (j > 0) mbar_wait(bar_b, (c - 1) & 1, sAbort);  // Y(c-1) done with Z
-          unsigned char* sz = sm + C::O_Z;
+          uint32_t ur[HC], vr[HC];
+          const uint32_t tcol = b * C::T_BUF2 + cb;
+          tmem_ld_cols<HC>(trow + tcol, ur);
+          tmem_ld_cols<HC>(trow + tcol + SC, vr);
+          tmem_ld_wait();
+          if (c >= 2) mbar_wait(bar_b + b, ((c - 2) >> 1) & 1, sAbort);  // Y(c-2) read this buffer
+          unsigned char* sz = sm + C::O_Z + buf_atom(b, 1);
 #pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
+          for (int jj = 0; jj < HC / 8; ++jj) {
             uint32_t wz[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
@@ -997,47 +1183,48 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
               const uint32_t v2 = pack2<BF16>(__uint_as_float(vr[i0]), __uint_as_float(vr[i0 + 1]));
               wz[e] = silu_mul2<BF16>(u2, v2);
             }
-            *reinterpret_cast<uint4*>(sz + sw128_off(r, cb + jj * 8, BM)) = make_uint4(wz[0], wz[1], wz[2], wz[3]);
+            *reinterpret_cast<uint4*>(sz + sw128_off(r, buf_col(b) + cb + jj * 8, BM)) =
+                make_uint4(wz[0], wz[1], wz[2], wz[3]);
           }
         }
         fence_proxy_async_smem();
         tc_fence_before();
-        if (tid == 0 && it < 3 && j < 4) OW_TR(0, it * 32 + 2 * j + 1);
-        mbar_arrive(bar_du);
+        if (tid == 0 && it < 3 && j < 8) OW_TR(0, it * 32 + 8 + j);
+        mbar_arrive(bar_du + b);
         if (role == R_O) {
-          // Zo chunk = A_o Z into the pair buffer (atom j & 1).
-          if ((j & 1) == 0 && (it > 0 || j > 0)) mbar_wait(bar_w, (pc - 1) & 1, sAbort);
+          // (A_o Z) of this sub-chunk into the pair buffer at feature offset fo.
+          const int fo = (j % (128 / SC)) * SC;
+          if (fo == 0 && pc > 0) mbar_wait(bar_w, (pc - 1) & 1, sAbort);  // previous pair's M_o read it
           comp_sync();
           __syncwarp();
-          const unsigned char* sz = sm + C::O_Z;
+          const unsigned char* sz = sm + C::O_Z + buf_atom(b, 1);
           unsigned char* szo = sm + C::O_ZO;
           uint32_t fAo[4];
           frag(2, false, fAo);
 #pragma unroll
-          for (int np = 0; np < 4; ++np) {
-            const int rowr = warp * 16 + (lane & 15), colr = np * 16 + (lane >> 4) * 8;
+          for (int np = 0; np < SC / 16; ++np) {
+            const int rowr = warp * 16 + (lane & 15), colr = buf_col(b) + np * 16 + (lane >> 4) * 8;
             uint32_t b0, b1, b2, b3;
             ldsm_x4_trans(smem_u32(sz + sw128_off(rowr, colr, BM)), b0, b1, b2, b3);
             float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
             mma16816<BF16>(c0, fAo, b0, b1);
             mma16816<BF16>(c1, fAo, b2, b3);
-            const int r0 = warp * 16 + g, k0 = (j & 1) * 64 + np * 16 + 2 * t4;
+            const int r0 = warp * 16 + g, k0 = fo + np * 16 + 2 * t4;
             *reinterpret_cast<uint32_t*>(szo + sw128_off(r0, k0, BM)) = pack2<BF16>(c0[0], c0[1]);
             *reinterpret_cast<uint32_t*>(szo + sw128_off(r0 + 8, k0, BM)) = pack2<BF16>(c0[2], c0[3]);
             *reinterpret_cast<uint32_t*>(szo + sw128_off(r0, k0 + 8, BM)) = pack2<BF16>(c1[0], c1[1]);
             *reinterpret_cast<uint32_t*>(szo + sw128_off(r0 + 8, k0 + 8, BM)) = pack2<BF16>(c1[2], c1[3]);
           }
-          if (j & 1) {
+          if (fo + SC == 128) {
             fence_proxy_async_smem();
             mbar_arrive(bar_zo);
             ++pc;
           }
-          comp_sync();  // every warp is done reading Z before it is rewritten
         }
       }
 
       // ---- per-item epilogue
-      if (tid == 0 && it < 3) OW_TR(0, it * 32 + 8);
+      if (tid == 0 && it < 3) OW_TR(0, it * 32 + 16);
       if (role == R_DGRAD) {
         // Metadata of this item for the dX scatter.
         if (tid < BM) sRow[tid] = mreg.row;
@@ -1046,112 +1233,148 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
         comp_sync();
         if (it + 1 < nit) mreg = meta_issue(it + 1);
         const bool cont = *sCont != 0;
-        mbar_wait(bar_b, (c - 1) & 1, sAbort);  // last dP done
-        mbar_wait(bar_t, it & 1, sAbort);       // T image of this item loaded
-        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 9);
+        mbar_wait(bar_b + ((c - 1) & 1), ((c - 1) >> 1) & 1, sAbort);  // last dP of the item done
+        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 17);
         __syncwarp();
         tc_fence_after();
         // Warp (lq, hw): tiles 2lq, 2lq+1 (TMEM lanes 32lq..32lq+31), channels
         // [hw*D/2, (hw+1)*D/2).  dP arrives in the mma C-fragment layout.
+        constexpr int NP = D / 32;
         const int hw = warp >> 2;
-        const uint32_t aT = smem_u32(sm + C::D_S);
-        uint32_t fuT[4], fvT[4];
-        frag(0, true, fuT);
-        frag(1, true, fvT);
+        // Pass 1: dT = A_u^T dP_u + A_v^T dP_v -> dX (needs no T).
+        {
+          uint32_t fuT[4], fvT[4];
+          frag(0, true, fuT);
+          frag(1, true, fvT);
 #pragma unroll 1
-        for (int tl = 0; tl < 2; ++tl) {
-          const int tile = 2 * lq + tl;
-          const int rwA = sRow[tile * 16 + g], rwB = sRow[tile * 16 + g + 8];
-          const uint32_t tl_addr = tbase + ((uint32_t)(tile * 16) << 16);
-#pragma unroll 1
-          for (int np = 0; np < D / 32; ++np) {
-            const int k0 = hw * (D / 2) + np * 16;
-            uint32_t pu[8], pv[8];
-            tmem_ld16x256_x2(tl_addr + C::T_DPU + k0, pu);
-            tmem_ld16x256_x2(tl_addr + C::T_DPV + k0, pv);
+          for (int tl = 0; tl < 2; ++tl) {
+            const int tile = 2 * lq + tl;
+            const int rwA = sRow[tile * 16 + g], rwB = sRow[tile * 16 + g + 8];
+            const uint32_t tl_addr = tbase + ((uint32_t)(tile * 16) << 16);
+            uint32_t pu[NP][8], pv[NP][8];
+#pragma unroll
+            for (int np = 0; np < NP; ++np) {
+              const int k0 = hw * (D / 2) + np * 16;
+              tmem_ld16x256_x2(tl_addr + C::T_DPU + k0, pu[np]);
+              tmem_ld16x256_x2(tl_addr + C::T_DPV + k0, pv[np]);
+            }
             tmem_ld_wait();
-            // A fragments (rows = tokens, k = channels k0..k0+15) of dP_u, dP_v
-            uint32_t au[4], av[4];
-            au[0] = pack2<BF16>(__uint_as_float(pu[0]), __uint_as_float(pu[1]));
-            au[1] = pack2<BF16>(__uint_as_float(pu[2]), __uint_as_float(pu[3]));
-            au[2] = pack2<BF16>(__uint_as_float(pu[4]), __uint_as_float(pu[5]));
-            au[3] = pack2<BF16>(__uint_as_float(pu[6]), __uint_as_float(pu[7]));
-            av[0] = pack2<BF16>(__uint_as_float(pv[0]), __uint_as_float(pv[1]));
-            av[1] = pack2<BF16>(__uint_as_float(pv[2]), __uint_as_float(pv[3]));
-            av[2] = pack2<BF16>(__uint_as_float(pv[4]), __uint_as_float(pv[5]));
-            av[3] = pack2<BF16>(__uint_as_float(pv[6]), __uint_as_float(pv[7]));
-            // dA += dP T^T : B[k = channel][n = token j] = T[j][k] (T image, SW128)
-            uint32_t tb[4];
-            ldsm_x4(aT + sw128_off(tile * 16 + (lane & 7) + (lane >> 4) * 8, k0 + ((lane >> 3) & 1) * 8, BM),
-                    tb[0], tb[1], tb[2], tb[3]);
-            mma16816<BF16>(accA[0][0], au, tb[0], tb[1]);
-            mma16816<BF16>(accA[0][1], au, tb[2], tb[3]);
-            mma16816<BF16>(accA[1][0], av, tb[0], tb[1]);
-            mma16816<BF16>(accA[1][1], av, tb[2], tb[3]);
-            // dT = A_u^T dP_u + A_v^T dP_v : B fragments = transposed 8x8 blocks
+            if (tid == 0 && it < 3) OW_TR(0, it * 32 + 20 + 2 * tl);
 #pragma unroll
-            for (int nb = 0; nb < 2; ++nb) {
-              const uint32_t bu0 = movm_trans(au[2 * nb]), bu1 = movm_trans(au[2 * nb + 1]);
-              const uint32_t bv0 = movm_trans(av[2 * nb]), bv1 = movm_trans(av[2 * nb + 1]);
-              float cc[4] = {0.f, 0.f, 0.f, 0.f};
-              mma16816<BF16>(cc, fuT, bu0, bu1);
-              mma16816<BF16>(cc, fvT, bv0, bv1);
-              const int k = k0 + nb * 8 + 2 * t4;
+            for (int np = 0; np < NP; ++np) {
+              const int k0 = hw * (D / 2) + np * 16;
+              uint32_t au[4], av[4];
 #pragma unroll
-              for (int hr = 0; hr < 2; ++hr) {
-                const int rw = hr ? rwB : rwA;
-                if (rw < 0) continue;
-                const int64_t row = rw;
-                const float d0 = cc[2 * hr], d1 = cc[2 * hr + 1];
-                if (cont) {
-                  const int64_t off = row * p.C + sCh[0] + k;
-                  if (a.dxn) {
-                    *reinterpret_cast<float2*>(a.dxn + off) = make_float2(d0, d1);
-                  } else if constexpr (std::is_same_v<TX, float>) {
-                    *reinterpret_cast<float2*>((float*)a.dx + off) = make_float2(d0, d1);
+              for (int q = 0; q < 4; ++q) {
+                au[q] = pack2<BF16>(__uint_as_float(pu[np][2 * q]), __uint_as_float(pu[np][2 * q + 1]));
+                av[q] = pack2<BF16>(__uint_as_float(pv[np][2 * q]), __uint_as_float(pv[np][2 * q + 1]));
+              }
+#pragma unroll
+              for (int nb = 0; nb < 2; ++nb) {
+                const uint32_t bu0 = movm_trans(au[2 * nb]), bu1 = movm_trans(au[2 * nb + 1]);
+                const uint32_t bv0 = movm_trans(av[2 * nb]), bv1 = movm_trans(av[2 * nb + 1]);
+                float cc[4] = {0.f, 0.f, 0.f, 0.f};
+                mma16816<BF16>(cc, fuT, bu0, bu1);
+                mma16816<BF16>(cc, fvT, bv0, bv1);
+                const int k = k0 + nb * 8 + 2 * t4;
+#pragma unroll
+                for (int hr = 0; hr < 2; ++hr) {
+                  const int rw = hr ? rwB : rwA;
+                  if (rw < 0) continue;
+                  const int64_t row = rw;
+                  const float d0 = cc[2 * hr], d1 = cc[2 * hr + 1];
+                  if (cont) {
+                    const int64_t off = row * p.C + sCh[0] + k;
+                    if (a.dxn) {
+                      *reinterpret_cast<float2*>(a.dxn + off) = make_float2(d0, d1);
+                    } else if constexpr (std::is_same_v<TX, float>) {
+                      *reinterpret_cast<float2*>((float*)a.dx + off) = make_float2(d0, d1);
+                    } else {
+                      *reinterpret_cast<uint32_t*>((TX*)a.dx + off) =
+                          pack2<std::is_same_v<TX, __nv_bfloat16>>(d0, d1);
+                    }
                   } else {
-                    *reinterpret_cast<uint32_t*>((TX*)a.dx + off) = pack2<std::is_same_v<TX, __nv_bfloat16>>(d0, d1);
-                  }
-                } else {
 #pragma unroll
-                  for (int e = 0; e < 2; ++e) {
-                    const int ch = sCh[k + e];
-                    if (ch >= p.C) continue;
-                    const int64_t off = row * p.C + ch;
-                    const float dv = e ? d1 : d0;
-                    if (a.dxn) a.dxn[off] = dv;
-                    else ((TX*)a.dx)[off] = Elem<TX>::from(dv);
+                    for (int e = 0; e < 2; ++e) {
+                      const int ch = sCh[k + e];
+                      if (ch >= p.C) continue;
+                      const int64_t off = row * p.C + ch;
+                      const float dv = e ? d1 : d0;
+                      if (a.dxn) a.dxn[off] = dv;
+                      else ((TX*)a.dx)[off] = Elem<TX>::from(dv);
+                    }
                   }
                 }
               }
             }
+            if (tid == 0 && it < 3) OW_TR(0, it * 32 + 21 + 2 * tl);
           }
         }
-        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 10);
+        // Pass 2: dA_u += dP_u T^T, dA_v += dP_v T^T with T from its image.
+        mbar_wait(bar_t, it & 1, sAbort);
+        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 18);
+        __syncwarp();
+        {
+          const uint32_t aT = smem_u32(sm + C::D_TT);
+#pragma unroll 1
+          for (int tl = 0; tl < 2; ++tl) {
+            const int tile = 2 * lq + tl;
+            const uint32_t tl_addr = tbase + ((uint32_t)(tile * 16) << 16);
+            uint32_t pu[NP][8], pv[NP][8];
+#pragma unroll
+            for (int np = 0; np < NP; ++np) {
+              const int k0 = hw * (D / 2) + np * 16;
+              tmem_ld16x256_x2(tl_addr + C::T_DPU + k0, pu[np]);
+              tmem_ld16x256_x2(tl_addr + C::T_DPV + k0, pv[np]);
+            }
+            tmem_ld_wait();
+#pragma unroll
+            for (int np = 0; np < NP; ++np) {
+              const int k0 = hw * (D / 2) + np * 16;
+              uint32_t au[4], av[4];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                au[q] = pack2<BF16>(__uint_as_float(pu[np][2 * q]), __uint_as_float(pu[np][2 * q + 1]));
+                av[q] = pack2<BF16>(__uint_as_float(pv[np][2 * q]), __uint_as_float(pv[np][2 * q + 1]));
+              }
+              // B[k = channel][n = token j] = T[j][k]
+              uint32_t tb[4];
+              ldsm_x4(aT + sw128_off(tile * 16 + (lane & 7) + (lane >> 4) * 8, k0 + ((lane >> 3) & 1) * 8, BM),
+                      tb[0], tb[1], tb[2], tb[3]);
+              mma16816<BF16>(accA[0][0], au, tb[0], tb[1]);
+              mma16816<BF16>(accA[0][1], au, tb[2], tb[3]);
+              mma16816<BF16>(accA[1][0], av, tb[0], tb[1]);
+              mma16816<BF16>(accA[1][1], av, tb[2], tb[3]);
+            }
+          }
+        }
+        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 19);
         tc_fence_before();
-        mbar_arrive(bar_epd);
-        comp_sync();  // T (in the dU/dV region) and the metadata are read out
+        mbar_arrive(bar_epd);  // T region free for the next item's T
+        comp_sync();  // T and the metadata are read out
       } else if (role == R_O) {
-        mbar_wait(bar_b, (c - 1) & 1, sAbort);   // Y complete
-        mbar_wait(bar_gl, it & 1, sAbort);      // G' of this item present
-        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 9);
+        mbar_wait(bar_yd, it & 1, sAbort);        // Y complete
+        mbar_wait(bar_w, (pc - 1) & 1, sAbort);   // last M_o done with the pair buffer
+        mbar_wait(bar_gl, it & 1, sAbort);        // G' of this item present
+        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 17);
         __syncwarp();
         tc_fence_after();
-        unsigned char* stY = sm + C::O_STG;
-        const uint32_t aY = smem_u32(stY), aG = smem_u32(sX1);
+        unsigned char* stY = sm + C::O_ZO;
+        const uint32_t aY = smem_u32(stY), aG = smem_u32(sm + C::OFF_X1);
+        const int cb32 = chh * 32;
         for (int hf = 0; hf < D / 64; ++hf) {
           uint32_t yr[32];
-          tmem_ld32(trow + C::T_Y + hf * 64 + cb, yr);
+          tmem_ld32(trow + C::T_Y + hf * 64 + cb32, yr);
           tmem_ld_wait();
 #pragma unroll
           for (int jj = 0; jj < 4; ++jj) {
             uint4 w;
-            const int k = hf * 64 + cb + jj * 8;
+            const int k = hf * 64 + cb32 + jj * 8;
             w.x = pack2<BF16>(__uint_as_float(yr[jj * 8 + 0]) * ggq[k + 0], __uint_as_float(yr[jj * 8 + 1]) * ggq[k + 1]);
             w.y = pack2<BF16>(__uint_as_float(yr[jj * 8 + 2]) * ggq[k + 2], __uint_as_float(yr[jj * 8 + 3]) * ggq[k + 3]);
             w.z = pack2<BF16>(__uint_as_float(yr[jj * 8 + 4]) * ggq[k + 4], __uint_as_float(yr[jj * 8 + 5]) * ggq[k + 5]);
             w.w = pack2<BF16>(__uint_as_float(yr[jj * 8 + 6]) * ggq[k + 6], __uint_as_float(yr[jj * 8 + 7]) * ggq[k + 7]);
-            *reinterpret_cast<uint4*>(stY + (r * STG_LD + cb + jj * 8) * 2) = w;
+            *reinterpret_cast<uint4*>(stY + (r * STG_LD + cb32 + jj * 8) * 2) = w;
           }
           comp_sync();
           __syncwarp();
@@ -1160,7 +1383,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           gram16<BF16>(accA[0], rowG, rowY, lane);
           comp_sync();
         }
-        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 10);
+        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 19);
         tc_fence_before();
         mbar_arrive(bar_epd);
       }
@@ -1184,14 +1407,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
       else mbar_wait(bar_w, (pc - 1) & 1, sAbort);
       __syncwarp();
       tc_fence_after();
+      const int cb32 = chh * 32;
       if (role == R_UV) {
         float* dst = a.puv + (int64_t)wslot * 2 * 128 * D;
         for (int m = 0; m < 2; ++m)
           for (int c0 = 0; c0 < D; c0 += 64) {
             uint32_t vr[32];
-            tmem_ld32(trow + (m ? C::T_ACCV : C::T_ACCU) + c0 + cb, vr);
+            tmem_ld32(trow + (m ? C::T_ACCV : C::T_ACCU) + c0 + cb32, vr);
             tmem_ld_wait();
-            float* o = dst + ((int64_t)m * 128 + r) * D + c0 + cb;
+            float* o = dst + ((int64_t)m * 128 + r) * D + c0 + cb32;
 #pragma unroll
             for (int i = 0; i < 32; i += 4)
               *reinterpret_cast<float4*>(o + i) = make_float4(__uint_as_float(vr[i]), __uint_as_float(vr[i + 1]),
@@ -1202,9 +1426,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
         for (int hb = 0; hb < C::NH; ++hb)
           for (int c0 = 0; c0 < D; c0 += 64) {
             uint32_t vr[32];
-            tmem_ld32(trow + C::T_ACCO + hb * D + c0 + cb, vr);
+            tmem_ld32(trow + C::T_ACCO + hb * D + c0 + cb32, vr);
             tmem_ld_wait();
-            float* o = dst + ((int64_t)hb * 128 + r) * D + c0 + cb;
+            float* o = dst + ((int64_t)hb * 128 + r) * D + c0 + cb32;
 #pragma unroll
             for (int i = 0; i < 32; i += 4)
               *reinterpret_cast<float4*>(o + i) = make_float4(__uint_as_float(vr[i]), __uint_as_float(vr[i + 1]),
@@ -1367,7 +1591,7 @@ int tc_backward_t(const ow_bigemm_args_t* ar, const ow_bigemm_grads_t* gr, const
 
   // Weight images.
   {
-    const int64_t n = 6LL * p.Qc * D * 2 * D;
+    const int64_t n = 4LL * p.Qc * 2 * D * D;
     const int grid = (int)std::min<int64_t>((n + 255) / 256, 148 * 8);
     auto run = [&](auto* tw) {
       using TW = std::remove_pointer_t<decltype(tw)>;
@@ -1392,9 +1616,16 @@ int tc_backward_t(const ow_bigemm_args_t* ar, const ow_bigemm_grads_t* gr, const
     using TO = std::remove_pointer_t<decltype(to)>;
     const int64_t items = (int64_t)p.Qc * ((p.BQ() + 7) / 8);
     if (items > 0) {
-      constexpr int pack_smem = STG_BYTES + (BM + D) * 4 + 128;
+      constexpr int pack_smem = 3 * BM * 128 + STG_BYTES + (BM + D) * 4 + 128;
+      auto pk = tc_pack_kernel<D, BF16, TX, TO>;
+      cudaError_t pe = cudaFuncSetAttribute(pk, cudaFuncAttributeMaxDynamicSharedMemorySize, pack_smem);
+      if (pe != cudaSuccess) {
+        set_error("tc backward: cannot reserve %d bytes of shared memory for the pack kernel: %s", pack_smem,
+                  cudaGetErrorString(pe));
+        return OW_ERR_CUDA;
+      }
       profile_mark(OW_PROF_PACK, false, st);
-      launch(tc_pack_kernel<D, BF16, TX, TO>, (int)items, NCOMP, pack_smem, st, a);
+      launch(pk, (int)items, NCOMP, pack_smem, st, a);
       profile_mark(OW_PROF_PACK, true, st);
       OW_CHECK_LAUNCH("tc_pack_kernel");
     }
