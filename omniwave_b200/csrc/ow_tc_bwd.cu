@@ -40,6 +40,7 @@
 // warp that owns TMEM, one producer warp issuing the bulk copies.
 
 #include <algorithm>
+#include <cmath>
 #include <type_traits>
 
 #include "ow_common.cuh"
@@ -110,12 +111,11 @@ struct BCfg {
   static constexpr int U_S = U_NB * 3 * P_BYTES;
   static constexpr int U_W = U_S + 4 * Z_BYTES;
   static constexpr int U_END = U_W + 2 * A_BYTES;
-  // O: P_u | P_v | G', two Z buffers, the (A_o Z) buffer of 128 features
-  // (reused for Y staging in the epilogue), two [B_u | B_v] stages, two B_o stages.
-  static constexpr int O_Z = 3 * P_BYTES;
-  static constexpr int ZB_BYTES = 2 * BM * SC * 2;
-  static constexpr int O_ZO = O_Z + ZB_BYTES;
-  static constexpr int O_W1 = O_ZO + 2 * Z_BYTES;
+  // O: P_u | P_v | H | G', the Z of one 128-feature pair (M_o reads it
+  // directly; Y staging in the epilogue), two [B_u | B_v] stages, two B_o stages.
+  static constexpr int O_G = 3 * P_BYTES;                    // G' (H sits at OFF_X1)
+  static constexpr int O_ZP = 4 * P_BYTES;                   // Z of one 128-feature pair
+  static constexpr int O_W1 = O_ZP + 2 * Z_BYTES;
   static constexpr int O_BO = O_W1 + 4 * SUB_BYTES;
   static constexpr int O_END = O_BO + 2 * BO_BYTES;
   static constexpr int MAX_END = D_END > U_END ? (D_END > O_END ? D_END : O_END) : (U_END > O_END ? U_END : O_END);
@@ -146,12 +146,14 @@ struct BPlan {
   BPlan(const Prob& p, bool block, int sms) {
     using C = BCfg<D>;
     nH = C::NH;
-    // Split one wave of CTAs across the roles, weighed by the work each
-    // role has per item (a UV half item has half the chunks).
-    const double wD = 1.0, wU = (D == 64 ? 1.0 : 0.8) * nH, wO = 1.0, tot = wD + wU + wO;
+    // Split one wave of CTAs across the roles in proportion to each role's
+    // time per item (UV summed over its halves), as measured on B200 with the
+    // kernel's timeline trace: DGRAD : UV : O = 1 : 0.67 : 0.59 at d = 64 and
+    // 1 : 0.90 : 0.76 at d = 128.
+    const double wD = 1.0, wU = D == 64 ? 0.67 : 0.90, wO = D == 64 ? 0.59 : 0.76, tot = wD + wU + wO;
     const int64_t nMB = (p.BQ() + 7) / 8;
-    nUVq = std::max(1, (int)(sms * (wU / nH) / tot) / p.Qc);
-    nOq = std::max(1, (int)(sms * wO / tot) / p.Qc);
+    nUVq = std::max(1, (int)std::lround(sms * wU / tot / (nH * p.Qc)));
+    nOq = std::max(1, (int)std::lround(sms * wO / tot / p.Qc));
     nUVq = (int)std::min<int64_t>(nUVq, nMB);
     nOq = (int)std::min<int64_t>(nOq, nMB);
     nD = std::max(1, sms - nH * p.Qc * nUVq - p.Qc * nOq);
@@ -672,10 +674,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
   uint64_t* bar_tf = bars + 19;   // DGRAD: last dP of the item done (commit)
   uint64_t* bar_t = bars + 20;    // DGRAD: T image loaded (tx)
   uint64_t* bar_w = bars + 21;    // UV: products of an item done; O: M_o of a pair done (commit)
-  uint64_t* bar_zo = bars + 22;   // O: (A_o Z) of a 128-feature pair written
   uint64_t* bar_yd = bars + 23;   // O: Y of the item complete (commit)
-  uint64_t* bar_epd = bars + 24;  // O: epilogue done with G' and the staging buffer
-  uint64_t* bar_gl = bars + 25;   // O: G' loaded (tx)
+  uint64_t* bar_epd = bars + 24;  // epilogue done (DGRAD: T; O: H, G' and the staging buffer)
+  uint64_t* bar_gl = bars + 25;   // O: H and G' loaded (tx)
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + C::NBARS);
   volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
 
@@ -745,7 +746,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
     mbar_init(bar_tf, 1);
     mbar_init(bar_t, 1);
     mbar_init(bar_w, 1);
-    mbar_init(bar_zo, NCOMP);
     mbar_init(bar_yd, 1);
     mbar_init(bar_epd, NCOMP);
     mbar_init(bar_gl, 1);
@@ -864,9 +864,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           mbar_arrive_expect_tx(bar_p, 2 * C::P_BYTES);
           bulk_g2s(sm, item_src(it), 2 * C::P_BYTES, bar_p);
         };
-        auto load_g = [&](int it) {
-          mbar_arrive_expect_tx(bar_gl, C::P_BYTES);
-          bulk_g2s(sm + C::OFF_X1, item_src(it) + C::PK_G * C::P_BYTES, C::P_BYTES, bar_gl);
+        auto load_g = [&](int it) {  // H | G' (adjacent in the packed item)
+          mbar_arrive_expect_tx(bar_gl, 2 * C::P_BYTES);
+          bulk_g2s(sm + C::OFF_X1, item_src(it) + C::PK_H * C::P_BYTES, 2 * C::P_BYTES, bar_gl);
         };
         auto load_w1 = [&](int c) {
           { const int i_ = c / nsub, j_ = c % nsub; if (i_ < 3 && j_ < 6) OW_TR(2, i_ * 32 + 26 + j_); }
@@ -958,6 +958,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
         int c = 0, epoch = 0;
         for (int it = 0; it < nit; ++it) {
           if (c > 0) dp(c - 1);  // finish the previous item before waiting for this one's operands
+          // The epilogue's warp-level MMAs share the tensor pipe: let them run
+          // before this item's first UMMAs are queued.
+          if (it > 0) mbar_wait(bar_epd, (it - 1) & 1, sAbort);
           if (C::RES) {
             if (it > 0 && item_of(it) / nMB != item_of(it - 1) / nMB) {
               umma_commit(bar_we);  // resident weights of the previous group no longer read
@@ -1027,34 +1030,34 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
         }
         if (NB_UV == 2 && nit > 0) products(nit - 1);
       } else {
-        const uint32_t aPu = s0 + C::OFF_PU, aPv = s0 + C::OFF_PV, aG = s0 + C::OFF_X1;
+        const uint32_t aPu = s0 + C::OFF_PU, aPv = s0 + C::OFF_PV, aH = s0 + C::OFF_X1, aZP = s0 + C::O_ZP;
         constexpr int SPP = 128 / SC;  // sub-chunks per 128-feature pair
-        int pc = 0;
-        auto y = [&](int x) {  // Y += Z_x B_o[x]; M_o[pair] += (A_o Z)^T G' once a pair is complete
+        auto y = [&](int x) {  // Y += Z_x B_o[x]; M_o[pair] += Z_pair^T H once a pair is complete
           const int bx = x & 1, jx = x % nsub, itx = x / nsub, kx = x / C::SPC;
-          mbar_wait(bar_du + bx, (x >> 1) & 1, sAbort);
+          mbar_wait(bar_du + bx, (x >> 1) & 1, sAbort);  // Z_x in the pair buffer
           if (!C::RES && x % C::SPC == 0) mbar_wait(bar_bo + (kx & 1), (kx >> 1) & 1, sAbort);
           tc_fence_after();
           if (!*sAbort) {
-            const uint32_t aZ = s0 + C::O_Z + buf_atom(bx, 1);
             const uint32_t aBo = s0 + C::O_BO + (C::RES ? sub_of(jx) / C::SPC : kx & 1) * C::BO_BYTES;
-            kmma(C::T_Y, aZ, BM, buf_col(bx) / 16, aBo, D, (x % C::SPC) * (SC / 16), SC / 16, ID_ND, jx > 0);
+            kmma(C::T_Y, aZP, BM, (jx % SPP) * (SC / 16), aBo, D, (x % C::SPC) * (SC / 16), SC / 16, ID_ND, jx > 0);
           }
-          umma_commit(bar_b + bx);
           if (!C::RES && x % C::SPC == C::SPC - 1) umma_commit(bar_boe + (kx & 1));
           if (jx == nsub - 1) umma_commit(bar_yd);
           if (jx % SPP == SPP - 1) {
-            if (jx == SPP - 1) mbar_wait(bar_gl, itx & 1, sAbort);
-            mbar_wait(bar_zo, pc & 1, sAbort);
-            tc_fence_after();
-            if (!*sAbort) mnmma(C::T_ACCO + (sub_of(jx) / SPP) * D, s0 + C::O_ZO, aG, itx > 0);
+            if (jx == SPP - 1) {
+              mbar_wait(bar_gl, itx & 1, sAbort);  // H of this item
+              tc_fence_after();
+            }
+            if (!*sAbort) mnmma(C::T_ACCO + (sub_of(jx) / SPP) * D, aZP, aH, itx > 0);
             umma_commit(bar_w);
-            ++pc;
           }
         };
         int c = 0;
         for (int it = 0; it < nit; ++it) {
           if (c > 0) y(c - 1);  // finish the previous item before waiting for this one's operands
+          // The epilogue's warp-level MMAs share the tensor pipe: let them run
+          // before this item's first UMMAs are queued.
+          if (it > 0) mbar_wait(bar_epd, (it - 1) & 1, sAbort);
           if (C::RES && it == 0) mbar_wait(bar_wf, 0, sAbort);
           mbar_wait(bar_p, it & 1, sAbort);
           if (it < 3) OW_TR(1, it * 32 + 20);
@@ -1129,6 +1132,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           tmem_ld_cols<HC>(trow + tcol + SC, vr);
           tmem_ld_cols<HC>(trow + tcol + 2 * SC, zr);
           tmem_ld_wait();
+          if (tid == 0 && it < 3 && j < 4) OW_TR(0, it * 32 + 24 + j);
           unsigned char* du_at;
           int col0;
           int dv_off;
@@ -1165,14 +1169,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
             *reinterpret_cast<uint4*>(du_at + off) = make_uint4(wu[0], wu[1], wu[2], wu[3]);
             *reinterpret_cast<uint4*>(du_at + dv_off + off) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
           }
-        } else {  // R_O: Z = silu(U) * V
+        } else {  // R_O: Z = silu(U) * V into the pair buffer at feature offset fo
           uint32_t ur[HC], vr[HC];
           const uint32_t tcol = b * C::T_BUF2 + cb;
           tmem_ld_cols<HC>(trow + tcol, ur);
           tmem_ld_cols<HC>(trow + tcol + SC, vr);
           tmem_ld_wait();
-          if (c >= 2) mbar_wait(bar_b + b, ((c - 2) >> 1) & 1, sAbort);  // Y(c-2) read this buffer
-          unsigned char* sz = sm + C::O_Z + buf_atom(b, 1);
+          const int fo = (j % (128 / SC)) * SC;
+          // The previous pair's M_o (issued after its Y MMAs) has read the buffer.
+          if (fo == 0 && pc > 0) mbar_wait(bar_w, (pc - 1) & 1, sAbort);
+          unsigned char* sz = sm + C::O_ZP;
 #pragma unroll
           for (int jj = 0; jj < HC / 8; ++jj) {
             uint32_t wz[4];
@@ -1183,44 +1189,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
               const uint32_t v2 = pack2<BF16>(__uint_as_float(vr[i0]), __uint_as_float(vr[i0 + 1]));
               wz[e] = silu_mul2<BF16>(u2, v2);
             }
-            *reinterpret_cast<uint4*>(sz + sw128_off(r, buf_col(b) + cb + jj * 8, BM)) =
+            *reinterpret_cast<uint4*>(sz + sw128_off(r, fo + cb + jj * 8, BM)) =
                 make_uint4(wz[0], wz[1], wz[2], wz[3]);
           }
+          if (fo + SC == 128) ++pc;
         }
+        if (tid == 0 && it < 3 && j < 4) OW_TR(0, it * 32 + 28 + j);
         fence_proxy_async_smem();
         tc_fence_before();
         if (tid == 0 && it < 3 && j < 8) OW_TR(0, it * 32 + 8 + j);
         mbar_arrive(bar_du + b);
-        if (role == R_O) {
-          // (A_o Z) of this sub-chunk into the pair buffer at feature offset fo.
-          const int fo = (j % (128 / SC)) * SC;
-          if (fo == 0 && pc > 0) mbar_wait(bar_w, (pc - 1) & 1, sAbort);  // previous pair's M_o read it
-          comp_sync();
-          __syncwarp();
-          const unsigned char* sz = sm + C::O_Z + buf_atom(b, 1);
-          unsigned char* szo = sm + C::O_ZO;
-          uint32_t fAo[4];
-          frag(2, false, fAo);
-#pragma unroll
-          for (int np = 0; np < SC / 16; ++np) {
-            const int rowr = warp * 16 + (lane & 15), colr = buf_col(b) + np * 16 + (lane >> 4) * 8;
-            uint32_t b0, b1, b2, b3;
-            ldsm_x4_trans(smem_u32(sz + sw128_off(rowr, colr, BM)), b0, b1, b2, b3);
-            float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
-            mma16816<BF16>(c0, fAo, b0, b1);
-            mma16816<BF16>(c1, fAo, b2, b3);
-            const int r0 = warp * 16 + g, k0 = fo + np * 16 + 2 * t4;
-            *reinterpret_cast<uint32_t*>(szo + sw128_off(r0, k0, BM)) = pack2<BF16>(c0[0], c0[1]);
-            *reinterpret_cast<uint32_t*>(szo + sw128_off(r0 + 8, k0, BM)) = pack2<BF16>(c0[2], c0[3]);
-            *reinterpret_cast<uint32_t*>(szo + sw128_off(r0, k0 + 8, BM)) = pack2<BF16>(c1[0], c1[1]);
-            *reinterpret_cast<uint32_t*>(szo + sw128_off(r0 + 8, k0 + 8, BM)) = pack2<BF16>(c1[2], c1[3]);
-          }
-          if (fo + SC == 128) {
-            fence_proxy_async_smem();
-            mbar_arrive(bar_zo);
-            ++pc;
-          }
-        }
       }
 
       // ---- per-item epilogue
@@ -1269,37 +1247,65 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
                 au[q] = pack2<BF16>(__uint_as_float(pu[np][2 * q]), __uint_as_float(pu[np][2 * q + 1]));
                 av[q] = pack2<BF16>(__uint_as_float(pv[np][2 * q]), __uint_as_float(pv[np][2 * q + 1]));
               }
+              float cc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};  // channel blocks nb = 0, 1
 #pragma unroll
               for (int nb = 0; nb < 2; ++nb) {
                 const uint32_t bu0 = movm_trans(au[2 * nb]), bu1 = movm_trans(au[2 * nb + 1]);
                 const uint32_t bv0 = movm_trans(av[2 * nb]), bv1 = movm_trans(av[2 * nb + 1]);
-                float cc[4] = {0.f, 0.f, 0.f, 0.f};
-                mma16816<BF16>(cc, fuT, bu0, bu1);
-                mma16816<BF16>(cc, fvT, bv0, bv1);
-                const int k = k0 + nb * 8 + 2 * t4;
-#pragma unroll
-                for (int hr = 0; hr < 2; ++hr) {
-                  const int rw = hr ? rwB : rwA;
-                  if (rw < 0) continue;
-                  const int64_t row = rw;
-                  const float d0 = cc[2 * hr], d1 = cc[2 * hr + 1];
-                  if (cont) {
-                    const int64_t off = row * p.C + sCh[0] + k;
-                    if (a.dxn) {
-                      *reinterpret_cast<float2*>(a.dxn + off) = make_float2(d0, d1);
-                    } else if constexpr (std::is_same_v<TX, float>) {
-                      *reinterpret_cast<float2*>((float*)a.dx + off) = make_float2(d0, d1);
-                    } else {
-                      *reinterpret_cast<uint32_t*>((TX*)a.dx + off) =
-                          pack2<std::is_same_v<TX, __nv_bfloat16>>(d0, d1);
-                    }
+                mma16816<BF16>(cc[nb], fuT, bu0, bu1);
+                mma16816<BF16>(cc[nb], fvT, bv0, bv1);
+              }
+              if (cont) {
+                // Quad exchange (4 x 4 transpose over the lanes of a quad, two
+                // xor stages): lane t4 ends with row g + 8 * (t4 >> 1), channels
+                // k0 + 8 * (t4 & 1) .. +8, so it stores one 16-byte (bf16) or
+                // 32-byte (f32) row piece.  V[d] is the pair this lane holds for
+                // quad lane d; W[s] the pair received from quad lane s.
+                const bool b0 = t4 & 1, b1 = t4 >> 1;
+                const float2 V0 = make_float2(cc[0][0], cc[0][1]), V1 = make_float2(cc[1][0], cc[1][1]);
+                const float2 V2 = make_float2(cc[0][2], cc[0][3]), V3 = make_float2(cc[1][2], cc[1][3]);
+                auto xchg = [&](float2 v, int m) {
+                  return make_float2(__shfl_xor_sync(0xffffffffu, v.x, m), __shfl_xor_sync(0xffffffffu, v.y, m));
+                };
+                // stage 1 (lane ^ 1): keep the pairs whose destination shares bit 0
+                const float2 ra = xchg(b0 ? V0 : V1, 1), rb = xchg(b0 ? V2 : V3, 1);
+                const float2 own_lo = b0 ? V1 : V0, own_hi = b0 ? V3 : V2;
+                const float2 ulo0 = b0 ? ra : own_lo, ulo1 = b0 ? own_lo : ra;  // by source bit 0
+                const float2 uhi0 = b0 ? rb : own_hi, uhi1 = b0 ? own_hi : rb;
+                // stage 2 (lane ^ 2): keep the pairs whose destination shares bit 1
+                const float2 r0 = xchg(b1 ? ulo0 : uhi0, 2), r1 = xchg(b1 ? ulo1 : uhi1, 2);
+                const float2 k0v = b1 ? uhi0 : ulo0, k1v = b1 ? uhi1 : ulo1;
+                const float2 W0 = b1 ? r0 : k0v, W1 = b1 ? r1 : k1v, W2 = b1 ? k0v : r0, W3 = b1 ? k1v : r1;
+                const float ov[8] = {W0.x, W0.y, W1.x, W1.y, W2.x, W2.y, W3.x, W3.y};
+                const int rw = sRow[tile * 16 + g + 8 * (t4 >> 1)];
+                if (rw >= 0) {
+                  const int64_t off = (int64_t)rw * p.C + sCh[0] + k0 + 8 * (t4 & 1);
+                  if (a.dxn || std::is_same_v<TX, float>) {
+                    float* dst = a.dxn ? a.dxn + off : (float*)a.dx + off;
+                    reinterpret_cast<float4*>(dst)[0] = make_float4(ov[0], ov[1], ov[2], ov[3]);
+                    reinterpret_cast<float4*>(dst)[1] = make_float4(ov[4], ov[5], ov[6], ov[7]);
                   } else {
+                    constexpr bool XB = std::is_same_v<TX, __nv_bfloat16>;
+                    *reinterpret_cast<uint4*>((TX*)a.dx + off) =
+                        make_uint4(pack2<XB>(ov[0], ov[1]), pack2<XB>(ov[2], ov[3]), pack2<XB>(ov[4], ov[5]),
+                                   pack2<XB>(ov[6], ov[7]));
+                  }
+                }
+              } else {
+#pragma unroll
+                for (int nb = 0; nb < 2; ++nb) {
+                  const int k = k0 + nb * 8 + 2 * t4;
+#pragma unroll
+                  for (int hr = 0; hr < 2; ++hr) {
+                    const int rw = hr ? rwB : rwA;
+                    if (rw < 0) continue;
+                    const int64_t row = rw;
 #pragma unroll
                     for (int e = 0; e < 2; ++e) {
                       const int ch = sCh[k + e];
                       if (ch >= p.C) continue;
                       const int64_t off = row * p.C + ch;
-                      const float dv = e ? d1 : d0;
+                      const float dv = cc[nb][2 * hr + e];
                       if (a.dxn) a.dxn[off] = dv;
                       else ((TX*)a.dx)[off] = Elem<TX>::from(dv);
                     }
@@ -1355,12 +1361,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
       } else if (role == R_O) {
         mbar_wait(bar_yd, it & 1, sAbort);        // Y complete
         mbar_wait(bar_w, (pc - 1) & 1, sAbort);   // last M_o done with the pair buffer
-        mbar_wait(bar_gl, it & 1, sAbort);        // G' of this item present
+        mbar_wait(bar_gl, it & 1, sAbort);        // H and G' of this item present
         if (tid == 0 && it < 3) OW_TR(0, it * 32 + 17);
         __syncwarp();
         tc_fence_after();
-        unsigned char* stY = sm + C::O_ZO;
-        const uint32_t aY = smem_u32(stY), aG = smem_u32(sm + C::OFF_X1);
+        unsigned char* stY = sm + C::O_ZP;
+        const uint32_t aY = smem_u32(stY), aG = smem_u32(sm + C::O_G);
         const int cb32 = chh * 32;
         for (int hf = 0; hf < D / 64; ++hf) {
           uint32_t yr[32];
