@@ -328,34 +328,36 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const float* __restrict__ rstd, 
     auto mNW = [&](int buf) { return reinterpret_cast<float*>(meta + buf * C::META1 + 2 * BM + 2 * D); };
     auto mCont = [&](int buf) { return meta + buf * C::META1 + 2 * BM + 3 * D; };
 
-    // Metadata of one item, held in registers between issue and store.
-    struct MetaReg { int tok, b, ch, cont; float gg, nw; };
+    // Metadata of one item, held in registers between issue and store.  The
+    // loads are unconditional (clamped indices) and their values are first
+    // used in meta_store, so issuing them does not wait for memory.
+    struct MetaReg { int tok, b, ch, cont; float gg, nw; bool valid; };
     auto meta_issue = [&](int it) {
-      MetaReg m{-1, 0, 0, 0, 0.f, 0.f};
+      MetaReg m{0, 0, 0, 0, 0.f, 0.f, false};
       const int64_t item = blockIdx.x + (int64_t)it * gridDim.x;
       const int qc = (int)(item / nMB), mb = (int)(item - (int64_t)qc * nMB);
       if (tid < BM) {
         const int64_t t = (int64_t)mb * 8 + (tid >> 4);
-        int tok = p.N, b = 0;
-        if (t < BQ) {
-          b = (int)(t / p.Qs);
-          tok = p.tok[(t - (int64_t)b * p.Qs) * 16 + (tid & 15)];
-        }
-        m.tok = tok < p.N ? tok : -1;
-        m.b = b;
+        m.valid = t < BQ;
+        const int64_t tc = m.valid ? t : 0;
+        m.b = (int)(tc / p.Qs);
+        m.tok = p.tok[(tc - (int64_t)m.b * p.Qs) * 16 + (tid & 15)];
       }
       if (tid < D) {
         m.ch = p.ch[qc * D + tid];
         m.gg = gg[(int64_t)qc * D + tid];
-        m.nw = rstd ? nw[(int64_t)qc * D + tid] : 0.f;
+        if (rstd) m.nw = nw[(int64_t)qc * D + tid];
       }
-      if (tid == 0) m.cont = vec_ok && contig[qc] != 0;
+      if (tid == 0) m.cont = contig[qc];
       return m;
     };
     auto meta_store = [&](const MetaReg& m, int buf) {
-      if (tid < BM) { mTok(buf)[tid] = m.tok; mRowB(buf)[tid] = m.b; }
+      if (tid < BM) {
+        mTok(buf)[tid] = m.valid && m.tok < p.N ? m.tok : -1;
+        mRowB(buf)[tid] = m.b;
+      }
       if (tid < D) { mCh(buf)[tid] = m.ch; mGG(buf)[tid] = m.gg; mNW(buf)[tid] = m.nw; }
-      if (tid == 0) *mCont(buf) = m.cont;
+      if (tid == 0) *mCont(buf) = vec_ok && m.cont != 0;
     };
 
     // Gathered rows of one 64-channel half, held in registers (contiguous path).
@@ -369,26 +371,24 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const float* __restrict__ rstd, 
       for (int u = 0; u < 4; ++u) {
         const int unit = tid + u * NCOMP;
         const int r = unit >> 3, cj = unit & 7;
-        const int tok = tk[r];
-        R.rs[u] = 1.f;
-        if (tok >= 0) {
-          const int64_t row = (int64_t)rb[r] * p.N + tok;
-          const uint4* src = reinterpret_cast<const uint4*>(x + row * p.C + ch0 + hf * 64 + cj * 8);
+        // Pad rows load row 0 (always valid) and are zeroed in rows_store;
+        // no value is used here, so the loads stay in flight.
+        const int tok = tk[r] >= 0 ? tk[r] : 0;
+        const int64_t row = (int64_t)rb[r] * p.N + tok;
+        const uint4* src = reinterpret_cast<const uint4*>(x + row * p.C + ch0 + hf * 64 + cj * 8);
 #pragma unroll
-          for (int vv = 0; vv < VW; ++vv) R.v[u][vv] = __ldg(src + vv);
-          if (rstd) R.rs[u] = rstd[row];
-        } else {
-#pragma unroll
-          for (int vv = 0; vv < VW; ++vv) R.v[u][vv] = make_uint4(0u, 0u, 0u, 0u);
-        }
+        for (int vv = 0; vv < VW; ++vv) R.v[u][vv] = __ldg(src + vv);
+        R.rs[u] = rstd ? rstd[row] : 1.f;
       }
     };
     auto rows_store = [&](const RowReg& R, int buf, int hf) {
       const float* nwq = mNW(buf);
+      const int* tk = mTok(buf);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int unit = tid + u * NCOMP;
         const int r = unit >> 3, cj = unit & 7;
+        const bool pad = tk[r] < 0;
         float v[8];
         if constexpr (sizeof(TX) == 2) {
           const uint32_t w[4] = {R.v[u][0].x, R.v[u][0].y, R.v[u][0].z, R.v[u][0].w};
@@ -414,6 +414,10 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const float* __restrict__ rstd, 
             float t = round_through(v[e] * R.rs[u], x_dt);
             v[e] = round_through(t * nwq[k0 + e], x_dt);
           }
+        }
+        if (pad) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = 0.f;
         }
         uint4 w;
         w.x = pack2<BF16>(v[0], v[1]);
@@ -464,6 +468,7 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const float* __restrict__ rstd, 
       const float* sG = mGG(buf);
       const int ch0 = sChs[0];
 
+      if (tid == 0 && it < 3) OW_TR(0, it * 32 + 0);
       // -------- gather + token mix, 64 channels at a time
       for (int hf = 0; hf < D / 64; ++hf) {
         if (cont) {
@@ -494,6 +499,7 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const float* __restrict__ rstd, 
         comp_sync();  // staging reused by the next half
       }
       fence_proxy_async_smem();
+      if (tid == 0 && it < 3) OW_TR(0, it * 32 + 1);
       mbar_arrive(bar_p);
 
       // -------- gate: Z_q = silu(U_q) * V_q
@@ -504,6 +510,7 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const float* __restrict__ rstd, 
         const int s = c & 1;
         const uint32_t ph = (c >> 1) & 1;
         mbar_wait(bar_uv + s, ph, sAbort);
+        if (tid == 0 && it < 3 && q < 4) OW_TR(0, it * 32 + 2 + 2 * q);
         __syncwarp();
         tc_fence_after();
         uint32_t ur[32], vr[32];
@@ -527,19 +534,26 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const float* __restrict__ rstd, 
         }
         fence_proxy_async_smem();
         tc_fence_before();
+        if (tid == 0 && it < 3 && q < 4) OW_TR(0, it * 32 + 3 + 2 * q);
         mbar_arrive(bar_z + s);
       }
 
       // -------- prefetch the next item's metadata and first half of rows
       if (it + 1 < my_items) {
         meta_store(mnext, buf ^ 1);
+        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 20);
         comp_sync();
+        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 21);
         if (*mCont(buf ^ 1)) rows_issue(R, buf ^ 1, 0);
+        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 22);
         if (it + 2 < my_items) mnext = meta_issue(it + 2);
+        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 23);
       }
 
       // -------- epilogue: delta = A_o Y, gamma, mask, residual, scatter
+      if (tid == 0 && it < 3) OW_TR(0, it * 32 + 12);
       mbar_wait(bar_yz + ((c - 1) & 1), ((c - 1) >> 1) & 1, sAbort);
+      if (tid == 0 && it < 3) OW_TR(0, it * 32 + 13);
       __syncwarp();
       tc_fence_after();
       for (int hf = 0; hf < D / 64; ++hf) {
@@ -610,6 +624,7 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const float* __restrict__ rstd, 
         }
         comp_sync();
       }
+      if (tid == 0 && it < 3) OW_TR(0, it * 32 + 14);
       tc_fence_before();
     }
   }
@@ -742,3 +757,14 @@ int tc_forward(const ow_bigemm_args_t* a, const Prob& p, void* stream, Carver& w
 }
 
 }  // namespace ow
+
+#ifdef OW_TRACE
+extern "C" __attribute__((visibility("default"))) int ow_trace_fwd(void* host, size_t bytes, int clear) {
+  if (clear) {
+    void* dev = nullptr;
+    cudaGetSymbolAddress(&dev, ow::sm100::g_trace);
+    return (int)cudaMemset(dev, 0, sizeof(ow::sm100::g_trace));
+  }
+  return (int)cudaMemcpyFromSymbol(host, ow::sm100::g_trace, bytes);
+}
+#endif

@@ -378,23 +378,16 @@ __device__ __forceinline__ void rows_issue(RowRegs<TS, NHF>& R, const GatherCtx&
   for (int u = 0; u < 4; ++u) {
     const int unit = tid + u * NCOMP;
     const int r = unit >> 3, cj = unit & 7;
-    const int rw = gc.row[r];
-    R.rs[u] = 1.f;
-    if (rw >= 0) {
+    // Pad rows load row 0 (always valid) and are zeroed in rows_store; no
+    // loaded value is used here, so the loads stay in flight.
+    const int rw = gc.row[r] >= 0 ? gc.row[r] : 0;
 #pragma unroll
-      for (int h = 0; h < NHF; ++h) {
-        const uint4* p = reinterpret_cast<const uint4*>(src + (int64_t)rw * gc.C + ch0 + (hf0 + h) * 64 + cj * 8);
+    for (int h = 0; h < NHF; ++h) {
+      const uint4* p = reinterpret_cast<const uint4*>(src + (int64_t)rw * gc.C + ch0 + (hf0 + h) * 64 + cj * 8);
 #pragma unroll
-        for (int vv = 0; vv < RowRegs<TS, NHF>::VW; ++vv) R.v[h][u][vv] = __ldg(p + vv);
-      }
-      if (rstd) R.rs[u] = rstd[rw];
-      else if (scale) R.rs[u] = scale[rw / gc.N];
-    } else {
-#pragma unroll
-      for (int h = 0; h < NHF; ++h)
-#pragma unroll
-        for (int vv = 0; vv < RowRegs<TS, NHF>::VW; ++vv) R.v[h][u][vv] = make_uint4(0u, 0u, 0u, 0u);
+      for (int vv = 0; vv < RowRegs<TS, NHF>::VW; ++vv) R.v[h][u][vv] = __ldg(p + vv);
     }
+    R.rs[u] = rstd ? rstd[rw] : (scale ? scale[rw / gc.N] : 1.f);
   }
 }
 
@@ -437,6 +430,10 @@ __device__ __forceinline__ void rows_store(const RowRegs<TS, NHF>& R, int h, int
     } else {
 #pragma unroll
       for (int e = 0; e < 8; ++e) v[e] *= R.rs[u] * (ggq ? ggq[k + e] : 1.f);
+    }
+    if (gc.row[r] < 0) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = 0.f;
     }
     uint4 w;
     w.x = pack2<BF16>(v[0], v[1]);
@@ -1093,25 +1090,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
     auto frag = [&](int m, bool tr, uint32_t (&f)[4]) { load_afrag(a.amat + m * 256, tr, g, t4, f); };
     float accA[2][2][4] = {};  // DGRAD: dA_u, dA_v ; O: dA_o in accA[0]
     int c = 0, pc = 0;
-    // DGRAD epilogue metadata, loaded into registers one item ahead.
-    struct MetaReg { int row, ch, cont; };
+    // DGRAD epilogue metadata, loaded into registers one item ahead.  The
+    // loads are unconditional (clamped index) and their values are first used
+    // where the metadata is stored, so issuing them does not wait for memory.
+    struct MetaReg { int tok, b, ch, cont; bool valid; };
     auto meta_issue = [&](int it) {
-      MetaReg m{-1, 0, 0};
+      MetaReg m{0, 0, 0, 0, false};
       const int64_t item = item_of(it);
       const int qc = (int)(item / nMB), mb = (int)(item - (int64_t)qc * nMB);
       if (tid < BM) {
         const int64_t t = (int64_t)mb * 8 + (tid >> 4);
-        if (t < BQ) {
-          const int b = (int)(t / p.Qs);
-          const int tok = p.tok[(t - (int64_t)b * p.Qs) * 16 + (tid & 15)];
-          m.row = tok < p.N ? b * p.N + tok : -1;
-        }
+        m.valid = t < BQ;
+        const int64_t tc = m.valid ? t : 0;
+        m.b = (int)(tc / p.Qs);
+        m.tok = p.tok[(tc - (int64_t)m.b * p.Qs) * 16 + (tid & 15)];
       }
       if (tid < D) m.ch = p.ch[qc * D + tid];
-      if (tid == 0) m.cont = a.vec_ok && a.contig[qc] != 0;
+      if (tid == 0) m.cont = a.contig[qc];
       return m;
     };
-    MetaReg mreg{-1, 0, 0};
+    MetaReg mreg{0, 0, 0, 0, false};
     if (role == R_DGRAD && nit > 0) mreg = meta_issue(0);
     for (int it = 0; it < nit; ++it) {
       const int64_t item = item_of(it);
@@ -1205,9 +1203,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
       if (tid == 0 && it < 3) OW_TR(0, it * 32 + 16);
       if (role == R_DGRAD) {
         // Metadata of this item for the dX scatter.
-        if (tid < BM) sRow[tid] = mreg.row;
+        if (tid < BM) sRow[tid] = mreg.valid && mreg.tok < p.N ? mreg.b * p.N + mreg.tok : -1;
         if (tid < D) sCh[tid] = mreg.ch;
-        if (tid == 0) *sCont = mreg.cont;
+        if (tid == 0) *sCont = a.vec_ok && mreg.cont != 0;
         comp_sync();
         if (it + 1 < nit) mreg = meta_issue(it + 1);
         const bool cont = *sCont != 0;
