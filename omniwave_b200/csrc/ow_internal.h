@@ -25,6 +25,25 @@ struct Prob {
   int64_t ntiles() const { return BQ() * Qc; }
 };
 
+#ifdef __CUDACC__
+// contig[qc] = 1 when channel group qc is one run of D consecutive channels
+// starting on a multiple of 8 (and C % 8 == 0), so 16-byte vector accesses
+// apply; one warp per group, called by every thread of the grid.
+template <int D>
+__device__ __forceinline__ void contig_flags(const Prob& p, int* contig) {
+  const int lane = threadIdx.x & 31;
+  const int gw = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int nw = (int)((gridDim.x * blockDim.x) >> 5);
+  for (int qc = gw; qc < p.Qc; qc += nw) {
+    const int c0 = p.ch[qc * D];
+    bool ok = true;
+    for (int k = lane; k < D; k += 32) ok &= p.ch[qc * D + k] == c0 + k;
+    ok = __all_sync(0xffffffffu, ok);
+    if (lane == 0) contig[qc] = ok && (c0 % 8 == 0) && (c0 + D <= p.C) && (p.C % 8 == 0);
+  }
+}
+#endif
+
 // Workspace carve-up helper: hands out aligned sub-ranges of one buffer and
 // tracks the total size (a dry run with base == nullptr measures it).
 struct Carver {

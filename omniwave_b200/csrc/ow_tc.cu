@@ -104,15 +104,16 @@ __global__ void tc_prep_kernel(Prob p, const TW* __restrict__ au, const TW* __re
                                float* __restrict__ gg, float* __restrict__ nw, int* __restrict__ contig) {
   using C = Cfg<D>;
   using T16 = std::conditional_t<BF16, __nv_bfloat16, __half>;
-  const int64_t per_chunk = 3LL * NC * D;
-  const int64_t n_img = (int64_t)p.Qc * C::NQ * per_chunk;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  for (int64_t i = tid; i < n_img; i += stride) {
-    int64_t chunk = i / per_chunk;
-    int e = (int)(i - chunk * per_chunk);
-    int qc = (int)(chunk / C::NQ), q = (int)(chunk - (int64_t)qc * C::NQ);
-    unsigned char* base = img + chunk * C::IMG_BYTES;
+  // 32-bit indices: the divisors are compile-time constants (multiply-shift).
+  constexpr int per_chunk = 3 * NC * D;
+  const int n_img = p.Qc * C::NQ * per_chunk;
+  const int stride = gridDim.x * blockDim.x;
+  const int tid = blockIdx.x * blockDim.x + threadIdx.x;
+  for (int i = tid; i < n_img; i += stride) {
+    const int chunk = i / per_chunk;
+    int e = i - chunk * per_chunk;
+    int qc = chunk / C::NQ, q = chunk - qc * C::NQ;
+    unsigned char* base = img + (int64_t)chunk * C::IMG_BYTES;
     float v;
     uint32_t off;
     if (e < 2 * NC * D) {  // Bu / Bv: row n (output feature), column k (input channel)
@@ -130,26 +131,21 @@ __global__ void tc_prep_kernel(Prob p, const TW* __restrict__ au, const TW* __re
     }
     *reinterpret_cast<T16*>(base + off) = Elem<T16>::from(v);
   }
-  for (int64_t i = tid; i < 3 * 256; i += stride) {
+  for (int i = tid; i < 3 * 256; i += stride) {
     const TW* src = i < 256 ? au : (i < 512 ? av : ao);
     T16 h = Elem<T16>::from(load_as<float>(src, i & 255));
     amat[i] = *reinterpret_cast<uint16_t*>(&h);
   }
-  for (int64_t i = tid; i < (int64_t)p.Qc * D; i += stride) {
+  for (int i = tid; i < p.Qc * D; i += stride) {
     int c = p.ch[i];
     gg[i] = c < p.C ? load_as<float>(gamma, c) : 0.f;
   }
   if (nw_in)
-    for (int64_t i = tid; i < (int64_t)p.Qc * D; i += stride) {
+    for (int i = tid; i < p.Qc * D; i += stride) {
       int c = p.ch[i];
       nw[i] = c < p.C ? load_as<float>(nw_in, c) : 0.f;
     }
-  for (int64_t qc = tid; qc < p.Qc; qc += stride) {
-    int c0 = p.ch[qc * D];
-    int ok = (c0 % 8 == 0) && (c0 + D <= p.C) && (p.C % 8 == 0);
-    for (int k = 1; k < D && ok; ++k) ok = p.ch[qc * D + k] == c0 + k;
-    contig[qc] = ok;
-  }
+  contig_flags<D>(p, contig);
 }
 
 // Named barrier over the compute warps only.
@@ -340,7 +336,9 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const float* __restrict__ rstd, 
         const int64_t t = (int64_t)mb * 8 + (tid >> 4);
         m.valid = t < BQ;
         const int64_t tc = m.valid ? t : 0;
-        m.b = (int)(tc / p.Qs);
+        // 32-bit division whenever the tile count allows (it always does at
+        // the supported batch sizes); the 64-bit one costs ~1000 cycles.
+        m.b = BQ < (int64_t)INT32_MAX ? (int)tc / p.Qs : (int)(tc / p.Qs);
         m.tok = p.tok[(tc - (int64_t)m.b * p.Qs) * 16 + (tid & 15)];
       }
       if (tid < D) {

@@ -189,14 +189,15 @@ __global__ void tc_bwd_prep_kernel(Prob p, const TW* __restrict__ au, const TW* 
                                    float* __restrict__ gg, float* __restrict__ nw, int* __restrict__ contig) {
   using C = BCfg<D>;
   using T16 = std::conditional_t<BF16, __nv_bfloat16, __half>;
-  constexpr int64_t per_a = 3LL * C::SC * D;           // one sub-chunk stage
-  constexpr int64_t per_qc = C::NSUB * per_a + (int64_t)C::RD * D;
-  const int64_t n_img = (int64_t)p.Qc * per_qc;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  for (int64_t i = tid; i < n_img; i += stride) {
-    const int qc = (int)(i / per_qc);
-    const int64_t e = i - (int64_t)qc * per_qc;
+  // 32-bit indices: the divisors are compile-time constants (multiply-shift).
+  constexpr int per_a = 3 * C::SC * D;  // one sub-chunk stage
+  constexpr int per_qc = C::NSUB * per_a + C::RD * D;
+  const int n_img = p.Qc * per_qc;
+  const int stride = gridDim.x * blockDim.x;
+  const int tid = blockIdx.x * blockDim.x + threadIdx.x;
+  for (int i = tid; i < n_img; i += stride) {
+    const int qc = i / per_qc;
+    const int e = i - qc * per_qc;
     unsigned char* base = img + (int64_t)qc * C::QC_IMG;
     float v;
     uint32_t off;
@@ -214,7 +215,7 @@ __global__ void tc_bwd_prep_kernel(Prob p, const TW* __restrict__ au, const TW* 
       }
       off = (uint32_t)(s * C::A_BYTES + sub * C::SUB_BYTES) + sw128_off(n, k, C::SC);
     } else {  // chunk k: B_o rows = D channels c, K = 64 features of the chunk
-      const int r = (int)(e - C::NSUB * per_a);
+      const int r = e - C::NSUB * per_a;
       const int kc = r / (64 * D), rr = r - kc * 64 * D;
       const int c = rr / 64, kf = rr - c * 64;
       v = load_as<float>(bo, ((int64_t)qc * C::RD + kc * 64 + kf) * D + c);
@@ -222,23 +223,18 @@ __global__ void tc_bwd_prep_kernel(Prob p, const TW* __restrict__ au, const TW* 
     }
     *reinterpret_cast<T16*>(base + off) = Elem<T16>::from(v);
   }
-  for (int64_t i = tid; i < 3 * 256; i += stride) {
+  for (int i = tid; i < 3 * 256; i += stride) {
     const TW* src = i < 256 ? au : (i < 512 ? av : ao);
     T16 h = Elem<T16>::from(load_as<float>(src, i & 255));
     amat[i] = *reinterpret_cast<uint16_t*>(&h);
   }
-  for (int64_t i = tid; i < (int64_t)p.Qc * D; i += stride) {
+  for (int i = tid; i < p.Qc * D; i += stride) {
     const int c = p.ch[i];
     gg[i] = c < p.C ? load_as<float>(gamma, c) : 0.f;
   }
   if (nw_in)
-    for (int64_t i = tid; i < p.C; i += stride) nw[i] = load_as<float>(nw_in, i);
-  for (int64_t qc = tid; qc < p.Qc; qc += stride) {
-    const int c0 = p.ch[qc * D];
-    int ok = (c0 % 8 == 0) && (c0 + D <= p.C) && (p.C % 8 == 0);
-    for (int k = 1; k < D && ok; ++k) ok = p.ch[qc * D + k] == c0 + k;
-    contig[qc] = ok;
-  }
+    for (int i = tid; i < p.C; i += stride) nw[i] = load_as<float>(nw_in, i);
+  contig_flags<D>(p, contig);
 }
 
 __device__ __forceinline__ void comp_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NCOMP) : "memory"); }
@@ -1102,7 +1098,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
         const int64_t t = (int64_t)mb * 8 + (tid >> 4);
         m.valid = t < BQ;
         const int64_t tc = m.valid ? t : 0;
-        m.b = (int)(tc / p.Qs);
+        // 32-bit division whenever the tile count allows (it always does at
+        // the supported batch sizes); the 64-bit one costs ~1000 cycles.
+        m.b = BQ < (int64_t)INT32_MAX ? (int)tc / p.Qs : (int)(tc / p.Qs);
         m.tok = p.tok[(tc - (int64_t)m.b * p.Qs) * 16 + (tid & 15)];
       }
       if (tid < D) m.ch = p.ch[qc * D + tid];
@@ -1482,14 +1480,14 @@ template <int D, typename TW>
 __global__ void tc_bwd_reduce_b_kernel(Prob p, BwdArgs a, TW* __restrict__ db_u, TW* __restrict__ db_v,
                                        TW* __restrict__ db_o, float* __restrict__ mo) {
   using C = BCfg<D>;
-  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  const int64_t nB = (int64_t)p.Qc * D * C::RD;
-  for (int64_t i = tid; i < 3 * nB; i += stride) {
-    const int m = (int)(i / nB);
-    const int64_t rem = i - m * nB;
-    const int qc = (int)(rem / (C::RD * D));
-    const int e = (int)((rem / D) % C::RD), c = (int)(rem % D);
+  const int tid = blockIdx.x * blockDim.x + threadIdx.x;
+  const int stride = gridDim.x * blockDim.x;
+  const int nB = p.Qc * D * C::RD;
+  for (int i = tid; i < 3 * nB; i += stride) {
+    const int m = i / nB;
+    const int rem = i - m * nB;
+    const int qc = rem / (C::RD * D);
+    const int e = (rem / D) % C::RD, c = rem % D;
     float s = 0.f;
     if (m < 2) {
       const int hh = e / 128, el = e % 128;
