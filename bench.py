@@ -64,14 +64,17 @@ def fwd_flops(b: int, h: int, w: int, c: int, d: int) -> float:
 
 
 def _kernel_flops(name: str, b: int, h: int, w: int, c: int, d: int) -> float:
-    """Algorithmic FLOPs one launch of ``name`` accounts for.  The backward's
-    algorithmic work (2x forward) is split between the pack kernel, which
-    does the three 16x16 token mixes of the operands (P_u, P_v, dY'), and the
-    role kernel, which does everything else."""
+    """Algorithmic FLOPs one launch of ``name`` accounts for.  The forward is
+    split between its pack kernel (the input token mixes P_u = A_u T,
+    P_v = A_v T) and the forward kernel (everything else); the backward's
+    (2x forward) between the backward pack kernel, which does the three 16x16
+    token mixes of the operands (P_u, P_v, dY'), and the role kernel."""
     tiles = b * math.ceil(h * w / G) * math.ceil(c / d)
     mixes = tiles * 3 * 2 * G * G * d
+    if name == "tc_pack_fwd_kernel":
+        return float(tiles * 4 * G * G * d)
     if name == "tc_fwd_kernel":
-        return fwd_flops(b, h, w, c, d)
+        return fwd_flops(b, h, w, c, d) - tiles * 4 * G * G * d
     if name == "tc_pack_kernel":
         return float(mixes)
     return 2.0 * fwd_flops(b, h, w, c, d) - mixes
@@ -215,10 +218,11 @@ def run_ours(args) -> None:
 
     def one_case(cs, ev=None):
         # ev: call boundaries [0..2] and, through ow_profile_events, the
-        # forward kernel [3, 4], the pack kernel [5, 6] and the backward role
-        # kernel [7, 8] on the same stream.
+        # forward kernel [3, 4], the backward pack kernel [5, 6], the backward
+        # role kernel [7, 8] and the forward pack kernel [9, 10] on the same
+        # stream.
         if ev is not None:
-            for k, i in ((0, 3), (1, 5), (2, 7)):
+            for k, i in ((0, 3), (1, 5), (2, 7), (3, 9)):
                 lib.ow_profile_events(k, ctypes.c_void_p(ev[i].cuda_event), ctypes.c_void_p(ev[i + 1].cuda_event))
             ev[0].record()
         out = bigemm(plan=cs["plan"], backend="cuda", **cs["leaves"])
@@ -227,7 +231,7 @@ def run_ours(args) -> None:
         grads = torch.autograd.grad(out, [cs["leaves"][k] for k in names], cs["dout"])
         if ev is not None:
             ev[2].record()
-            for k in range(3):
+            for k in range(4):
                 lib.ow_profile_events(k, None, None)
         return out, grads
 
@@ -240,7 +244,7 @@ def run_ours(args) -> None:
     torch.cuda.synchronize()
 
     # --- device-timed region -------------------------------------------------
-    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(9)] for _ in cases]
+    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(11)] for _ in cases]
            for _ in range(args.steps)]
     for e in (e for st in evs for ce in st for e in ce):
         e.record()  # torch creates the CUDA event on first record; the library needs the handle
@@ -275,7 +279,8 @@ def run_ours(args) -> None:
     per, kern = {}, {}
     for i, cs in enumerate(cases):
         per[(cs["shape"], cs["route"])] = (mean_ms(i, 0, 1), mean_ms(i, 1, 2))
-        kern[(cs["shape"], cs["route"])] = {"tc_fwd_kernel": mean_ms(i, 3, 4), "tc_pack_kernel": mean_ms(i, 5, 6),
+        kern[(cs["shape"], cs["route"])] = {"tc_pack_fwd_kernel": mean_ms(i, 9, 10),
+                                            "tc_fwd_kernel": mean_ms(i, 3, 4), "tc_pack_kernel": mean_ms(i, 5, 6),
                                             "tc_bwd_kernel": mean_ms(i, 7, 8)}
     # Dominant kernel: the single launch with the largest device time.
     dom_key, dom_name, dom_ms = max(((k, n, t) for k, v in kern.items() for n, t in v.items()),

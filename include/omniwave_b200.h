@@ -136,9 +136,10 @@ OW_API uint64_t ow_launch_count(void);
  * process (any host thread) records the caller's CUDA events (cudaEvent_t
  * cast to void*) on the call's stream immediately before and after one of
  * its kernels:
- *   OW_PROF_FWD  the tensor-core forward kernel,
- *   OW_PROF_PACK the backward pack kernel (operand images),
- *   OW_PROF_BWD  the backward role kernel.
+ *   OW_PROF_FWD   the tensor-core forward kernel,
+ *   OW_PROF_PACK  the backward pack kernel (operand images),
+ *   OW_PROF_BWD   the backward role kernel,
+ *   OW_PROF_FPACK the forward pack kernel (P_u | P_v images).
  * Passing NULL for both events stops recording for that kernel.  Returns
  * OW_ERR_INVALID for an unknown ``kernel``.  No counterpart in the reference
  * (it is a measurement aid, not part of the operator).
@@ -146,6 +147,7 @@ OW_API uint64_t ow_launch_count(void);
 #define OW_PROF_FWD 0
 #define OW_PROF_PACK 1
 #define OW_PROF_BWD 2
+#define OW_PROF_FPACK 3
 OW_API int ow_profile_events(int kernel, void* start, void* stop);
 
 /* ABI version compiled into the library (OW_ABI_VERSION). */

@@ -21,7 +21,7 @@ static std::atomic<uint64_t> g_launches{0};
 void count_launches(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
 
 // Process-wide (autograd runs backward calls on its own device threads).
-static std::atomic<void*> g_prof[3][2] = {};
+static std::atomic<void*> g_prof[4][2] = {};
 
 void profile_mark(int kernel, bool after, cudaStream_t st) {
   void* e = g_prof[kernel][after ? 1 : 0].load(std::memory_order_acquire);
@@ -109,7 +109,7 @@ int ow_abi_version(void) { return OW_ABI_VERSION; }
 uint64_t ow_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int ow_profile_events(int kernel, void* start, void* stop) {
-  if (kernel < OW_PROF_FWD || kernel > OW_PROF_BWD) {
+  if (kernel < OW_PROF_FWD || kernel > OW_PROF_FPACK) {
     set_error("ow_profile_events: unknown kernel %d", kernel);
     return OW_ERR_INVALID;
   }

@@ -73,6 +73,9 @@ int rmsnorm_rstd(const void* x, int x_dtype, int compute_dtype, int64_t rows, in
 // Tensor-core path (bf16/f16 compute, g=16, d in {64,128}, rd=2d).
 bool tc_supported(const ow_bigemm_args_t* a, const Prob& p, const char** why);
 int tc_forward(const ow_bigemm_args_t* a, const Prob& p, void* stream, Carver& ws);
+// The forward's pre-pass: [P_u | P_v] operand images per item (ow_tc_bwd.cu).
+int tc_pack_forward(const ow_bigemm_args_t* a, const Prob& p, const uint16_t* amat, const float* nwc,
+                    const int* contig, unsigned char* packed, void* stream);
 int tc_fault(int device, int reset);
 
 // RMSNorm backward of block mode from the f32 gradient w.r.t. the normalised

@@ -1,23 +1,29 @@
 // Tensor-core BiGEMM forward for sm_100a (bf16 / f16 compute, g = 16,
 // d in {64, 128}, rd = 2d).
 //
-// Work unit: one channel group q_c and an "M-block" of 128 token rows (eight
-// consecutive spatial tiles).  Per M-block (reference.py:147-171):
+// Work unit ("item"): one channel group q_c and an M-block of 128 token rows
+// (eight consecutive spatial tiles).  Per item (reference.py:147-171):
 //
-//   gather T (route tables, optional RMSNorm)    compute warps, registers -> smem
-//   P_u = A_u T, P_v = A_v T                      compute warps, mma.sync m16n8k16
-//   for each 64-wide chunk q of rd:
+//   gather T (route tables, optional RMSNorm)    pack kernel (ow_tc_bwd.cu), one CTA per item
+//   P_u = A_u T, P_v = A_v T                      pack kernel, mma.sync, SW128 images in HBM
+//   for each 64-wide chunk q of rd:               forward kernel (this file):
 //     U_q = P_u B_u[:, q], V_q = P_v B_v[:, q]    tcgen05.mma, f32 in TMEM (double buffered)
 //     Z_q = silu(U_q) * V_q                       compute warps, TMEM -> smem
 //     Y  += Z_q B_o[q, :]                         tcgen05.mma, f32 in TMEM
-//   delta = A_o Y * gamma * mask (+ x)            compute warps, mma.sync, scattered stores
+//   delta = A_o Y * gamma * scale (+ x)           compute warps: TMEM C-fragments, mma.sync,
+//                                                 quad exchange, 16/32-byte row stores
 //
-// Roles (320 threads): warps 0-7 compute, warp 8 issues every tcgen05.mma
-// (one thread) and owns the TMEM allocation, warp 9 streams pre-swizzled
-// weight chunks with cp.async.bulk into a two-stage ring.  Synchronisation is
-// mbarrier-only; every wait is bounded (ow_sm100.cuh).  The grid is
-// persistent (one CTA per SM) and walks items channel-group-major so that the
-// weight chunks of a group are shared through L2 by neighbouring CTAs.
+// Roles of the forward kernel (320 threads): warps 0-7 compute, warp 8 issues
+// every tcgen05.mma (one thread) and owns the TMEM allocation, warp 9 issues
+// the bulk copies: the packed [P_u | P_v] of each item (two item buffers at
+// d = 64, one at d = 128) and the pre-swizzled weight chunk images (resident
+// per channel group at d = 64, a two-stage ring at d = 128).  The epilogue's
+// warp MMAs run while the tensor pipe is idle (the next item's second chunk
+// waits for it): mma.sync latency rises tenfold behind queued tcgen05 work.
+// Synchronisation is mbarrier-only; every wait is bounded (ow_sm100.cuh).
+// The grid is persistent (one CTA per SM) and walks items
+// channel-group-major so that the weight chunks of a group are shared
+// through L2 by neighbouring CTAs.
 
 #include <algorithm>
 #include <type_traits>
@@ -39,7 +45,6 @@ constexpr int NCOMP = NCOMP_WARPS * 32;
 constexpr int MMA_WARP = NCOMP_WARPS;
 constexpr int PROD_WARP = NCOMP_WARPS + 1;
 constexpr int TC_THREADS = (NCOMP_WARPS + 2) * 32;
-constexpr int STG_LD = 72;              // staging row stride (elements): 64 + 8 pad
 constexpr int TMEM_COLS = 512;
 
 template <int D>
@@ -47,44 +52,54 @@ struct Cfg {
   static constexpr int RD = 2 * D;
   static constexpr int NQ = RD / NC;
   static constexpr int P_BYTES = BM * D * 2;
+  static constexpr int PP_BYTES = 2 * P_BYTES;           // [P_u | P_v] of one item
+  static constexpr int ROWS_BYTES = BM * 4;              // output row of each token row (-1: none)
+  static constexpr int PK_BYTES = PP_BYTES + ROWS_BYTES;  // one item of the packed buffer
   static constexpr int Z_BYTES = BM * NC * 2;
-  static constexpr int BU_BYTES = NC * D * 2;     // one of Bu/Bv chunk images
+  static constexpr int BU_BYTES = NC * D * 2;            // one of Bu/Bv chunk images
   static constexpr int WUV_BYTES = 2 * BU_BYTES;
   static constexpr int WO_BYTES = D * NC * 2;
   static constexpr int IMG_BYTES = WUV_BYTES + WO_BYTES;
-  static constexpr int STG_BYTES = BM * STG_LD * 2;
-  static constexpr int OFF_PU = 0;
-  static constexpr int OFF_PV = OFF_PU + P_BYTES;
-  static constexpr int OFF_Z = OFF_PV + P_BYTES;
-  static constexpr int OFF_WUV = OFF_Z + 2 * Z_BYTES;
-  static constexpr int OFF_WO = OFF_WUV + 2 * WUV_BYTES;
-  static constexpr int OFF_STG = OFF_WO + 2 * WO_BYTES;
-  static constexpr int OFF_META = OFF_STG + STG_BYTES;     // 2 x {tok[128], rowb[128], ch[D], gg[D], nw[D], cont}
-  static constexpr int META1 = 2 * BM + 3 * D + 4;         // 32-bit words per buffer
-  static constexpr int META_BYTES = 2 * META1 * 4;
-  static constexpr int OFF_BAR = OFF_META + META_BYTES;
-  static constexpr int BAR_BYTES = 16 * 8 + 16;
+  static constexpr int GRP_BYTES = NQ * IMG_BYTES;       // chunk images of one channel group
+  // d = 64: two groups of chunk images (48 KB each) stay resident (the next
+  // group's arrives while the current one is in use), the item operands are
+  // double-buffered, and the compute warps run the next item's first gate
+  // before this item's epilogue.  d = 128: the chunk images stream through a
+  // two-stage ring, one item buffer, gates then epilogue.
+  static constexpr bool RES = D == 64;
+  static constexpr int NB = RES ? 2 : 1;
+  static constexpr int OFF_P = 0;
+  static constexpr int OFF_Z = OFF_P + NB * PP_BYTES;
+  static constexpr int OFF_W = OFF_Z + 2 * Z_BYTES;       // resident: 2 x GRP_BYTES
+  static constexpr int OFF_WUV = OFF_W;                   // streaming: 2 x [Bu | Bv]
+  static constexpr int OFF_WO = OFF_WUV + 2 * WUV_BYTES;  // streaming: 2 x Bo
+  static constexpr int W_END = RES ? OFF_W + 2 * GRP_BYTES : OFF_WO + 2 * WO_BYTES;
+  static constexpr int OFF_ROWS = W_END;                  // 2 x ROWS_BYTES
+  static constexpr int OFF_BAR = OFF_ROWS + 2 * ROWS_BYTES;
+  static constexpr int NBAR = 22;
+  static constexpr int BAR_BYTES = NBAR * 8 + 16;
   static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024;  // + alignment slack
-  // TMEM columns.
+  // TMEM columns: U/V of two chunks, Y of two items.
   __host__ __device__ static constexpr int T_U(int s) { return s * 128; }
   __host__ __device__ static constexpr int T_V(int s) { return s * 128 + 64; }
-  static constexpr int T_Y = 256;
-  static_assert(T_Y + D <= TMEM_COLS, "TMEM budget");
+  __host__ __device__ static constexpr int T_Y(int b) { return 256 + b * D; }
+  static_assert(256 + 2 * D <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
 // Workspace layout of the tensor-core path (offsets in bytes from its base).
 template <int D>
 struct TcWs {
-  size_t img, amat, gg, nw, contig, total;
+  size_t img, amat, gg, nwc, contig, packed, total;
   TcWs(const Prob& p) {
     size_t o = 0;
     auto take = [&](size_t n) { size_t r = o; o = (o + n + 255) / 256 * 256; return r; };
     img = take((size_t)p.Qc * Cfg<D>::NQ * Cfg<D>::IMG_BYTES);
     amat = take(3 * 256 * 2);
     gg = take((size_t)p.Qc * D * 4);
-    nw = take((size_t)p.Qc * D * 4);
+    nwc = take((size_t)p.C * 4);
     contig = take((size_t)p.Qc * 4);
+    packed = take((size_t)p.Qc * ((p.BQ() + 7) / 8) * Cfg<D>::PK_BYTES);
     total = o;
   }
 };
@@ -92,8 +107,9 @@ struct TcWs {
 // ---------------------------------------------------------------------------
 // Weight preparation: SW128 K-major chunk images of B_u, B_v (B operand
 // [NC x D] per chunk) and B_o (B operand [D x NC] per chunk), 16-bit copies of
-// the token-mix matrices, f32 grouped gamma and norm weight, and a per-group
-// flag telling whether the group's channels are one aligned contiguous run.
+// the token-mix matrices, f32 grouped gamma, the f32 norm weight per channel,
+// and a per-group flag telling whether the group's channels are one aligned
+// contiguous run.
 // ---------------------------------------------------------------------------
 template <int D, typename TW, bool BF16>
 __global__ void tc_prep_kernel(Prob p, const TW* __restrict__ au, const TW* __restrict__ av,
@@ -101,7 +117,8 @@ __global__ void tc_prep_kernel(Prob p, const TW* __restrict__ au, const TW* __re
                                const TW* __restrict__ bv, const TW* __restrict__ bo,
                                const TW* __restrict__ gamma, const TW* __restrict__ nw_in,
                                unsigned char* __restrict__ img, uint16_t* __restrict__ amat,
-                               float* __restrict__ gg, float* __restrict__ nw, int* __restrict__ contig) {
+                               float* __restrict__ gg, float* __restrict__ nwc,
+                               int* __restrict__ contig) {
   using C = Cfg<D>;
   using T16 = std::conditional_t<BF16, __nv_bfloat16, __half>;
   // 32-bit indices: the divisors are compile-time constants (multiply-shift).
@@ -141,80 +158,64 @@ __global__ void tc_prep_kernel(Prob p, const TW* __restrict__ au, const TW* __re
     gg[i] = c < p.C ? load_as<float>(gamma, c) : 0.f;
   }
   if (nw_in)
-    for (int i = tid; i < p.Qc * D; i += stride) {
-      int c = p.ch[i];
-      nw[i] = c < p.C ? load_as<float>(nw_in, c) : 0.f;
-    }
+    for (int i = tid; i < p.C; i += stride) nwc[i] = load_as<float>(nw_in, i);
   contig_flags<D>(p, contig);
 }
 
-// Named barrier over the compute warps only.
-__device__ __forceinline__ void comp_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NCOMP) : "memory"); }
-
-template <typename TX>
-__device__ __forceinline__ void load8(const TX* __restrict__ src, float (&v)[8]) {
-  if constexpr (sizeof(TX) == 2) {
-    uint4 u = __ldg(reinterpret_cast<const uint4*>(src));
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float2 f = unpack2<std::is_same_v<TX, __nv_bfloat16>>(w[i]);
-      v[2 * i] = f.x;
-      v[2 * i + 1] = f.y;
-    }
-  } else {
-    float4 a = __ldg(reinterpret_cast<const float4*>(src));
-    float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-  }
-}
-
 // ---------------------------------------------------------------------------
-// Forward kernel.
+// Forward kernel.  [P_u | P_v] and the output rows of every item come
+// pre-packed (pack pass) and arrive by bulk copy; the compute warps run the
+// gates and the epilogue only.
 // ---------------------------------------------------------------------------
 template <int D, bool BF16, typename TX, typename TO>
 __global__ void __launch_bounds__(TC_THREADS, 1)
-tc_fwd_kernel(Prob p, const TX* __restrict__ x, const float* __restrict__ rstd, int x_dt,
+tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict__ packed,
               const unsigned char* __restrict__ img, const uint16_t* __restrict__ amat,
-              const float* __restrict__ gg, const float* __restrict__ nw, const int* __restrict__ contig,
-              const float* __restrict__ scale, int residual, TO* __restrict__ out, int vec_ok) {
+              const float* __restrict__ gg, const int* __restrict__ contig, const float* __restrict__ scale,
+              int residual, TO* __restrict__ out, int vec_ok) {
   using C = Cfg<D>;
+  constexpr bool EARLY = C::RES;  // next item's first gate before this item's epilogue
+  constexpr bool QUIET_Y = true;  // early order: hold Y(item, 0) until the previous epilogue is done
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  unsigned char* sPu = sm + C::OFF_PU;
-  unsigned char* sPv = sm + C::OFF_PV;
   unsigned char* sZ = sm + C::OFF_Z;
-  unsigned char* sWuv = sm + C::OFF_WUV;
-  unsigned char* sWo = sm + C::OFF_WO;
-  unsigned char* sStg = sm + C::OFF_STG;
-  int* sTok = reinterpret_cast<int*>(sm + C::OFF_META);
-  int* sRowB = sTok + BM;
-  int* sCh = sRowB + BM;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
-  uint64_t* bar_p = bars + 0;
-  uint64_t* bar_uv = bars + 1;   // [2]
-  uint64_t* bar_z = bars + 3;    // [2]
-  uint64_t* bar_yz = bars + 5;   // [2]
-  uint64_t* bar_wuv = bars + 7;  // [2]
-  uint64_t* bar_wo = bars + 9;   // [2]
-  uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* bar_p = bars + 0;       // [2] item operands of item buffer i loaded (tx)
+  uint64_t* bar_uv = bars + 2;      // [2] U/V of TMEM buffer s computed (commit)
+  uint64_t* bar_z = bars + 4;       // [2] Z_s written, TMEM buffer s read
+  uint64_t* bar_yz = bars + 6;      // [2] Y MMA of Z buffer s done (commit)
+  uint64_t* bar_wuv = bars + 8;     // [2] streaming: [B_u | B_v] stage loaded (tx)
+  uint64_t* bar_wo = bars + 10;     // [2] streaming: B_o stage loaded (tx)
+  uint64_t* bar_pf = bars + 12;     // [2] operands of item buffer i no longer read (commit)
+  uint64_t* bar_epd = bars + 14;    // [2] epilogue of an item with parity b done
+  uint64_t* bar_wres = bars + 16;   // [2] resident: chunk images of group buffer b loaded (tx)
+  uint64_t* bar_wfree = bars + 18;  // [2] resident: group buffer b no longer read (commit)
+  uint64_t* bar_m = bars + 20;      // [2] output rows of row slot b loaded (tx)
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + C::NBAR);
   volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t BQ = (int64_t)p.B * p.Qs;
   const int nMB = (int)((BQ + 7) / 8);
   const int64_t items = (int64_t)p.Qc * nMB;
-  const int my_items = items > blockIdx.x ? (int)((items - 1 - blockIdx.x) / gridDim.x + 1) : 0;
+  const int nit = items > blockIdx.x ? (int)((items - 1 - blockIdx.x) / gridDim.x + 1) : 0;
+  const int total = nit * C::NQ;
+  auto item_of = [&](int it) { return (int64_t)blockIdx.x + (int64_t)it * gridDim.x; };
+  auto qc_of = [&](int it) { return (int)(item_of(it) / nMB); };
 
   if (threadIdx.x == 0) {
-    mbar_init(bar_p, NCOMP);
     for (int s = 0; s < 2; ++s) {
+      mbar_init(bar_p + s, 1);
       mbar_init(bar_uv + s, 1);
       mbar_init(bar_z + s, NCOMP);
       mbar_init(bar_yz + s, 1);
       mbar_init(bar_wuv + s, 1);
       mbar_init(bar_wo + s, 1);
+      mbar_init(bar_pf + s, 1);
+      mbar_init(bar_epd + s, NCOMP);
+      mbar_init(bar_wres + s, 1);
+      mbar_init(bar_wfree + s, 1);
+      mbar_init(bar_m + s, 1);
     }
     *sAbort = 0;
     fence_mbar_init();
@@ -226,32 +227,77 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const float* __restrict__ rstd, 
   const uint32_t tbase = *sTmem;
 
   if (warp == PROD_WARP) {
-    // ------------------------------------------------ weight producer
-    if (lane == 0 && my_items > 0) {
-      const int total = my_items * C::NQ;
-      auto chunk_src = [&](int c) {
-        int it = c / C::NQ, q = c - it * C::NQ;
-        int64_t item = blockIdx.x + (int64_t)it * gridDim.x;
-        int qc = (int)(item / nMB);
-        return img + ((int64_t)qc * C::NQ + q) * C::IMG_BYTES;
+    // ------------------------------------------------ producer (bulk copies)
+    if (lane == 0 && nit > 0) {
+      auto load_p = [&](int it) {
+        const int bf = it % C::NB;
+        mbar_arrive_expect_tx(bar_p + bf, C::PP_BYTES);
+        bulk_g2s(sm + C::OFF_P + bf * C::PP_BYTES, packed + item_of(it) * C::PK_BYTES, C::PP_BYTES, bar_p + bf);
       };
-      auto load_uv = [&](int c) {
-        int s = c & 1;
-        mbar_arrive_expect_tx(bar_wuv + s, C::WUV_BYTES);
-        bulk_g2s(sWuv + s * C::WUV_BYTES, chunk_src(c), C::WUV_BYTES, bar_wuv + s);
+      // Output rows of item it into row slot it & 1, once the epilogue of
+      // item it - 2 (the slot's last reader) is done.
+      auto load_rows = [&](int it) {
+        const int sl = it & 1;
+        if (it >= 2 && !mbar_wait(bar_epd + sl, ((it - 2) >> 1) & 1, sAbort)) return;
+        mbar_arrive_expect_tx(bar_m + sl, C::ROWS_BYTES);
+        bulk_g2s(sm + C::OFF_ROWS + sl * C::ROWS_BYTES, packed + item_of(it) * C::PK_BYTES + C::PP_BYTES,
+                 C::ROWS_BYTES, bar_m + sl);
       };
-      auto load_o = [&](int c) {
-        int s = c & 1;
-        mbar_arrive_expect_tx(bar_wo + s, C::WO_BYTES);
-        bulk_g2s(sWo + s * C::WO_BYTES, chunk_src(c) + C::WUV_BYTES, C::WO_BYTES, bar_wo + s);
-      };
-      for (int c = 0; c < 2 && c < total; ++c) { load_uv(c); load_o(c); }
-      for (int c = 0; c + 2 < total; ++c) {
-        const int s = c & 1;
-        const uint32_t ph = (c >> 1) & 1;
-        if (mbar_wait(bar_uv + s, ph, sAbort)) load_uv(c + 2);
-        if (mbar_wait(bar_yz + s, ph, sAbort)) load_o(c + 2);
-        if (*sAbort) break;
+      if constexpr (C::RES) {
+        // Group e (a run of items of one channel group) uses buffer e & 1; it
+        // is loaded once group e - 2 has released that buffer.
+        int we = 0, wq = qc_of(0);
+        auto load_w = [&](int e, int qc) {
+          const int b = e & 1;
+          if (e >= 2 && !mbar_wait(bar_wfree + b, ((e - 2) >> 1) & 1, sAbort)) return;
+          mbar_arrive_expect_tx(bar_wres + b, C::GRP_BYTES);
+          bulk_g2s(sm + C::OFF_W + b * C::GRP_BYTES, img + (int64_t)qc * C::GRP_BYTES, C::GRP_BYTES, bar_wres + b);
+        };
+        load_w(0, wq);
+        load_p(0);
+        load_rows(0);
+        if (nit > 1) {
+          load_p(1);
+          load_rows(1);
+          if (qc_of(1) != wq) load_w(++we, wq = qc_of(1));
+        }
+        for (int it = 0; it + 2 < nit && !*sAbort; ++it) {
+          if (mbar_wait(bar_pf + (it & 1), (it >> 1) & 1, sAbort)) load_p(it + 2);
+          if (qc_of(it + 2) != wq) load_w(++we, wq = qc_of(it + 2));
+          load_rows(it + 2);
+        }
+      } else {
+        auto chunk_src = [&](int c) {
+          const int it = c / C::NQ, q = c - it * C::NQ;
+          return img + ((int64_t)qc_of(it) * C::NQ + q) * C::IMG_BYTES;
+        };
+        auto load_uv = [&](int c) {
+          const int s = c & 1;
+          mbar_arrive_expect_tx(bar_wuv + s, C::WUV_BYTES);
+          bulk_g2s(sm + C::OFF_WUV + s * C::WUV_BYTES, chunk_src(c), C::WUV_BYTES, bar_wuv + s);
+        };
+        auto load_o = [&](int c) {
+          const int s = c & 1;
+          mbar_arrive_expect_tx(bar_wo + s, C::WO_BYTES);
+          bulk_g2s(sm + C::OFF_WO + s * C::WO_BYTES, chunk_src(c) + C::WUV_BYTES, C::WO_BYTES, bar_wo + s);
+        };
+        load_p(0);
+        load_rows(0);
+        if (nit > 1) load_rows(1);
+        for (int c = 0; c < 2 && c < total; ++c) {
+          load_uv(c);
+          load_o(c);
+        }
+        for (int c = 0; c < total && !*sAbort; ++c) {
+          const int it = c / C::NQ, q = c - it * C::NQ;
+          const int s = c & 1;
+          const uint32_t ph = (c >> 1) & 1;
+          if (c + 2 < total && mbar_wait(bar_uv + s, ph, sAbort)) load_uv(c + 2);
+          if (q == C::NQ - 1 && it + 1 < nit && mbar_wait(bar_pf, it & 1, sAbort)) load_p(it + 1);
+          if (c + 2 < total && mbar_wait(bar_yz + s, ph, sAbort)) load_o(c + 2);
+          // Rows of item it + 1 once the epilogue of item it - 1 is done.
+          if (q == 1 && it >= 1 && it + 1 < nit) load_rows(it + 1);
+        }
       }
     }
   } else if (warp == MMA_WARP) {
@@ -259,33 +305,59 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const float* __restrict__ rstd, 
     if (lane == 0) {
       constexpr uint32_t ID_UV = idesc_f16(BM, NC, BF16);
       constexpr uint32_t ID_Y = idesc_f16(BM, D, BF16);
-      const uint32_t aPu = smem_u32(sPu), aPv = smem_u32(sPv);
-      int c = 0;
-      auto issue_y = [&](int cy, int qy) {
-        const int s = cy & 1;
-        const uint32_t ph = (cy >> 1) & 1;
+      const uint32_t s0 = smem_u32(sm);
+      uint32_t wb0 = s0 + C::OFF_W, wb1 = wb0;  // resident group buffer of the items with parity 0 / 1
+      auto issue_y = [&](int x) {  // Y(item) (+)= Z_x B_o[x]
+        const int s = x & 1, ix = x / C::NQ, q = x - ix * C::NQ, yb = ix & 1;
+        const uint32_t ph = (x >> 1) & 1;
+        // Y buffer yb was last read by the epilogue of item ix - 2.  With the
+        // early gate order the wait is for item ix - 1 instead: the tensor
+        // pipe then idles while that epilogue's warp MMAs run (their latency
+        // rises tenfold behind queued tcgen05 work), and the MMAs held back
+        // (this Y, the next item's first U/V) are not needed before it ends.
+        constexpr int YD = EARLY && QUIET_Y ? 1 : 2;
+        if (q == 0 && ix >= YD) mbar_wait(bar_epd + ((ix - YD) & 1), ((ix - YD) >> 1) & 1, sAbort);
         mbar_wait(bar_z + s, ph, sAbort);
-        mbar_wait(bar_wo + s, ph, sAbort);
+        if (!C::RES) mbar_wait(bar_wo + s, ph, sAbort);
         tc_fence_after();
         if (!*sAbort) {
-          const uint32_t aZ = smem_u32(sZ + s * C::Z_BYTES), aW = smem_u32(sWo + s * C::WO_BYTES);
+          const uint32_t aZ = s0 + C::OFF_Z + s * C::Z_BYTES;
+          const uint32_t aW = C::RES ? ((ix & 1) ? wb1 : wb0) + q * C::IMG_BYTES + C::WUV_BYTES
+                                     : s0 + C::OFF_WO + s * C::WO_BYTES;
 #pragma unroll
           for (int kk = 0; kk < NC / 16; ++kk)
-            umma_f16(tbase + C::T_Y, sdesc_sw128(sw128_kstep(aZ, kk, BM)),
-                     sdesc_sw128(sw128_kstep(aW, kk, D)), ID_Y, (qy > 0 || kk > 0) ? 1u : 0u);
+            umma_f16(tbase + C::T_Y(yb), sdesc_sw128(sw128_kstep(aZ, kk, BM)),
+                     sdesc_sw128(sw128_kstep(aW, kk, D)), ID_Y, (q > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(bar_yz + s);
       };
-      for (int it = 0; it < my_items; ++it) {
-        mbar_wait(bar_p, it & 1, sAbort);
+      int c = 0, e = 0;
+      for (int it = 0; it < nit; ++it) {
+        const bool newgrp = C::RES && it > 0 && qc_of(it) != qc_of(it - 1);
+        if (!EARLY && it > 0) {
+          // One item buffer: finish the previous item, then hold this item's
+          // MMAs until the previous epilogue (warp MMAs) is done.
+          issue_y(c - 1);
+          mbar_wait(bar_epd + ((it - 1) & 1), ((it - 1) >> 1) & 1, sAbort);
+        }
+        if (C::RES) {
+          if (newgrp) ++e;
+          ((it & 1) ? wb1 : wb0) = s0 + C::OFF_W + (e & 1) * C::GRP_BYTES;
+          if (it == 0 || newgrp) mbar_wait(bar_wres + (e & 1), (e >> 1) & 1, sAbort);
+        }
+        if (it < 3) OW_TR(1, it * 32 + 0);
+        mbar_wait(bar_p + it % C::NB, (it / C::NB) & 1, sAbort);
+        if (it < 3) OW_TR(1, it * 32 + 1);
         tc_fence_after();
+        const uint32_t aPu = s0 + C::OFF_P + (it % C::NB) * C::PP_BYTES, aPv = aPu + C::P_BYTES;
         for (int q = 0; q < C::NQ; ++q, ++c) {
           const int s = c & 1;
           const uint32_t ph = (c >> 1) & 1;
-          mbar_wait(bar_wuv + s, ph, sAbort);
+          if (!C::RES) mbar_wait(bar_wuv + s, ph, sAbort);
+          if (it < 3 && q < 4) OW_TR(1, it * 32 + 2 + q);
           tc_fence_after();
           if (!*sAbort) {
-            const uint32_t aBu = smem_u32(sWuv + s * C::WUV_BYTES);
+            const uint32_t aBu = C::RES ? ((it & 1) ? wb1 : wb0) + q * C::IMG_BYTES : s0 + C::OFF_WUV + s * C::WUV_BYTES;
             const uint32_t aBv = aBu + C::BU_BYTES;
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
@@ -296,323 +368,207 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const float* __restrict__ rstd, 
             }
           }
           umma_commit(bar_uv + s);
-          if (q >= 1) issue_y(c - 1, q - 1);
+          if (q == C::NQ - 1) umma_commit(bar_pf + it % C::NB);
+          if (c > 0 && (EARLY || q > 0)) {
+            issue_y(c - 1);
+            if (it < 3 && q < 4) OW_TR(1, it * 32 + 8 + q);
+            // The previous item's last Y was the last reader of its group buffer.
+            if (q == 0 && newgrp) umma_commit(bar_wfree + ((e - 1) & 1));
+          }
         }
-        issue_y(c - 1, C::NQ - 1);
       }
+      if (total > 0) issue_y(total - 1);
     }
   } else {
     // ------------------------------------------------ compute warps
     const int tid = threadIdx.x;
     const int g = lane >> 2, t4 = lane & 3;
-    // Token-mix matrices as m16n8k16 A fragments.
-    uint32_t fa[3][4];
-#pragma unroll
-    for (int m = 0; m < 3; ++m) {
-      const uint16_t* A = amat + m * 256;
-      fa[m][0] = *reinterpret_cast<const uint32_t*>(A + g * 16 + 2 * t4);
-      fa[m][1] = *reinterpret_cast<const uint32_t*>(A + (g + 8) * 16 + 2 * t4);
-      fa[m][2] = *reinterpret_cast<const uint32_t*>(A + g * 16 + 2 * t4 + 8);
-      fa[m][3] = *reinterpret_cast<const uint32_t*>(A + (g + 8) * 16 + 2 * t4 + 8);
-    }
-    const uint32_t aStg = smem_u32(sStg);
-    int32_t* meta = reinterpret_cast<int32_t*>(sTok);
-    auto mTok = [&](int buf) { return meta + buf * C::META1; };
-    auto mRowB = [&](int buf) { return meta + buf * C::META1 + BM; };
-    auto mCh = [&](int buf) { return meta + buf * C::META1 + 2 * BM; };
-    auto mGG = [&](int buf) { return reinterpret_cast<float*>(meta + buf * C::META1 + 2 * BM + D); };
-    auto mNW = [&](int buf) { return reinterpret_cast<float*>(meta + buf * C::META1 + 2 * BM + 2 * D); };
-    auto mCont = [&](int buf) { return meta + buf * C::META1 + 2 * BM + 3 * D; };
+    uint32_t fo[4];  // A_o as an m16n8k16 A fragment
+    load_afrag(amat + 512, false, g, t4, fo);
+    // Gate: warp (lq, hw) reads TMEM lanes 32 lq .. +31, columns 32 hw .. +31
+    // of a chunk.  Epilogue: the same warp owns tiles 2 lq, 2 lq + 1 and
+    // channels [hw D / 2, (hw + 1) D / 2); after the quad exchange a lane
+    // stores row rsel of a tile, channels csel .. csel + 7 of each 16-channel
+    // step.
+    const int lq = warp & 3, hw = warp >> 2;
+    const int r = lq * 32 + lane, cb = hw * 32;
+    const uint32_t trow = tbase + ((uint32_t)(lq * 32) << 16);
+    constexpr int NP = D / 32;                   // 16-channel steps per warp
+    constexpr int VW = sizeof(TX) == 2 ? 1 : 2;  // 16-byte vectors per 8 elements of x
+    const int rsel = g + 8 * (t4 >> 1), csel = 8 * (t4 & 1);
 
-    // Metadata of one item, held in registers between issue and store.  The
-    // loads are unconditional (clamped indices) and their values are first
-    // used in meta_store, so issuing them does not wait for memory.
-    struct MetaReg { int tok, b, ch, cont; float gg, nw; bool valid; };
-    auto meta_issue = [&](int it) {
-      MetaReg m{0, 0, 0, 0, 0.f, 0.f, false};
-      const int64_t item = blockIdx.x + (int64_t)it * gridDim.x;
-      const int qc = (int)(item / nMB), mb = (int)(item - (int64_t)qc * nMB);
-      if (tid < BM) {
-        const int64_t t = (int64_t)mb * 8 + (tid >> 4);
-        m.valid = t < BQ;
-        const int64_t tc = m.valid ? t : 0;
-        // 32-bit division whenever the tile count allows (it always does at
-        // the supported batch sizes); the 64-bit one costs ~1000 cycles.
-        m.b = BQ < (int64_t)INT32_MAX ? (int)tc / p.Qs : (int)(tc / p.Qs);
-        m.tok = p.tok[(tc - (int64_t)m.b * p.Qs) * 16 + (tid & 15)];
-      }
-      if (tid < D) {
-        m.ch = p.ch[qc * D + tid];
-        m.gg = gg[(int64_t)qc * D + tid];
-        if (rstd) m.nw = nw[(int64_t)qc * D + tid];
-      }
-      if (tid == 0) m.cont = contig[qc];
-      return m;
-    };
-    auto meta_store = [&](const MetaReg& m, int buf) {
-      if (tid < BM) {
-        mTok(buf)[tid] = m.valid && m.tok < p.N ? m.tok : -1;
-        mRowB(buf)[tid] = m.b;
-      }
-      if (tid < D) { mCh(buf)[tid] = m.ch; mGG(buf)[tid] = m.gg; mNW(buf)[tid] = m.nw; }
-      if (tid == 0) *mCont(buf) = vec_ok && m.cont != 0;
+    // Channel-group state, reloaded when the group changes (rarely: items
+    // are walked group-major).
+    int cur_qc = -1, ch0 = 0;
+    bool cont = false;
+    float gam[NP][8];
+    auto set_group = [&](int qc) {
+      if (qc == cur_qc) return;
+      cur_qc = qc;
+      ch0 = p.ch[qc * D];
+      cont = vec_ok && contig[qc] != 0;
+#pragma unroll
+      for (int np = 0; np < NP; ++np)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) gam[np][e] = gg[qc * D + hw * (D / 2) + np * 16 + csel + e];
     };
 
-    // Gathered rows of one 64-channel half, held in registers (contiguous path).
-    constexpr int VW = sizeof(TX) == 2 ? 1 : 2;  // 16-byte vectors per 8 elements
-    struct RowReg { uint4 v[4][VW]; float rs[4]; };
-    auto rows_issue = [&](RowReg& R, int buf, int hf) {
-      const int* tk = mTok(buf);
-      const int* rb = mRowB(buf);
-      const int ch0 = mCh(buf)[0];
+    // -------- gate: Z_x = silu(U_x) * V_x for chunk x
+    auto gate = [&](int cx) {
+      const int s = cx & 1;
+      const uint32_t ph = (cx >> 1) & 1;
+      const int it = cx / C::NQ, q = cx - it * C::NQ;
+      mbar_wait(bar_uv + s, ph, sAbort);
+      if (tid == 0 && it < 3 && q < 4) OW_TR(0, it * 32 + 2 + 2 * q);
+      __syncwarp();
+      tc_fence_after();
+      uint32_t ur[32], vr[32];
+      tmem_ld32(trow + C::T_U(s) + cb, ur);
+      tmem_ld32(trow + C::T_V(s) + cb, vr);
+      tmem_ld_wait();
+      if (cx >= 2) mbar_wait(bar_yz + s, ((cx - 2) >> 1) & 1, sAbort);
+      unsigned char* Zs = sZ + s * C::Z_BYTES;
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int unit = tid + u * NCOMP;
-        const int r = unit >> 3, cj = unit & 7;
-        // Pad rows load row 0 (always valid) and are zeroed in rows_store;
-        // no value is used here, so the loads stay in flight.
-        const int tok = tk[r] >= 0 ? tk[r] : 0;
-        const int64_t row = (int64_t)rb[r] * p.N + tok;
-        const uint4* src = reinterpret_cast<const uint4*>(x + row * p.C + ch0 + hf * 64 + cj * 8);
-#pragma unroll
-        for (int vv = 0; vv < VW; ++vv) R.v[u][vv] = __ldg(src + vv);
-        R.rs[u] = rstd ? rstd[row] : 1.f;
-      }
-    };
-    auto rows_store = [&](const RowReg& R, int buf, int hf) {
-      const float* nwq = mNW(buf);
-      const int* tk = mTok(buf);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int unit = tid + u * NCOMP;
-        const int r = unit >> 3, cj = unit & 7;
-        const bool pad = tk[r] < 0;
-        float v[8];
-        if constexpr (sizeof(TX) == 2) {
-          const uint32_t w[4] = {R.v[u][0].x, R.v[u][0].y, R.v[u][0].z, R.v[u][0].w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            float2 f = unpack2<std::is_same_v<TX, __nv_bfloat16>>(w[i]);
-            v[2 * i] = f.x;
-            v[2 * i + 1] = f.y;
-          }
-        } else {
-#pragma unroll
-          for (int vv = 0; vv < 2; ++vv) {
-            v[4 * vv + 0] = __uint_as_float(R.v[u][vv].x);
-            v[4 * vv + 1] = __uint_as_float(R.v[u][vv].y);
-            v[4 * vv + 2] = __uint_as_float(R.v[u][vv].z);
-            v[4 * vv + 3] = __uint_as_float(R.v[u][vv].w);
-          }
-        }
-        if (rstd) {
-          const int k0 = hf * 64 + cj * 8;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            float t = round_through(v[e] * R.rs[u], x_dt);
-            v[e] = round_through(t * nwq[k0 + e], x_dt);
-          }
-        }
-        if (pad) {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) v[e] = 0.f;
-        }
+      for (int jj = 0; jj < 4; ++jj) {
         uint4 w;
-        w.x = pack2<BF16>(v[0], v[1]);
-        w.y = pack2<BF16>(v[2], v[3]);
-        w.z = pack2<BF16>(v[4], v[5]);
-        w.w = pack2<BF16>(v[6], v[7]);
-        *reinterpret_cast<uint4*>(sStg + (r * STG_LD + cj * 8) * 2) = w;
-      }
-    };
-    // Element-wise gather (channels not one aligned run): synchronous.
-    auto rows_elem = [&](int buf, int hf) {
-      const int* tk = mTok(buf);
-      const int* rb = mRowB(buf);
-      const int* chs = mCh(buf);
-      const float* nwq = mNW(buf);
-      for (int e = tid; e < BM * 64; e += NCOMP) {
-        const int r = e >> 6, k = e & 63;
-        const int tok = tk[r], ch = chs[hf * 64 + k];
-        float v = 0.f;
-        if (tok >= 0 && ch < p.C) {
-          const int64_t row = (int64_t)rb[r] * p.N + tok;
-          v = load_as<float>(x, row * p.C + ch);
-          if (rstd) {
-            v = round_through(v * rstd[row], x_dt);
-            v = round_through(v * nwq[hf * 64 + k], x_dt);
-          }
-        }
-        uint32_t pk = pack2<BF16>(v, 0.f);
-        *reinterpret_cast<uint16_t*>(sStg + (r * STG_LD + k) * 2) = (uint16_t)(pk & 0xFFFF);
-      }
-    };
-
-    RowReg R;
-    MetaReg mnext{};
-    if (my_items > 0) {
-      meta_store(meta_issue(0), 0);
-      comp_sync();
-      if (*mCont(0)) rows_issue(R, 0, 0);
-      if (my_items > 1) mnext = meta_issue(1);
-    }
-    int c = 0;
-    for (int it = 0; it < my_items; ++it) {
-      const int buf = it & 1;
-      const bool cont = *mCont(buf) != 0;
-      const int* sTk = mTok(buf);
-      const int* sRb = mRowB(buf);
-      const int* sChs = mCh(buf);
-      const float* sG = mGG(buf);
-      const int ch0 = sChs[0];
-
-      if (tid == 0 && it < 3) OW_TR(0, it * 32 + 0);
-      // -------- gather + token mix, 64 channels at a time
-      for (int hf = 0; hf < D / 64; ++hf) {
-        if (cont) {
-          rows_store(R, buf, hf);
-          if (hf + 1 < D / 64) rows_issue(R, buf, hf + 1);
-        } else {
-          rows_elem(buf, hf);
-        }
-        comp_sync();
+        uint32_t* wp = &w.x;
 #pragma unroll
-        for (int np = 0; np < 4; ++np) {
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4_trans(aStg + ((warp * 16 + (lane & 15)) * STG_LD + np * 16 + (lane >> 4) * 8) * 2, b0, b1, b2,
-                        b3);
-#pragma unroll
-          for (int m = 0; m < 2; ++m) {
-            float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
-            mma16816<BF16>(c0, fa[m], b0, b1);
-            mma16816<BF16>(c1, fa[m], b2, b3);
-            unsigned char* P = m ? sPv : sPu;
-            const int r0 = warp * 16 + g, k0 = hf * 64 + np * 16 + 2 * t4;
-            *reinterpret_cast<uint32_t*>(P + sw128_off(r0, k0, BM)) = pack2<BF16>(c0[0], c0[1]);
-            *reinterpret_cast<uint32_t*>(P + sw128_off(r0 + 8, k0, BM)) = pack2<BF16>(c0[2], c0[3]);
-            *reinterpret_cast<uint32_t*>(P + sw128_off(r0, k0 + 8, BM)) = pack2<BF16>(c1[0], c1[1]);
-            *reinterpret_cast<uint32_t*>(P + sw128_off(r0 + 8, k0 + 8, BM)) = pack2<BF16>(c1[2], c1[3]);
-          }
+        for (int e = 0; e < 4; ++e) {
+          const int i0 = jj * 8 + 2 * e;
+          uint32_t u2 = pack2<BF16>(__uint_as_float(ur[i0]), __uint_as_float(ur[i0 + 1]));
+          uint32_t v2 = pack2<BF16>(__uint_as_float(vr[i0]), __uint_as_float(vr[i0 + 1]));
+          wp[e] = silu_mul2<BF16>(u2, v2);
         }
-        comp_sync();  // staging reused by the next half
+        *reinterpret_cast<uint4*>(Zs + sw128_off(r, cb + jj * 8, BM)) = w;
       }
       fence_proxy_async_smem();
-      if (tid == 0 && it < 3) OW_TR(0, it * 32 + 1);
-      mbar_arrive(bar_p);
+      tc_fence_before();
+      if (tid == 0 && it < 3 && q < 4) OW_TR(0, it * 32 + 3 + 2 * q);
+      mbar_arrive(bar_z + s);
+    };
 
-      // -------- gate: Z_q = silu(U_q) * V_q
-      const int lq = warp & 3, cb = (warp >> 2) * 32;
-      const int r = lq * 32 + lane;
-      const uint32_t trow = tbase + ((uint32_t)(lq * 32) << 16);
-      for (int q = 0; q < C::NQ; ++q, ++c) {
-        const int s = c & 1;
-        const uint32_t ph = (c >> 1) & 1;
-        mbar_wait(bar_uv + s, ph, sAbort);
-        if (tid == 0 && it < 3 && q < 4) OW_TR(0, it * 32 + 2 + 2 * q);
-        __syncwarp();
-        tc_fence_after();
-        uint32_t ur[32], vr[32];
-        tmem_ld32(trow + C::T_U(s) + cb, ur);
-        tmem_ld32(trow + C::T_V(s) + cb, vr);
-        tmem_ld_wait();
-        if (c >= 2) mbar_wait(bar_yz + s, ((c - 2) >> 1) & 1, sAbort);
-        unsigned char* Zs = sZ + s * C::Z_BYTES;
+    // -------- epilogue state of one item: its output rows, sample scales and
+    // residual values (requested ahead of use; pad rows read row 0 and are
+    // never stored, so no load waits for a comparison).
+    int rowr[2];
+    float scr[2];
+    uint4 xres[2][NP][VW];
+    auto epi_prepare = [&](int it) {
+      const int sl = it & 1;
+      set_group(qc_of(it));
+      mbar_wait(bar_m + sl, (it >> 1) & 1, sAbort);
+      const int* sRows = reinterpret_cast<const int*>(sm + C::OFF_ROWS + sl * C::ROWS_BYTES);
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          uint4 w;
-          uint32_t* wp = &w.x;
+      for (int tl = 0; tl < 2; ++tl) {
+        rowr[tl] = sRows[(2 * lq + tl) * 16 + rsel];
+        scr[tl] = scale ? scale[(rowr[tl] >= 0 ? rowr[tl] : 0) / p.N] : 1.f;
+      }
+      if (cont && residual) {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int i0 = jj * 8 + 2 * e;
-            uint32_t u2 = pack2<BF16>(__uint_as_float(ur[i0]), __uint_as_float(ur[i0 + 1]));
-            uint32_t v2 = pack2<BF16>(__uint_as_float(vr[i0]), __uint_as_float(vr[i0 + 1]));
-            wp[e] = silu_mul2<BF16>(u2, v2);
+        for (int tl = 0; tl < 2; ++tl) {
+          const int64_t row = rowr[tl] >= 0 ? rowr[tl] : 0;
+#pragma unroll
+          for (int np = 0; np < NP; ++np) {
+            const uint4* src = reinterpret_cast<const uint4*>(x + row * p.C + ch0 + hw * (D / 2) + np * 16 + csel);
+#pragma unroll
+            for (int vv = 0; vv < VW; ++vv) xres[tl][np][vv] = __ldg(src + vv);
           }
-          *reinterpret_cast<uint4*>(Zs + sw128_off(r, cb + jj * 8, BM)) = w;
         }
-        fence_proxy_async_smem();
-        tc_fence_before();
-        if (tid == 0 && it < 3 && q < 4) OW_TR(0, it * 32 + 3 + 2 * q);
-        mbar_arrive(bar_z + s);
       }
+    };
 
-      // -------- prefetch the next item's metadata and first half of rows
-      if (it + 1 < my_items) {
-        meta_store(mnext, buf ^ 1);
-        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 20);
-        comp_sync();
-        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 21);
-        if (*mCont(buf ^ 1)) rows_issue(R, buf ^ 1, 0);
-        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 22);
-        if (it + 2 < my_items) mnext = meta_issue(it + 2);
-        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 23);
-      }
-
-      // -------- epilogue: delta = A_o Y, gamma, mask, residual, scatter
+    // -------- epilogue: delta = A_o Y, gamma, sample scale, residual
+    auto epilogue = [&](int it) {
+      const int yb = it & 1, cl = it * C::NQ + C::NQ - 1;
       if (tid == 0 && it < 3) OW_TR(0, it * 32 + 12);
-      mbar_wait(bar_yz + ((c - 1) & 1), ((c - 1) >> 1) & 1, sAbort);
+      mbar_wait(bar_yz + (cl & 1), (cl >> 1) & 1, sAbort);
       if (tid == 0 && it < 3) OW_TR(0, it * 32 + 13);
       __syncwarp();
       tc_fence_after();
-      for (int hf = 0; hf < D / 64; ++hf) {
-        uint32_t yr[32];
-        tmem_ld32(trow + C::T_Y + hf * 64 + cb, yr);
-        tmem_ld_wait();
+      const int* sRows = reinterpret_cast<const int*>(sm + C::OFF_ROWS + (it & 1) * C::ROWS_BYTES);
+      // Y of both tiles in the C-fragment layout, one wait.
+      uint32_t yv[2][NP][8];
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          uint4 w;
-          w.x = pack2<BF16>(__uint_as_float(yr[jj * 8 + 0]), __uint_as_float(yr[jj * 8 + 1]));
-          w.y = pack2<BF16>(__uint_as_float(yr[jj * 8 + 2]), __uint_as_float(yr[jj * 8 + 3]));
-          w.z = pack2<BF16>(__uint_as_float(yr[jj * 8 + 4]), __uint_as_float(yr[jj * 8 + 5]));
-          w.w = pack2<BF16>(__uint_as_float(yr[jj * 8 + 6]), __uint_as_float(yr[jj * 8 + 7]));
-          *reinterpret_cast<uint4*>(sPu + (r * STG_LD + cb + jj * 8) * 2) = w;
-        }
-        comp_sync();
-        const int row0 = warp * 16 + g;
-        const int tokA = sTk[row0], tokB = sTk[row0 + 8];
-        const int bA = sRb[row0], bB = sRb[row0 + 8];
-        const float sA = scale ? scale[bA] : 1.f, sB = scale ? scale[bB] : 1.f;
-        const uint32_t aEp = smem_u32(sPu);
+      for (int tl = 0; tl < 2; ++tl) {
+        const uint32_t ta = tbase + ((uint32_t)((2 * lq + tl) * 16) << 16) + C::T_Y(yb) + hw * (D / 2);
 #pragma unroll
-        for (int np = 0; np < 4; ++np) {
-          __syncwarp();
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4_trans(aEp + ((warp * 16 + (lane & 15)) * STG_LD + np * 16 + (lane >> 4) * 8) * 2, b0, b1, b2,
-                        b3);
-          float cc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-          mma16816<BF16>(cc[0], fa[2], b0, b1);
-          mma16816<BF16>(cc[1], fa[2], b2, b3);
+        for (int np = 0; np < NP; ++np) tmem_ld16x256_x2(ta + np * 16, yv[tl][np]);
+      }
+      tmem_ld_wait();
+      if (tid == 0 && it < 3) OW_TR(0, it * 32 + 15);
 #pragma unroll
-          for (int nb = 0; nb < 2; ++nb) {
-            const int k = hf * 64 + np * 16 + nb * 8 + 2 * t4;
-            const float g0 = sG[k], g1 = sG[k + 1];
+      for (int tl = 0; tl < 2; ++tl) {
+        const int tile = 2 * lq + tl;
 #pragma unroll
-            for (int hr = 0; hr < 2; ++hr) {
-              const int tok = hr ? tokB : tokA;
-              if (tok < 0) continue;
-              const int64_t row = (int64_t)(hr ? bB : bA) * p.N + tok;
-              const float sc = hr ? sB : sA;
-              float d0 = cc[nb][2 * hr] * g0 * sc;
-              float d1 = cc[nb][2 * hr + 1] * g1 * sc;
-              if (cont) {
-                const int64_t off = row * p.C + ch0 + k;
-                if (residual) {
-                  d0 += load_as<float>(x, off);
-                  d1 += load_as<float>(x, off + 1);
-                }
-                if constexpr (std::is_same_v<TO, float>) {
-                  *reinterpret_cast<float2*>(out + off) = make_float2(d0, d1);
+        for (int np = 0; np < NP; ++np) {
+          const int k0 = hw * (D / 2) + np * 16;
+          uint32_t ay[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            ay[q] = pack2<BF16>(__uint_as_float(yv[tl][np][2 * q]), __uint_as_float(yv[tl][np][2 * q + 1]));
+          float cc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};  // channel blocks nb = 0, 1
+#pragma unroll
+          for (int nb = 0; nb < 2; ++nb)
+            mma16816<BF16>(cc[nb], fo, movm_trans(ay[2 * nb]), movm_trans(ay[2 * nb + 1]));
+          if (cont) {
+            float ov[8];
+            quad_rows8(cc, t4, ov);
+            if (rowr[tl] >= 0) {
+              const float sc = scr[tl];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) ov[e] = ov[e] * gam[np][e] * sc;
+              if (residual) {
+                float xv[8];
+                if constexpr (sizeof(TX) == 2) {
+                  const uint32_t w[4] = {xres[tl][np][0].x, xres[tl][np][0].y, xres[tl][np][0].z,
+                                         xres[tl][np][0].w};
+#pragma unroll
+                  for (int i = 0; i < 4; ++i) {
+                    const float2 f = unpack2<std::is_same_v<TX, __nv_bfloat16>>(w[i]);
+                    xv[2 * i] = f.x;
+                    xv[2 * i + 1] = f.y;
+                  }
                 } else {
-                  *reinterpret_cast<uint32_t*>(out + off) =
-                      pack2<std::is_same_v<TO, __nv_bfloat16>>(d0, d1);
+#pragma unroll
+                  for (int vv = 0; vv < 2; ++vv) {
+                    xv[4 * vv + 0] = __uint_as_float(xres[tl][np][vv].x);
+                    xv[4 * vv + 1] = __uint_as_float(xres[tl][np][vv].y);
+                    xv[4 * vv + 2] = __uint_as_float(xres[tl][np][vv].z);
+                    xv[4 * vv + 3] = __uint_as_float(xres[tl][np][vv].w);
+                  }
                 }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) ov[e] += xv[e];
+              }
+              TO* dst = out + (int64_t)rowr[tl] * p.C + ch0 + k0 + csel;
+              if constexpr (std::is_same_v<TO, float>) {
+                reinterpret_cast<float4*>(dst)[0] = make_float4(ov[0], ov[1], ov[2], ov[3]);
+                reinterpret_cast<float4*>(dst)[1] = make_float4(ov[4], ov[5], ov[6], ov[7]);
               } else {
+                constexpr bool OB = std::is_same_v<TO, __nv_bfloat16>;
+                *reinterpret_cast<uint4*>(dst) = make_uint4(pack2<OB>(ov[0], ov[1]), pack2<OB>(ov[2], ov[3]),
+                                                            pack2<OB>(ov[4], ov[5]), pack2<OB>(ov[6], ov[7]));
+              }
+            }
+          } else {
+            // Channels not one aligned run: element stores (channel list and
+            // gamma read through the cache).
+            const int* chq = p.ch + cur_qc * D;
+            const float* gq = gg + cur_qc * D;
+#pragma unroll
+            for (int nb = 0; nb < 2; ++nb) {
+              const int k = k0 + nb * 8 + 2 * t4;
+#pragma unroll
+              for (int hr = 0; hr < 2; ++hr) {
+                const int row = sRows[tile * 16 + g + 8 * hr];
+                if (row < 0) continue;
+                const float sc = scale ? scale[row / p.N] : 1.f;
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
-                  const int ch = sChs[k + e];
+                  const int ch = chq[k + e];
                   if (ch >= p.C) continue;
-                  const int64_t off = row * p.C + ch;
-                  float dv = e ? d1 : d0;
+                  const int64_t off = (int64_t)row * p.C + ch;
+                  float dv = cc[nb][2 * hr + e] * gq[k + e] * sc;
                   if (residual) dv += load_as<float>(x, off);
                   out[off] = Elem<TO>::from(dv);
                 }
@@ -620,10 +576,29 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const float* __restrict__ rstd, 
             }
           }
         }
-        comp_sync();
+        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 16 + 2 * tl);
       }
-      if (tid == 0 && it < 3) OW_TR(0, it * 32 + 14);
       tc_fence_before();
+      mbar_arrive(bar_epd + (it & 1));
+      if (tid == 0 && it < 3) OW_TR(0, it * 32 + 14);
+    };
+
+    if constexpr (EARLY) {
+      if (nit > 0) gate(0);
+      for (int it = 0; it < nit; ++it) {
+        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 0);
+        for (int q = 1; q < C::NQ; ++q) gate(it * C::NQ + q);
+        epi_prepare(it);
+        if (it + 1 < nit) gate((it + 1) * C::NQ);
+        epilogue(it);
+      }
+    } else {
+      for (int it = 0; it < nit; ++it) {
+        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 0);
+        for (int q = 0; q < C::NQ; ++q) gate(it * C::NQ + q);
+        epi_prepare(it);
+        epilogue(it);
+      }
     }
   }
 
@@ -663,7 +638,7 @@ int tc_prep(const ow_bigemm_args_t* a, const Prob& p, const TcWs<D>& w, unsigned
     launch(tc_prep_kernel<D, TW, BF16>, grid, 256, 0, st, p, (const TW*)a->a_u, (const TW*)a->a_v,
            (const TW*)a->a_o, (const TW*)a->b_u, (const TW*)a->b_v, (const TW*)a->b_o,
            (const TW*)a->gamma, (const TW*)(a->rstd ? a->norm_w : nullptr), base + w.img,
-           (uint16_t*)(base + w.amat), (float*)(base + w.gg), (float*)(base + w.nw),
+           (uint16_t*)(base + w.amat), (float*)(base + w.gg), (float*)(base + w.nwc),
            (int*)(base + w.contig));
   };
   switch (a->w_dtype) {
@@ -683,6 +658,10 @@ int tc_forward_t(const ow_bigemm_args_t* a, const Prob& p, cudaStream_t st, Carv
   unsigned char* base = (unsigned char*)ws.take(w.total);
   if (!ws.base) return OW_OK;
   OW_RETURN_IF((tc_prep<D, BF16>(a, p, w, base, st)));
+  profile_mark(OW_PROF_FPACK, false, st);
+  OW_RETURN_IF((tc_pack_forward(a, p, (const uint16_t*)(base + w.amat), (const float*)(base + w.nwc),
+                                (const int*)(base + w.contig), base + w.packed, st)));
+  profile_mark(OW_PROF_FPACK, true, st);
   const int64_t items = (int64_t)p.Qc * ((p.BQ() + 7) / 8);
   const int grid = (int)std::min<int64_t>(items, num_sms());
   // 16-byte vector loads/stores need aligned bases (channel runs are checked
@@ -698,9 +677,9 @@ int tc_forward_t(const ow_bigemm_args_t* a, const Prob& p, cudaStream_t st, Carv
       return OW_ERR_CUDA;
     }
     profile_mark(OW_PROF_FWD, false, st);
-    launch(kern, grid, TC_THREADS, Cfg<D>::SMEM, st, p, (const TX*)a->x, (const float*)a->rstd, a->x_dtype,
-           (const unsigned char*)(base + w.img), (const uint16_t*)(base + w.amat),
-           (const float*)(base + w.gg), (const float*)(base + w.nw), (const int*)(base + w.contig),
+    launch(kern, grid, TC_THREADS, Cfg<D>::SMEM, st, p, (const TX*)a->x,
+           (const unsigned char*)(base + w.packed), (const unsigned char*)(base + w.img),
+           (const uint16_t*)(base + w.amat), (const float*)(base + w.gg), (const int*)(base + w.contig),
            a->sample_scale, a->residual, (TO*)a->out, vec_ok);
     profile_mark(OW_PROF_FWD, true, st);
     OW_CHECK_LAUNCH("tc_fwd_kernel");

@@ -251,16 +251,6 @@ __device__ __forceinline__ uint64_t sdesc_sw128_mn(uint32_t addr, uint32_t lbo) 
          ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-// m16n8k16 A fragment of a 16x16 matrix in shared/global row-major 16-bit
-// storage (optionally transposed).
-__device__ __forceinline__ void load_afrag(const uint16_t* A, bool trans, int g, int t4, uint32_t (&f)[4]) {
-  auto el = [&](int m, int k) -> uint32_t { return trans ? A[k * 16 + m] : A[m * 16 + k]; };
-  f[0] = el(g, 2 * t4) | (el(g, 2 * t4 + 1) << 16);
-  f[1] = el(g + 8, 2 * t4) | (el(g + 8, 2 * t4 + 1) << 16);
-  f[2] = el(g, 2 * t4 + 8) | (el(g, 2 * t4 + 9) << 16);
-  f[3] = el(g + 8, 2 * t4 + 8) | (el(g + 8, 2 * t4 + 9) << 16);
-}
-
 template <typename T>
 __device__ __forceinline__ void load8v(const T* __restrict__ src, float (&v)[8]) {
   if constexpr (sizeof(T) == 2) {
@@ -522,7 +512,8 @@ struct BwdArgs {
 // half of an image is one 16 KB SW128 atom; it is built in shared memory and
 // written with one bulk copy, so the global writes are full lines.
 // ---------------------------------------------------------------------------
-template <int D, bool BF16, typename TX, typename TO>
+// FWD: the forward's pre-pass; writes only [P_u | P_v] per item (2 images).
+template <int D, bool BF16, typename TX, typename TO, bool FWD = false>
 __global__ void __launch_bounds__(NCOMP) tc_pack_kernel(BwdArgs a) {
   using C = BCfg<D>;
   constexpr int ATOM = BM * 128;  // one 64-channel half of an operand image
@@ -554,7 +545,8 @@ __global__ void __launch_bounds__(NCOMP) tc_pack_kernel(BwdArgs a) {
   for (int k = tid; k < D; k += NCOMP) sCh[k] = p.ch[qc * D + k];
   __syncthreads();
   GatherCtx gc{sRow, sCh, p.N, p.C, a.vec_ok && a.contig[qc] != 0};
-  unsigned char* out = a.packed + item * C::ITEM_BYTES;
+  // FWD item: [P_u | P_v | output row of each of the BM token rows (int32, -1: none)].
+  unsigned char* out = a.packed + item * (FWD ? 2 * C::P_BYTES + BM * 4 : C::ITEM_BYTES);
   const uint32_t aStg = smem_u32(stg);
   const TX* x = (const TX*)a.x;
   const TO* dout = (const TO*)a.dout;
@@ -582,13 +574,13 @@ __global__ void __launch_bounds__(NCOMP) tc_pack_kernel(BwdArgs a) {
     if (gc.cont) {
       RowRegs<TX, 1> rx;
       rows_issue<TX, 1>(rx, gc, x, hf, a.rstd, nullptr, tid);
-      rows_issue<TO, 1>(rg, gc, dout, hf, nullptr, a.scale, tid);
+      if (!FWD) rows_issue<TO, 1>(rg, gc, dout, hf, nullptr, a.scale, tid);
       rows_store<TX, 1, BF16>(rx, 0, hf, gc, stg, false, a.rstd != nullptr, a.nw, nullptr, a.x_dt, tid);
     } else {
       gather_half<TX, BF16>(gc, x, hf, a.rstd, a.nw, a.x_dt, nullptr, nullptr, stg, false, tid);
     }
     atoms_free();  // also publishes stg
-    to_atom(atom0);
+    if (!FWD) to_atom(atom0);
     {
       uint32_t f[4];
       load_afrag(a.amat, false, g, t4, f);
@@ -598,11 +590,13 @@ __global__ void __launch_bounds__(NCOMP) tc_pack_kernel(BwdArgs a) {
     }
     atoms_ready();
     if (tid == 0) {
-      bulk_s2g(out + C::PK_T * C::P_BYTES + hf * ATOM, atom0, ATOM);
+      if (!FWD) bulk_s2g(out + C::PK_T * C::P_BYTES + hf * ATOM, atom0, ATOM);
+      if (FWD && hf == 0) bulk_s2g(out + 2 * C::P_BYTES, sRow, BM * 4);
       bulk_s2g(out + hf * ATOM, atom1, ATOM);
       bulk_s2g(out + C::P_BYTES + hf * ATOM, atom2, ATOM);
       bulk_commit();
     }
+    if (FWD) continue;
     if (gc.cont) rows_store<TO, 1, BF16>(rg, 0, hf, gc, stg, false, false, nullptr, nullptr, 0, tid);
     else gather_half<TO, BF16>(gc, dout, hf, nullptr, nullptr, 0, a.scale, nullptr, stg, false, tid);
     atoms_free();
@@ -620,18 +614,6 @@ __global__ void __launch_bounds__(NCOMP) tc_pack_kernel(BwdArgs a) {
     }
   }
   if (tid == 0) bulk_wait_all();
-}
-
-__device__ __forceinline__ void tmem_ld16x256_x2(uint32_t taddr, uint32_t (&r)[8]) {
-  asm volatile("tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
-}
-
-__device__ __forceinline__ uint32_t movm_trans(uint32_t v) {
-  uint32_t o;
-  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(o) : "r"(v));
-  return o;
 }
 
 // ---------------------------------------------------------------------------
@@ -1252,27 +1234,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
                 mma16816<BF16>(cc[nb], fvT, bv0, bv1);
               }
               if (cont) {
-                // Quad exchange (4 x 4 transpose over the lanes of a quad, two
-                // xor stages): lane t4 ends with row g + 8 * (t4 >> 1), channels
-                // k0 + 8 * (t4 & 1) .. +8, so it stores one 16-byte (bf16) or
-                // 32-byte (f32) row piece.  V[d] is the pair this lane holds for
-                // quad lane d; W[s] the pair received from quad lane s.
-                const bool b0 = t4 & 1, b1 = t4 >> 1;
-                const float2 V0 = make_float2(cc[0][0], cc[0][1]), V1 = make_float2(cc[1][0], cc[1][1]);
-                const float2 V2 = make_float2(cc[0][2], cc[0][3]), V3 = make_float2(cc[1][2], cc[1][3]);
-                auto xchg = [&](float2 v, int m) {
-                  return make_float2(__shfl_xor_sync(0xffffffffu, v.x, m), __shfl_xor_sync(0xffffffffu, v.y, m));
-                };
-                // stage 1 (lane ^ 1): keep the pairs whose destination shares bit 0
-                const float2 ra = xchg(b0 ? V0 : V1, 1), rb = xchg(b0 ? V2 : V3, 1);
-                const float2 own_lo = b0 ? V1 : V0, own_hi = b0 ? V3 : V2;
-                const float2 ulo0 = b0 ? ra : own_lo, ulo1 = b0 ? own_lo : ra;  // by source bit 0
-                const float2 uhi0 = b0 ? rb : own_hi, uhi1 = b0 ? own_hi : rb;
-                // stage 2 (lane ^ 2): keep the pairs whose destination shares bit 1
-                const float2 r0 = xchg(b1 ? ulo0 : uhi0, 2), r1 = xchg(b1 ? ulo1 : uhi1, 2);
-                const float2 k0v = b1 ? uhi0 : ulo0, k1v = b1 ? uhi1 : ulo1;
-                const float2 W0 = b1 ? r0 : k0v, W1 = b1 ? r1 : k1v, W2 = b1 ? k0v : r0, W3 = b1 ? k1v : r1;
-                const float ov[8] = {W0.x, W0.y, W1.x, W1.y, W2.x, W2.y, W3.x, W3.y};
+                // Lane t4 stores row g + 8 (t4 >> 1), channels k0 + 8 (t4 & 1) .. +8.
+                float ov[8];
+                quad_rows8(cc, t4, ov);
                 const int rw = sRow[tile * 16 + g + 8 * (t4 >> 1)];
                 if (rw >= 0) {
                   const int64_t off = (int64_t)rw * p.C + sCh[0] + k0 + 8 * (t4 & 1);
@@ -1680,6 +1644,56 @@ int tc_backward_t(const ow_bigemm_args_t* ar, const ow_bigemm_grads_t* gr, const
 }
 
 }  // namespace
+
+namespace {
+template <int D, bool BF16>
+int tc_pack_forward_t(const ow_bigemm_args_t* ar, const Prob& p, const uint16_t* amat, const float* nwc,
+                      const int* contig, unsigned char* packed, cudaStream_t st) {
+  BwdArgs a{};
+  a.p = p;
+  a.x = ar->x;
+  a.rstd = (const float*)ar->rstd;
+  a.x_dt = ar->x_dtype;
+  a.amat = amat;
+  a.nw = nwc;
+  a.contig = contig;
+  a.vec_ok = ((uintptr_t)ar->x % 16 == 0) && (p.C % 8 == 0);
+  a.packed = packed;
+  const int64_t items = (int64_t)p.Qc * ((p.BQ() + 7) / 8);
+  if (items == 0) return OW_OK;
+  constexpr int pack_smem = 3 * BM * 128 + STG_BYTES + (BM + D) * 4 + 128;
+  auto go = [&](auto* tx) -> int {
+    using TX = std::remove_pointer_t<decltype(tx)>;
+    auto pk = tc_pack_kernel<D, BF16, TX, TX, true>;
+    cudaError_t e = cudaFuncSetAttribute(pk, cudaFuncAttributeMaxDynamicSharedMemorySize, pack_smem);
+    if (e != cudaSuccess) {
+      set_error("tc forward: cannot reserve %d bytes of shared memory for the pack kernel: %s", pack_smem,
+                cudaGetErrorString(e));
+      return OW_ERR_CUDA;
+    }
+    launch(pk, (int)items, NCOMP, pack_smem, st, a);
+    OW_CHECK_LAUNCH("tc_pack_kernel (forward)");
+    return OW_OK;
+  };
+  using T16 = std::conditional_t<BF16, __nv_bfloat16, __half>;
+  const int c16 = BF16 ? OW_DTYPE_BF16 : OW_DTYPE_F16;
+  if (ar->x_dtype == c16) return go((T16*)nullptr);
+  if (ar->x_dtype == OW_DTYPE_F32) return go((float*)nullptr);
+  set_error("tc forward: unsupported x dtype %s", dtype_name(ar->x_dtype));
+  return OW_ERR_UNSUPPORTED;
+}
+}  // namespace
+
+int tc_pack_forward(const ow_bigemm_args_t* a, const Prob& p, const uint16_t* amat, const float* nwc,
+                    const int* contig, unsigned char* packed, void* stream) {
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool bf = a->compute_dtype == OW_DTYPE_BF16;
+  if (p.d == 64)
+    return bf ? tc_pack_forward_t<64, true>(a, p, amat, nwc, contig, packed, st)
+              : tc_pack_forward_t<64, false>(a, p, amat, nwc, contig, packed, st);
+  return bf ? tc_pack_forward_t<128, true>(a, p, amat, nwc, contig, packed, st)
+            : tc_pack_forward_t<128, false>(a, p, amat, nwc, contig, packed, st);
+}
 
 int tc_backward(const ow_bigemm_args_t* a, const ow_bigemm_grads_t* gr, const Prob& p, void* stream,
                 Carver& ws) {

@@ -47,7 +47,7 @@ def test_profile_events_checks_kernel_id():
     lib = _lib.load()
     assert lib.ow_profile_events(7, None, None) == 1  # OW_ERR_INVALID
     assert "unknown kernel" in lib.ow_last_error().decode()
-    for k in (0, 1, 2):  # NULL events: recording off, nothing touches CUDA
+    for k in (0, 1, 2, 3):  # NULL events: recording off, nothing touches CUDA
         assert lib.ow_profile_events(k, None, None) == 0
 
 
