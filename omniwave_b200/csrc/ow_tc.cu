@@ -75,7 +75,10 @@ struct Cfg {
   static constexpr int OFF_WO = OFF_WUV + 2 * WUV_BYTES;  // streaming: 2 x Bo
   static constexpr int W_END = RES ? OFF_W + 2 * GRP_BYTES : OFF_WO + 2 * WO_BYTES;
   static constexpr int OFF_ROWS = W_END;                  // 2 x ROWS_BYTES
-  static constexpr int OFF_BAR = OFF_ROWS + 2 * ROWS_BYTES;
+  static constexpr int ST_LD = 72;                         // epilogue staging row stride (f32): 64 + 8 pad
+  static constexpr int STG_WARP = 8 * ST_LD * 4;           // per compute warp: 8 rows x 64 channels
+  static constexpr int OFF_STG = OFF_ROWS + 2 * ROWS_BYTES;
+  static constexpr int OFF_BAR = OFF_STG + 8 * STG_WARP;
   static constexpr int NBAR = 22;
   static constexpr int BAR_BYTES = NBAR * 8 + 16;
   static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024;  // + alignment slack
@@ -175,7 +178,7 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict_
               int residual, TO* __restrict__ out, int vec_ok) {
   using C = Cfg<D>;
   constexpr bool EARLY = C::RES;  // next item's first gate before this item's epilogue
-  constexpr bool QUIET_Y = true;  // early order: hold Y(item, 0) until the previous epilogue is done
+  constexpr bool QUIET_Y = false;  // early order: hold Y(item, 0) until the previous epilogue is done
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   unsigned char* sZ = sm + C::OFF_Z;
@@ -386,22 +389,21 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict_
     uint32_t fo[4];  // A_o as an m16n8k16 A fragment
     load_afrag(amat + 512, false, g, t4, fo);
     // Gate: warp (lq, hw) reads TMEM lanes 32 lq .. +31, columns 32 hw .. +31
-    // of a chunk.  Epilogue: the same warp owns tiles 2 lq, 2 lq + 1 and
-    // channels [hw D / 2, (hw + 1) D / 2); after the quad exchange a lane
-    // stores row rsel of a tile, channels csel .. csel + 7 of each 16-channel
-    // step.
+    // of a chunk.  Epilogue: the same warp owns tile 2 lq + hw (TMEM lanes
+    // 32 lq + 16 hw .. +15) and all D channels.
     const int lq = warp & 3, hw = warp >> 2;
     const int r = lq * 32 + lane, cb = hw * 32;
     const uint32_t trow = tbase + ((uint32_t)(lq * 32) << 16);
-    constexpr int NP = D / 32;                   // 16-channel steps per warp
-    constexpr int VW = sizeof(TX) == 2 ? 1 : 2;  // 16-byte vectors per 8 elements of x
-    const int rsel = g + 8 * (t4 >> 1), csel = 8 * (t4 & 1);
+    const int tile_e = 2 * lq + hw;
+    constexpr int NP = D / 16;  // 16-channel steps of the epilogue
+    constexpr int NH = D / 64;  // 64-channel passes
+    float* stg = reinterpret_cast<float*>(sm + C::OFF_STG + warp * C::STG_WARP);
 
     // Channel-group state, reloaded when the group changes (rarely: items
     // are walked group-major).
     int cur_qc = -1, ch0 = 0;
     bool cont = false;
-    float gam[NP][8];
+    float gam[NP][4];  // gamma of channels np 16 + nb 8 + 2 t4 + e at [np][2 nb + e]
     auto set_group = [&](int qc) {
       if (qc == cur_qc) return;
       cur_qc = qc;
@@ -410,7 +412,7 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict_
 #pragma unroll
       for (int np = 0; np < NP; ++np)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) gam[np][e] = gg[qc * D + hw * (D / 2) + np * 16 + csel + e];
+        for (int e = 0; e < 4; ++e) gam[np][e] = gg[qc * D + np * 16 + (e >> 1) * 8 + 2 * t4 + (e & 1)];
     };
 
     // -------- gate: Z_x = silu(U_x) * V_x for chunk x
@@ -447,37 +449,49 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict_
       mbar_arrive(bar_z + s);
     };
 
-    // -------- epilogue state of one item: its output rows, sample scales and
-    // residual values (requested ahead of use; pad rows read row 0 and are
-    // never stored, so no load waits for a comparison).
-    int rowr[2];
-    float scr[2];
-    uint4 xres[2][NP][VW];
+    // -------- epilogue state of one item: the output rows of this warp's
+    // tile (C-fragment rows g, g + 8), their sample scales, and the residual
+    // of the first staged half-pass (requested ahead of use; pad rows read
+    // row 0 and are never stored, so no load waits for a comparison).
+    int rowf[2];
+    float scf[2];
+    uint4 xb[2][4];
+    const int* sRowsE = nullptr;
+    // Residual of half-pass sp (64-channel pass sp >> 1, tile rows 8 (sp & 1)
+    // .. +8) in the read-back layout: lane handles row 8 (sp & 1) + ((i * 32 +
+    // lane) >> 4), channels 4 (lane & 15) .. +4 of the pass, for i < 4.
+    auto xload = [&](int sp, uint4 (&dst)[4]) {
+      const int hf = sp >> 1, hr = sp & 1;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int rw = sRowsE[tile_e * 16 + hr * 8 + ((i * 32 + lane) >> 4)];
+        const int64_t off = (int64_t)(rw >= 0 ? rw : 0) * p.C + ch0 + hf * 64 + (lane & 15) * 4;
+        if constexpr (sizeof(TX) == 2) {
+          const uint2 v = __ldg(reinterpret_cast<const uint2*>(x + off));
+          dst[i] = make_uint4(v.x, v.y, 0u, 0u);
+        } else {
+          dst[i] = __ldg(reinterpret_cast<const uint4*>(x + off));
+        }
+      }
+    };
     auto epi_prepare = [&](int it) {
       const int sl = it & 1;
       set_group(qc_of(it));
       mbar_wait(bar_m + sl, (it >> 1) & 1, sAbort);
-      const int* sRows = reinterpret_cast<const int*>(sm + C::OFF_ROWS + sl * C::ROWS_BYTES);
+      sRowsE = reinterpret_cast<const int*>(sm + C::OFF_ROWS + sl * C::ROWS_BYTES);
 #pragma unroll
-      for (int tl = 0; tl < 2; ++tl) {
-        rowr[tl] = sRows[(2 * lq + tl) * 16 + rsel];
-        scr[tl] = scale ? scale[(rowr[tl] >= 0 ? rowr[tl] : 0) / p.N] : 1.f;
+      for (int hr = 0; hr < 2; ++hr) {
+        rowf[hr] = sRowsE[tile_e * 16 + g + 8 * hr];
+        scf[hr] = scale ? scale[(rowf[hr] >= 0 ? rowf[hr] : 0) / p.N] : 1.f;
       }
-      if (cont && residual) {
-#pragma unroll
-        for (int tl = 0; tl < 2; ++tl) {
-          const int64_t row = rowr[tl] >= 0 ? rowr[tl] : 0;
-#pragma unroll
-          for (int np = 0; np < NP; ++np) {
-            const uint4* src = reinterpret_cast<const uint4*>(x + row * p.C + ch0 + hw * (D / 2) + np * 16 + csel);
-#pragma unroll
-            for (int vv = 0; vv < VW; ++vv) xres[tl][np][vv] = __ldg(src + vv);
-          }
-        }
-      }
+      if (cont && residual) xload(0, xb[0]);
     };
 
-    // -------- epilogue: delta = A_o Y, gamma, sample scale, residual
+    // -------- epilogue: delta = A_o Y, gamma, sample scale, residual.  Per
+    // 64-channel pass the warp MMA results (C-fragment layout) are scaled by
+    // gamma and the row's sample scale, and each half (rows g / g + 8) goes
+    // through the warp's f32 staging tile so that 16 lanes write one
+    // 128-byte row segment (bf16) with the residual added on the way out.
     auto epilogue = [&](int it) {
       const int yb = it & 1, cl = it * C::NQ + C::NQ - 1;
       if (tid == 0 && it < 3) OW_TR(0, it * 32 + 12);
@@ -485,99 +499,102 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict_
       if (tid == 0 && it < 3) OW_TR(0, it * 32 + 13);
       __syncwarp();
       tc_fence_after();
-      const int* sRows = reinterpret_cast<const int*>(sm + C::OFF_ROWS + (it & 1) * C::ROWS_BYTES);
-      // Y of both tiles in the C-fragment layout, one wait.
-      uint32_t yv[2][NP][8];
+      const int* sRows = sRowsE;
+      const uint32_t ta = tbase + ((uint32_t)(tile_e * 16) << 16) + C::T_Y(yb);
+      uint32_t yv[NP][8];
 #pragma unroll
-      for (int tl = 0; tl < 2; ++tl) {
-        const uint32_t ta = tbase + ((uint32_t)((2 * lq + tl) * 16) << 16) + C::T_Y(yb) + hw * (D / 2);
-#pragma unroll
-        for (int np = 0; np < NP; ++np) tmem_ld16x256_x2(ta + np * 16, yv[tl][np]);
-      }
+      for (int np = 0; np < NP; ++np) tmem_ld16x256_x2(ta + np * 16, yv[np]);
       tmem_ld_wait();
       if (tid == 0 && it < 3) OW_TR(0, it * 32 + 15);
+      const bool res_vec = cont && residual;
 #pragma unroll
-      for (int tl = 0; tl < 2; ++tl) {
-        const int tile = 2 * lq + tl;
+      for (int hf = 0; hf < NH; ++hf) {
+        float cc[4][2][4];  // [16-channel step][channel block nb][C fragment]
 #pragma unroll
-        for (int np = 0; np < NP; ++np) {
-          const int k0 = hw * (D / 2) + np * 16;
+        for (int n4 = 0; n4 < 4; ++n4) {
+          const int np = hf * 4 + n4;
           uint32_t ay[4];
 #pragma unroll
           for (int q = 0; q < 4; ++q)
-            ay[q] = pack2<BF16>(__uint_as_float(yv[tl][np][2 * q]), __uint_as_float(yv[tl][np][2 * q + 1]));
-          float cc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};  // channel blocks nb = 0, 1
+            ay[q] = pack2<BF16>(__uint_as_float(yv[np][2 * q]), __uint_as_float(yv[np][2 * q + 1]));
 #pragma unroll
-          for (int nb = 0; nb < 2; ++nb)
-            mma16816<BF16>(cc[nb], fo, movm_trans(ay[2 * nb]), movm_trans(ay[2 * nb + 1]));
-          if (cont) {
-            float ov[8];
-            quad_rows8(cc, t4, ov);
-            if (rowr[tl] >= 0) {
-              const float sc = scr[tl];
+          for (int nb = 0; nb < 2; ++nb) {
+            cc[n4][nb][0] = cc[n4][nb][1] = cc[n4][nb][2] = cc[n4][nb][3] = 0.f;
+            mma16816<BF16>(cc[n4][nb], fo, movm_trans(ay[2 * nb]), movm_trans(ay[2 * nb + 1]));
+          }
+        }
+        if (cont) {
 #pragma unroll
-              for (int e = 0; e < 8; ++e) ov[e] = ov[e] * gam[np][e] * sc;
-              if (residual) {
-                float xv[8];
-                if constexpr (sizeof(TX) == 2) {
-                  const uint32_t w[4] = {xres[tl][np][0].x, xres[tl][np][0].y, xres[tl][np][0].z,
-                                         xres[tl][np][0].w};
+          for (int hr = 0; hr < 2; ++hr) {
+            const int sp = hf * 2 + hr;
+            if (res_vec && sp + 1 < 2 * NH) xload(sp + 1, xb[(sp + 1) & 1]);
+            const float sc = scf[hr];
 #pragma unroll
-                  for (int i = 0; i < 4; ++i) {
-                    const float2 f = unpack2<std::is_same_v<TX, __nv_bfloat16>>(w[i]);
-                    xv[2 * i] = f.x;
-                    xv[2 * i + 1] = f.y;
-                  }
-                } else {
+            for (int n4 = 0; n4 < 4; ++n4)
 #pragma unroll
-                  for (int vv = 0; vv < 2; ++vv) {
-                    xv[4 * vv + 0] = __uint_as_float(xres[tl][np][vv].x);
-                    xv[4 * vv + 1] = __uint_as_float(xres[tl][np][vv].y);
-                    xv[4 * vv + 2] = __uint_as_float(xres[tl][np][vv].z);
-                    xv[4 * vv + 3] = __uint_as_float(xres[tl][np][vv].w);
-                  }
-                }
-#pragma unroll
-                for (int e = 0; e < 8; ++e) ov[e] += xv[e];
+              for (int nb = 0; nb < 2; ++nb) {
+                const float* gm = gam[hf * 4 + n4] + 2 * nb;
+                *reinterpret_cast<float2*>(stg + g * C::ST_LD + n4 * 16 + nb * 8 + 2 * t4) =
+                    make_float2(cc[n4][nb][2 * hr] * gm[0] * sc, cc[n4][nb][2 * hr + 1] * gm[1] * sc);
               }
-              TO* dst = out + (int64_t)rowr[tl] * p.C + ch0 + k0 + csel;
-              if constexpr (std::is_same_v<TO, float>) {
-                reinterpret_cast<float4*>(dst)[0] = make_float4(ov[0], ov[1], ov[2], ov[3]);
-                reinterpret_cast<float4*>(dst)[1] = make_float4(ov[4], ov[5], ov[6], ov[7]);
-              } else {
-                constexpr bool OB = std::is_same_v<TO, __nv_bfloat16>;
-                *reinterpret_cast<uint4*>(dst) = make_uint4(pack2<OB>(ov[0], ov[1]), pack2<OB>(ov[2], ov[3]),
-                                                            pack2<OB>(ov[4], ov[5]), pack2<OB>(ov[6], ov[7]));
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int r8 = (i * 32 + lane) >> 4, c4 = (lane & 15) * 4;
+              const float4 a = *reinterpret_cast<const float4*>(stg + r8 * C::ST_LD + c4);
+              float ov[4] = {a.x, a.y, a.z, a.w};
+              if (residual) {
+                const uint4 xv = xb[sp & 1][i];
+                if constexpr (sizeof(TX) == 2) {
+                  const float2 f0 = unpack2<std::is_same_v<TX, __nv_bfloat16>>(xv.x);
+                  const float2 f1 = unpack2<std::is_same_v<TX, __nv_bfloat16>>(xv.y);
+                  ov[0] += f0.x; ov[1] += f0.y; ov[2] += f1.x; ov[3] += f1.y;
+                } else {
+                  ov[0] += __uint_as_float(xv.x); ov[1] += __uint_as_float(xv.y);
+                  ov[2] += __uint_as_float(xv.z); ov[3] += __uint_as_float(xv.w);
+                }
+              }
+              const int rw = sRows[tile_e * 16 + hr * 8 + r8];
+              if (rw >= 0) {
+                TO* dst = out + (int64_t)rw * p.C + ch0 + hf * 64 + c4;
+                if constexpr (std::is_same_v<TO, float>) {
+                  *reinterpret_cast<float4*>(dst) = make_float4(ov[0], ov[1], ov[2], ov[3]);
+                } else {
+                  constexpr bool OB = std::is_same_v<TO, __nv_bfloat16>;
+                  *reinterpret_cast<uint2*>(dst) = make_uint2(pack2<OB>(ov[0], ov[1]), pack2<OB>(ov[2], ov[3]));
+                }
               }
             }
-          } else {
-            // Channels not one aligned run: element stores (channel list and
-            // gamma read through the cache).
-            const int* chq = p.ch + cur_qc * D;
-            const float* gq = gg + cur_qc * D;
+            __syncwarp();  // the staging tile is rewritten by the next half-pass
+          }
+        } else {
+          // Channels not one aligned run: element stores (channel list and
+          // gamma read through the cache).
+          const int* chq = p.ch + cur_qc * D;
+          const float* gq = gg + cur_qc * D;
+#pragma unroll
+          for (int n4 = 0; n4 < 4; ++n4)
 #pragma unroll
             for (int nb = 0; nb < 2; ++nb) {
-              const int k = k0 + nb * 8 + 2 * t4;
+              const int k = (hf * 4 + n4) * 16 + nb * 8 + 2 * t4;
 #pragma unroll
               for (int hr = 0; hr < 2; ++hr) {
-                const int row = sRows[tile * 16 + g + 8 * hr];
+                const int row = rowf[hr];
                 if (row < 0) continue;
-                const float sc = scale ? scale[row / p.N] : 1.f;
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
                   const int ch = chq[k + e];
                   if (ch >= p.C) continue;
                   const int64_t off = (int64_t)row * p.C + ch;
-                  float dv = cc[nb][2 * hr + e] * gq[k + e] * sc;
+                  float dv = cc[n4][nb][2 * hr + e] * gq[k + e] * scf[hr];
                   if (residual) dv += load_as<float>(x, off);
                   out[off] = Elem<TO>::from(dv);
                 }
               }
             }
-          }
         }
-        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 16 + 2 * tl);
       }
+      if (tid == 0 && it < 3) OW_TR(0, it * 32 + 16);
       tc_fence_before();
       mbar_arrive(bar_epd + (it & 1));
       if (tid == 0 && it < 3) OW_TR(0, it * 32 + 14);
