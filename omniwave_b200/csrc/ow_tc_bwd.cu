@@ -520,10 +520,13 @@ __global__ void __launch_bounds__(NCOMP) tc_pack_kernel(BwdArgs a) {
   const Prob& p = a.p;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
-  unsigned char* atom0 = sm;             // T, then G'
-  unsigned char* atom1 = sm + ATOM;      // P_u, then H
-  unsigned char* atom2 = sm + 2 * ATOM;  // P_v
-  unsigned char* stg = sm + 3 * ATOM;    // gathered half, row-major
+  // The forward mode needs no third atom: a smaller footprint lets more
+  // CTAs share an SM.
+  constexpr int NATOM = FWD ? 2 : 3;
+  unsigned char* atom1 = sm;             // P_u, then H
+  unsigned char* atom2 = sm + ATOM;      // P_v
+  unsigned char* atom0 = sm + 2 * ATOM;  // T, then G' (not in the forward mode)
+  unsigned char* stg = sm + NATOM * ATOM;  // gathered half, row-major
   int* sRow = reinterpret_cast<int*>(stg + STG_BYTES);
   int* sCh = sRow + BM;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1661,7 +1664,7 @@ int tc_pack_forward_t(const ow_bigemm_args_t* ar, const Prob& p, const uint16_t*
   a.packed = packed;
   const int64_t items = (int64_t)p.Qc * ((p.BQ() + 7) / 8);
   if (items == 0) return OW_OK;
-  constexpr int pack_smem = 3 * BM * 128 + STG_BYTES + (BM + D) * 4 + 128;
+  constexpr int pack_smem = 2 * BM * 128 + STG_BYTES + (BM + D) * 4 + 128;
   auto go = [&](auto* tx) -> int {
     using TX = std::remove_pointer_t<decltype(tx)>;
     auto pk = tc_pack_kernel<D, BF16, TX, TX, true>;
