@@ -40,6 +40,9 @@
 // warp that owns TMEM, one producer warp issuing the bulk copies.
 
 #include <algorithm>
+#include <array>
+#include <map>
+#include <mutex>
 #include <cmath>
 #include <type_traits>
 
@@ -146,16 +149,40 @@ struct BPlan {
   BPlan(const Prob& p, bool block, int sms) {
     using C = BCfg<D>;
     nH = C::NH;
-    // Split one wave of CTAs across the roles in proportion to each role's
-    // time per item (UV summed over its halves), as measured on B200 with the
-    // kernel's timeline trace: DGRAD : UV : O = 1 : 0.67 : 0.59 at d = 64 and
-    // 1 : 0.90 : 0.76 at d = 128.
-    const double wD = 1.0, wU = D == 64 ? 0.67 : 0.90, wO = D == 64 ? 0.59 : 0.76, tot = wD + wU + wO;
+    // Split one wave of CTAs across the roles so that the slowest role
+    // finishes first: each role's time is its items per CTA times its time
+    // per item, measured on B200 with the kernel's timeline trace (us per
+    // item; UV per 128-feature half): DGRAD 5.69, UV 3.82, O 3.86 at d = 64;
+    // 17.5, 7.97, 13.7 at d = 128.  Every split of one wave is tried.
+    const double tD = D == 64 ? 5.69 : 17.5, tU = D == 64 ? 3.82 : 7.97, tO = D == 64 ? 3.86 : 13.7;
     const int64_t nMB = (p.BQ() + 7) / 8;
-    nUVq = std::max(1, (int)std::lround(sms * wU / tot / (nH * p.Qc)));
-    nOq = std::max(1, (int)std::lround(sms * wO / tot / p.Qc));
-    nUVq = (int)std::min<int64_t>(nUVq, nMB);
-    nOq = (int)std::min<int64_t>(nOq, nMB);
+    // The search is a few thousand steps; its result is kept per shape.
+    static std::mutex mu;
+    static std::map<std::array<int64_t, 4>, std::pair<int, int>> memo;
+    const std::array<int64_t, 4> key{nMB, p.Qc, nH, sms};
+    {
+      std::lock_guard<std::mutex> lk(mu);
+      auto f = memo.find(key);
+      if (f != memo.end()) {
+        nUVq = f->second.first;
+        nOq = f->second.second;
+      } else {
+        double best = -1.0;
+        nUVq = nOq = 1;
+        for (int u = 1; u <= nMB && nH * p.Qc * u + p.Qc + 1 <= sms; ++u)
+          for (int o = 1; o <= nMB && nH * p.Qc * u + p.Qc * o + 1 <= sms; ++o) {
+            const int64_t d = std::min<int64_t>(sms - nH * p.Qc * u - p.Qc * o, nMB * p.Qc);
+            const double t = std::max({tD * (double)((nMB * p.Qc + d - 1) / d),
+                                       tU * (double)((nMB + u - 1) / u), tO * (double)((nMB + o - 1) / o)});
+            if (best < 0.0 || t < best) {
+              best = t;
+              nUVq = u;
+              nOq = o;
+            }
+          }
+        memo.emplace(key, std::make_pair(nUVq, nOq));
+      }
+    }
     nD = std::max(1, sms - nH * p.Qc * nUVq - p.Qc * nOq);
     nD = (int)std::min<int64_t>(nD, nMB * p.Qc);
     grid = nD + nH * p.Qc * nUVq + p.Qc * nOq;
@@ -1133,18 +1160,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
             uint32_t wu[4], wv[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              float du[2], dv[2];
-#pragma unroll
-              for (int h2 = 0; h2 < 2; ++h2) {
-                const int i = jj * 8 + 2 * e + h2;
-                const float u = __uint_as_float(ur[i]), v = __uint_as_float(vr[i]), dz = __uint_as_float(zr[i]);
-                const float s = sigm_fast(u);
-                const float ds = dz * s;
-                dv[h2] = ds * u;
-                du[h2] = ds * v * fmaf(-u, s, u + 1.f);
-              }
-              wu[e] = pack2<BF16>(du[0], du[1]);
-              wv[e] = pack2<BF16>(dv[0], dv[1]);
+              // Two features at a time in packed f32x2 arithmetic:
+              // s = sigmoid(u), dV = dZ s u, dU = dZ s v (1 + u (1 - s)).
+              const int i = jj * 8 + 2 * e;
+              const uint64_t u2 = f2pack(__uint_as_float(ur[i]), __uint_as_float(ur[i + 1]));
+              const uint64_t v2 = f2pack(__uint_as_float(vr[i]), __uint_as_float(vr[i + 1]));
+              const uint64_t z2 = f2pack(__uint_as_float(zr[i]), __uint_as_float(zr[i + 1]));
+              const uint64_t half = f2pack(0.5f, 0.5f), nhalf = f2pack(-0.5f, -0.5f), one = f2pack(1.f, 1.f);
+              const float2 h = f2unpack(mul2(u2, half));
+              float t0, t1;
+              asm("tanh.approx.f32 %0, %1;" : "=f"(t0) : "f"(h.x));
+              asm("tanh.approx.f32 %0, %1;" : "=f"(t1) : "f"(h.y));
+              const uint64_t t2 = f2pack(t0, t1);
+              const uint64_t s2 = fma2(t2, half, half);      // sigmoid(u)
+              const uint64_t oms = fma2(t2, nhalf, half);    // 1 - sigmoid(u)
+              const uint64_t ds2 = mul2(z2, s2);
+              const float2 dv = f2unpack(mul2(ds2, u2));
+              const float2 du = f2unpack(mul2(mul2(ds2, v2), fma2(u2, oms, one)));
+              wu[e] = pack2<BF16>(du.x, du.y);
+              wv[e] = pack2<BF16>(dv.x, dv.y);
             }
             const uint32_t off = sw128_off(r, col0 + cb + jj * 8, BM);
             *reinterpret_cast<uint4*>(du_at + off) = make_uint4(wu[0], wu[1], wu[2], wu[3]);
