@@ -1477,6 +1477,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
 // ---------------------------------------------------------------------------
 // dB_u, dB_v [qc][c][e] and M_o -> dB_o [qc][e][c]: one thread per output,
 // consecutive threads on consecutive c so the partial reads coalesce.
+// Sum of at(0) + at(1) + ... + at(n - 1) in that order (bitwise reproducible),
+// with the loads requested eight at a time so their latencies overlap.
+template <typename F>
+__device__ __forceinline__ float sum_in_order(int64_t n, F at) {
+  float s = 0.f;
+  for (int64_t j = 0; j < n; j += 8) {
+    float v[8];
+    // Unconditional loads from a clamped index; only the first n terms count.
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = at(j + k < n ? j + k : n - 1);
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (j + k < n) s += v[k];
+  }
+  return s;
+}
+
 template <int D, typename TW>
 __global__ void tc_bwd_reduce_b_kernel(Prob p, BwdArgs a, TW* __restrict__ db_u, TW* __restrict__ db_v,
                                        TW* __restrict__ db_o, float* __restrict__ mo) {
@@ -1489,14 +1506,15 @@ __global__ void tc_bwd_reduce_b_kernel(Prob p, BwdArgs a, TW* __restrict__ db_u,
     const int rem = i - m * nB;
     const int qc = rem / (C::RD * D);
     const int e = (rem / D) % C::RD, c = rem % D;
-    float s = 0.f;
     if (m < 2) {
       const int hh = e / 128, el = e % 128;
-      for (int j = 0; j < a.nUVq; ++j)
-        s += a.puv[((((int64_t)(hh * p.Qc + qc) * a.nUVq + j) * 2 + m) * 128 + el) * D + c];
+      const float* src = a.puv + ((((int64_t)(hh * p.Qc + qc) * a.nUVq) * 2 + m) * 128 + el) * D + c;
+      const int64_t st = (int64_t)2 * 128 * D;
+      const float s = sum_in_order(a.nUVq, [&](int64_t j) { return __ldg(src + j * st); });
       (m ? db_v : db_u)[((int64_t)qc * D + c) * C::RD + e] = Elem<TW>::from(s);
     } else {
-      for (int j = 0; j < a.nOq; ++j) s += a.po[((int64_t)qc * a.nOq + j) * C::RD * D + (int64_t)e * D + c];
+      const float* src = a.po + (int64_t)qc * a.nOq * C::RD * D + (int64_t)e * D + c;
+      const float s = sum_in_order(a.nOq, [&](int64_t j) { return __ldg(src + j * (int64_t)C::RD * D); });
       mo[rem] = s;
       db_o[rem] = Elem<TW>::from(s * a.gg[(int64_t)qc * D + c]);
     }
@@ -1524,19 +1542,29 @@ __global__ void tc_bwd_reduce_small_kernel(Prob p, BwdArgs a, const TW* __restri
     float s = 0.f;
     if (w < n_gamma) {
       const int qc = (int)(w / D), c = (int)(w % D);
-      for (int e = lane; e < C::RD; e += 32)
-        s += load_as<float>(bo, ((int64_t)qc * C::RD + e) * D + c) * mo[((int64_t)qc * C::RD + e) * D + c];
+      float bv[C::RD / 32], mv[C::RD / 32];
+#pragma unroll
+      for (int k = 0; k < C::RD / 32; ++k) {
+        const int64_t idx = ((int64_t)qc * C::RD + lane + 32 * k) * D + c;
+        bv[k] = load_as<float>(bo, idx);
+        mv[k] = mo[idx];
+      }
+#pragma unroll
+      for (int k = 0; k < C::RD / 32; ++k) s += bv[k] * mv[k];
       s = warp_sum(s);
       const int ch = p.ch[w];
       if (lane == 0 && ch < p.C) dgamma[ch] = Elem<TW>::from(s);
     } else {
       const int m = (int)((w - n_gamma) / 256), e = (int)((w - n_gamma) % 256);
+      // Lane l sums partials l, l + 32, ... in order, then a fixed butterfly.
       if (m < 2) {
         const int64_t n = (int64_t)a.nD * NCOMP_WARPS;
-        for (int64_t b = lane; b < n; b += 32) s += a.pdA[b * 512 + m * 256 + e];
+        const float* src = a.pdA + (int64_t)lane * 512 + m * 256 + e;
+        s = sum_in_order(n > lane ? (n - 1 - lane) / 32 + 1 : 0, [&](int64_t k) { return __ldg(src + k * 32 * 512); });
       } else {
         const int64_t n = (int64_t)p.Qc * a.nOq * NCOMP_WARPS;
-        for (int64_t b = lane; b < n; b += 32) s += a.pdAo[b * 256 + e];
+        const float* src = a.pdAo + (int64_t)lane * 256 + e;
+        s = sum_in_order(n > lane ? (n - 1 - lane) / 32 + 1 : 0, [&](int64_t k) { return __ldg(src + k * 32 * 256); });
       }
       s = warp_sum(s);
       if (lane == 0) (m == 0 ? da_u : (m == 1 ? da_v : da_o))[e] = Elem<TW>::from(s);
@@ -1661,7 +1689,8 @@ int tc_backward_t(const ow_bigemm_args_t* ar, const ow_bigemm_grads_t* gr, const
   auto red = [&](auto* tw) {
     using TW = std::remove_pointer_t<decltype(tw)>;
     float* mo = (float*)(base + pl.mo);
-    launch(tc_bwd_reduce_b_kernel<D, TW>, 148 * 8, 256, 0, st, p, a, (TW*)gr->db_u, (TW*)gr->db_v,
+    launch(tc_bwd_reduce_b_kernel<D, TW>, (int)std::min<int64_t>((3LL * p.Qc * D * 2 * D + 255) / 256, 148 * 32), 256,
+           0, st, p, a, (TW*)gr->db_u, (TW*)gr->db_v,
            (TW*)gr->db_o, mo);
     launch(tc_bwd_reduce_small_kernel<D, TW>, 148, 256, 0, st, p, a, (const TW*)ar->b_o, (const float*)mo,
            (TW*)gr->dgamma, (TW*)gr->da_u, (TW*)gr->da_v, (TW*)gr->da_o);
