@@ -560,8 +560,11 @@ __global__ void __launch_bounds__(NCOMP) tc_pack_kernel(BwdArgs a) {
   const int g = lane >> 2, t4 = lane & 3;
   const int64_t BQ = (int64_t)p.B * p.Qs;
   const int nMB = (int)((BQ + 7) / 8);
-  const int64_t item = blockIdx.x;
-  const int qc = (int)(item / nMB), mb = (int)(item - (int64_t)qc * nMB);
+  // CTAs run M-block-major (all channel groups of one M-block in a row), so
+  // the groups of a token row are gathered close together in time and share
+  // DRAM pages; the images stay in channel-group-major item order.
+  const int mb = (int)(blockIdx.x / p.Qc), qc = (int)(blockIdx.x - (int64_t)mb * p.Qc);
+  const int64_t item = (int64_t)qc * nMB + mb;
   for (int r = tid; r < BM; r += NCOMP) {
     const int64_t t = (int64_t)mb * 8 + (r >> 4);
     int rw = -1;
