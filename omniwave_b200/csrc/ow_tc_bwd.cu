@@ -152,9 +152,9 @@ struct BPlan {
     // Split one wave of CTAs across the roles so that the slowest role
     // finishes first: each role's time is its items per CTA times its
     // steady-state time per item, measured on B200 from each CTA's finish
-    // time (us per item; UV per 128-feature half): DGRAD 5.0, UV 3.0, O 3.7 at
-    // d = 64; 18.3, 8.1, 15.3 at d = 128.  Every split of one wave is tried.
-    const double tD = D == 64 ? 5.0 : 18.3, tU = D == 64 ? 3.0 : 8.1, tO = D == 64 ? 3.7 : 15.3;
+    // time (us per item; UV per 128-feature half): DGRAD 5.1, UV 3.0, O 3.5 at
+    // d = 64; 18.3, 8.0, 15.0 at d = 128.  Every split of one wave is tried.
+    const double tD = D == 64 ? 5.1 : 18.3, tU = D == 64 ? 3.0 : 8.0, tO = D == 64 ? 3.5 : 15.0;
     const int64_t nMB = (p.BQ() + 7) / 8;
     // The search is a few thousand steps; its result is kept per shape.
     static std::mutex mu;
@@ -1067,15 +1067,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
         int c = 0;
         for (int it = 0; it < nit; ++it) {
           if (c > 0) y(c - 1);  // finish the previous item before waiting for this one's operands
-          // The epilogue's warp-level MMAs share the tensor pipe: let them run
-          // before this item's first UMMAs are queued.
-          if (it > 0) mbar_wait(bar_epd, (it - 1) & 1, sAbort);
+          // The epilogue's warp-level MMAs share the tensor pipe: only this
+          // item's first U/V go ahead of them (the compute warps find them done
+          // when the epilogue ends; the epilogue's closing barrier orders the
+          // reuse of the Z pair buffer), the rest waits below.
           if (C::RES && it == 0) mbar_wait(bar_wf, 0, sAbort);
           mbar_wait(bar_p, it & 1, sAbort);
           if (it < 3) OW_TR(1, it * 32 + 20);
           tc_fence_after();
           for (int j = 0; j < nsub; ++j, ++c) {
             const int b = c & 1;
+            if (j == 1 && it > 0) mbar_wait(bar_epd, (it - 1) & 1, sAbort);
             if (!C::RES) mbar_wait(bar_wf + b, (c >> 1) & 1, sAbort);
             if (it < 3 && j < 3) OW_TR(1, it * 32 + 21 + j);
             tc_fence_after();
