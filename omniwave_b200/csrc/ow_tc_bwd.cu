@@ -153,8 +153,8 @@ struct BPlan {
     // finishes first: each role's time is its items per CTA times its
     // steady-state time per item, measured on B200 from each CTA's finish
     // time (us per item; UV per 128-feature half): DGRAD 5.1, UV 3.0, O 3.5 at
-    // d = 64; 18.3, 8.0, 15.0 at d = 128.  Every split of one wave is tried.
-    const double tD = D == 64 ? 5.1 : 18.3, tU = D == 64 ? 3.0 : 8.0, tO = D == 64 ? 3.5 : 15.0;
+    // d = 64; 17.9, 8.0, 14.9 at d = 128.  Every split of one wave is tried.
+    const double tD = D == 64 ? 5.1 : 17.9, tU = D == 64 ? 3.0 : 8.0, tO = D == 64 ? 3.5 : 14.9;
     const int64_t nMB = (p.BQ() + 7) / 8;
     // The search is a few thousand steps; its result is kept per shape.
     static std::mutex mu;
@@ -966,12 +966,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
         int c = 0, epoch = 0;
         for (int it = 0; it < nit; ++it) {
           if (c > 0) dp(c - 1);  // finish the previous item before waiting for this one's operands
-          // The epilogue's warp-level MMAs share the tensor pipe: let them run
-          // before this item's UMMAs are queued.  With resident weights the
-          // first sub-chunk's U/V/dZ (12 MMAs) go ahead, so the compute warps
-          // find them done when the epilogue ends; at d = 128 the epilogue's T
-          // shares the dU/dV buffers, so nothing goes ahead.
-          if (!C::RES && it > 0) mbar_wait(bar_epd, (it - 1) & 1, sAbort);
+          // The epilogue's warp-level MMAs share the tensor pipe: only the
+          // first sub-chunk's U/V/dZ go ahead of them (the compute warps find
+          // them done when the epilogue ends; the epilogue's closing barrier
+          // orders the reuse of the dU/dV buffers, which hold T at d = 128),
+          // the rest waits below.
           if (C::RES) {
             if (it > 0 && item_of(it) / nMB != item_of(it - 1) / nMB) {
               umma_commit(bar_we);  // resident weights of the previous group no longer read
@@ -984,7 +983,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           tc_fence_after();
           for (int j = 0; j < nsub; ++j, ++c) {
             const int b = c & 1;
-            if (C::RES && j == 1 && it > 0) mbar_wait(bar_epd, (it - 1) & 1, sAbort);
+            if (j == 1 && it > 0) mbar_wait(bar_epd, (it - 1) & 1, sAbort);
             if (!C::RES) mbar_wait(bar_wf + c % C::D_NST, (c / C::D_NST) & 1, sAbort);
             if (it < 3 && j < 3) OW_TR(1, it * 32 + 21 + j);
             tc_fence_after();
