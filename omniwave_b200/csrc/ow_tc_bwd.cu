@@ -107,7 +107,13 @@ struct BCfg {
   static constexpr bool RES = D == 64;
   static constexpr int D_W = D_S + DS_BYTES;
   static constexpr int D_T = D_W + (RES ? NSUB : D_NST) * A_BYTES;
-  static constexpr int D_END = D_T + (RES ? P_BYTES : 0);
+  static constexpr int D_T_END = D_T + (RES ? P_BYTES : 0);
+  // DGRAD epilogue: per compute warp an f32 staging tile of 8 rows x 64
+  // channels (row stride 72) for the dX stores.
+  static constexpr int D_ST_LD = 72;
+  static constexpr int D_STG_WARP = 8 * D_ST_LD * 4;
+  static constexpr int D_STG = D_T_END;
+  static constexpr int D_END = D_STG + 8 * D_STG_WARP;
   static constexpr int D_TT = RES ? D_T : D_S;              // where the epilogue reads T
   // UV: item buffers (two at d = 64), dU_h | dV_h for 128 features, two stages.
   static constexpr int U_NB = D == 64 ? 2 : 1;
@@ -1242,64 +1248,81 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
         // [hw*D/2, (hw+1)*D/2).  dP arrives in the mma C-fragment layout.
         constexpr int NP = D / 32;
         const int hw = warp >> 2;
-        // Pass 1: dT = A_u^T dP_u + A_v^T dP_v -> dX (needs no T).
+        // Pass 1: dT = A_u^T dP_u + A_v^T dP_v -> dX (needs no T).  Warp
+        // (lq, hw) owns tile 2 lq + hw and all D channels.  Per 64-channel pass
+        // each half-tile (rows g / g + 8 of the C fragments) goes through the
+        // warp's f32 staging tile, so that 16 lanes write one row segment.
         {
           uint32_t fuT[4], fvT[4];
           frag(0, true, fuT);
           frag(1, true, fvT);
+          const int tile = 2 * lq + hw;
+          const int rwA = sRow[tile * 16 + g], rwB = sRow[tile * 16 + g + 8];
+          const uint32_t tl_addr = tbase + ((uint32_t)(tile * 16) << 16);
+          float* stg = reinterpret_cast<float*>(sm + C::D_STG + warp * C::D_STG_WARP);
 #pragma unroll 1
-          for (int tl = 0; tl < 2; ++tl) {
-            const int tile = 2 * lq + tl;
-            const int rwA = sRow[tile * 16 + g], rwB = sRow[tile * 16 + g + 8];
-            const uint32_t tl_addr = tbase + ((uint32_t)(tile * 16) << 16);
-            uint32_t pu[NP][8], pv[NP][8];
+          for (int hf = 0; hf < D / 64; ++hf) {
+            uint32_t pu[4][8], pv[4][8];
 #pragma unroll
-            for (int np = 0; np < NP; ++np) {
-              const int k0 = hw * (D / 2) + np * 16;
-              tmem_ld16x256_x2(tl_addr + C::T_DPU + k0, pu[np]);
-              tmem_ld16x256_x2(tl_addr + C::T_DPV + k0, pv[np]);
+            for (int n4 = 0; n4 < 4; ++n4) {
+              const int k0 = hf * 64 + n4 * 16;
+              tmem_ld16x256_x2(tl_addr + C::T_DPU + k0, pu[n4]);
+              tmem_ld16x256_x2(tl_addr + C::T_DPV + k0, pv[n4]);
             }
             tmem_ld_wait();
-            if (tid == 0 && it < 3) OW_TR(0, it * 32 + 20 + 2 * tl);
+            if (tid == 0 && it < 3) OW_TR(0, it * 32 + 20 + 2 * hf);
+            float cc[4][2][4];  // [16-channel step][channel block nb][C fragment]
 #pragma unroll
-            for (int np = 0; np < NP; ++np) {
-              const int k0 = hw * (D / 2) + np * 16;
+            for (int n4 = 0; n4 < 4; ++n4) {
               uint32_t au[4], av[4];
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
-                au[q] = pack2<BF16>(__uint_as_float(pu[np][2 * q]), __uint_as_float(pu[np][2 * q + 1]));
-                av[q] = pack2<BF16>(__uint_as_float(pv[np][2 * q]), __uint_as_float(pv[np][2 * q + 1]));
+                au[q] = pack2<BF16>(__uint_as_float(pu[n4][2 * q]), __uint_as_float(pu[n4][2 * q + 1]));
+                av[q] = pack2<BF16>(__uint_as_float(pv[n4][2 * q]), __uint_as_float(pv[n4][2 * q + 1]));
               }
-              float cc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};  // channel blocks nb = 0, 1
 #pragma unroll
               for (int nb = 0; nb < 2; ++nb) {
+                cc[n4][nb][0] = cc[n4][nb][1] = cc[n4][nb][2] = cc[n4][nb][3] = 0.f;
                 const uint32_t bu0 = movm_trans(au[2 * nb]), bu1 = movm_trans(au[2 * nb + 1]);
                 const uint32_t bv0 = movm_trans(av[2 * nb]), bv1 = movm_trans(av[2 * nb + 1]);
-                mma16816<BF16>(cc[nb], fuT, bu0, bu1);
-                mma16816<BF16>(cc[nb], fvT, bv0, bv1);
+                mma16816<BF16>(cc[n4][nb], fuT, bu0, bu1);
+                mma16816<BF16>(cc[n4][nb], fvT, bv0, bv1);
               }
-              if (cont) {
-                // Lane t4 stores row g + 8 (t4 >> 1), channels k0 + 8 (t4 & 1) .. +8.
-                float ov[8];
-                quad_rows8(cc, t4, ov);
-                const int rw = sRow[tile * 16 + g + 8 * (t4 >> 1)];
-                if (rw >= 0) {
-                  const int64_t off = (int64_t)rw * p.C + sCh[0] + k0 + 8 * (t4 & 1);
-                  if (a.dxn || std::is_same_v<TX, float>) {
-                    float* dst = a.dxn ? a.dxn + off : (float*)a.dx + off;
-                    reinterpret_cast<float4*>(dst)[0] = make_float4(ov[0], ov[1], ov[2], ov[3]);
-                    reinterpret_cast<float4*>(dst)[1] = make_float4(ov[4], ov[5], ov[6], ov[7]);
-                  } else {
-                    constexpr bool XB = std::is_same_v<TX, __nv_bfloat16>;
-                    *reinterpret_cast<uint4*>((TX*)a.dx + off) =
-                        make_uint4(pack2<XB>(ov[0], ov[1]), pack2<XB>(ov[2], ov[3]), pack2<XB>(ov[4], ov[5]),
-                                   pack2<XB>(ov[6], ov[7]));
+            }
+            if (cont) {
+#pragma unroll
+              for (int hr = 0; hr < 2; ++hr) {
+#pragma unroll
+                for (int n4 = 0; n4 < 4; ++n4)
+#pragma unroll
+                  for (int nb = 0; nb < 2; ++nb)
+                    *reinterpret_cast<float2*>(stg + g * C::D_ST_LD + n4 * 16 + nb * 8 + 2 * t4) =
+                        make_float2(cc[n4][nb][2 * hr], cc[n4][nb][2 * hr + 1]);
+                __syncwarp();
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  const int r8 = (i * 32 + lane) >> 4, c4 = (lane & 15) * 4;
+                  const float4 v = *reinterpret_cast<const float4*>(stg + r8 * C::D_ST_LD + c4);
+                  const int rw = sRow[tile * 16 + hr * 8 + r8];
+                  if (rw >= 0) {
+                    const int64_t off = (int64_t)rw * p.C + sCh[0] + hf * 64 + c4;
+                    if (a.dxn || std::is_same_v<TX, float>) {
+                      float* dst = a.dxn ? a.dxn + off : (float*)a.dx + off;
+                      *reinterpret_cast<float4*>(dst) = v;
+                    } else {
+                      constexpr bool XB = std::is_same_v<TX, __nv_bfloat16>;
+                      *reinterpret_cast<uint2*>((TX*)a.dx + off) = make_uint2(pack2<XB>(v.x, v.y), pack2<XB>(v.z, v.w));
+                    }
                   }
                 }
-              } else {
+                __syncwarp();  // the staging tile is rewritten by the next half-tile
+              }
+            } else {
+#pragma unroll
+              for (int n4 = 0; n4 < 4; ++n4)
 #pragma unroll
                 for (int nb = 0; nb < 2; ++nb) {
-                  const int k = k0 + nb * 8 + 2 * t4;
+                  const int k = hf * 64 + n4 * 16 + nb * 8 + 2 * t4;
 #pragma unroll
                   for (int hr = 0; hr < 2; ++hr) {
                     const int rw = hr ? rwB : rwA;
@@ -1310,15 +1333,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
                       const int ch = sCh[k + e];
                       if (ch >= p.C) continue;
                       const int64_t off = row * p.C + ch;
-                      const float dv = cc[nb][2 * hr + e];
+                      const float dv = cc[n4][nb][2 * hr + e];
                       if (a.dxn) a.dxn[off] = dv;
                       else ((TX*)a.dx)[off] = Elem<TX>::from(dv);
                     }
                   }
                 }
-              }
             }
-            if (tid == 0 && it < 3) OW_TR(0, it * 32 + 21 + 2 * tl);
+            if (tid == 0 && it < 3) OW_TR(0, it * 32 + 21 + 2 * hf);
           }
         }
         // Pass 2: dA_u += dP_u T^T, dA_v += dP_v T^T with T from its image.
