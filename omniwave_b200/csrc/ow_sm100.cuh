@@ -260,32 +260,6 @@ __device__ __forceinline__ void load_afrag(const uint16_t* A, bool trans, int g,
   f[3] = el(g + 8, 2 * t4 + 8) | (el(g + 8, 2 * t4 + 9) << 16);
 }
 
-// Quad exchange of two m16n8 f32 accumulators cc[nb] (channel blocks nb = 0,
-// 1 of a 16-channel step): a 4 x 4 transpose of float pairs over the lanes
-// of a quad in two xor stages.  Lane t4 ends with row g + 8 * (t4 >> 1),
-// channels 8 * (t4 & 1) .. +8 of the step in ov, so it can store one
-// 16-byte (16-bit) or 32-byte (f32) row piece.  V[d] is the pair this lane
-// holds for quad lane d; W[s] the pair received from quad lane s.
-__device__ __forceinline__ void quad_rows8(const float (&cc)[2][4], int t4, float (&ov)[8]) {
-  const bool b0 = t4 & 1, b1 = t4 >> 1;
-  const float2 V0 = make_float2(cc[0][0], cc[0][1]), V1 = make_float2(cc[1][0], cc[1][1]);
-  const float2 V2 = make_float2(cc[0][2], cc[0][3]), V3 = make_float2(cc[1][2], cc[1][3]);
-  auto xchg = [&](float2 v, int m) {
-    return make_float2(__shfl_xor_sync(0xffffffffu, v.x, m), __shfl_xor_sync(0xffffffffu, v.y, m));
-  };
-  // stage 1 (lane ^ 1): keep the pairs whose destination shares bit 0
-  const float2 ra = xchg(b0 ? V0 : V1, 1), rb = xchg(b0 ? V2 : V3, 1);
-  const float2 own_lo = b0 ? V1 : V0, own_hi = b0 ? V3 : V2;
-  const float2 ulo0 = b0 ? ra : own_lo, ulo1 = b0 ? own_lo : ra;  // by source bit 0
-  const float2 uhi0 = b0 ? rb : own_hi, uhi1 = b0 ? own_hi : rb;
-  // stage 2 (lane ^ 2): keep the pairs whose destination shares bit 1
-  const float2 r0 = xchg(b1 ? ulo0 : uhi0, 2), r1 = xchg(b1 ? ulo1 : uhi1, 2);
-  const float2 k0v = b1 ? uhi0 : ulo0, k1v = b1 ? uhi1 : ulo1;
-  const float2 W0 = b1 ? r0 : k0v, W1 = b1 ? r1 : k1v, W2 = b1 ? k0v : r0, W3 = b1 ? k1v : r1;
-  ov[0] = W0.x; ov[1] = W0.y; ov[2] = W1.x; ov[3] = W1.y;
-  ov[4] = W2.x; ov[5] = W2.y; ov[6] = W3.x; ov[7] = W3.y;
-}
-
 // ---------------------------------------------------------------- warp MMA
 template <bool BF16>
 __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {

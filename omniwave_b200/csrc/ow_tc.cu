@@ -11,7 +11,7 @@
 //     Z_q = silu(U_q) * V_q                       compute warps, TMEM -> smem
 //     Y  += Z_q B_o[q, :]                         tcgen05.mma, f32 in TMEM
 //   delta = A_o Y * gamma * scale (+ x)           compute warps: TMEM C-fragments, mma.sync,
-//                                                 quad exchange, 16/32-byte row stores
+//                                                 f32 staging, full-line row stores
 //
 // Roles of the forward kernel (320 threads): warps 0-7 compute, warp 8 issues
 // every tcgen05.mma (one thread) and owns the TMEM allocation, warp 9 issues
