@@ -158,9 +158,9 @@ struct BPlan {
     // Split one wave of CTAs across the roles so that the slowest role
     // finishes first: each role's time is its items per CTA times its
     // steady-state time per item, measured on B200 from each CTA's finish
-    // time (us per item; UV per 128-feature half): DGRAD 5.1, UV 3.0, O 3.5 at
-    // d = 64; 17.9, 8.0, 14.9 at d = 128.  Every split of one wave is tried.
-    const double tD = D == 64 ? 5.1 : 17.9, tU = D == 64 ? 3.0 : 8.0, tO = D == 64 ? 3.5 : 14.9;
+    // time (us per item; UV per 128-feature half): DGRAD 5.5, UV 3.05, O 3.65
+    // at d = 64; 17.9, 8.0, 14.9 at d = 128.  Every split of one wave is tried.
+    const double tD = D == 64 ? 5.5 : 17.9, tU = D == 64 ? 3.05 : 8.0, tO = D == 64 ? 3.65 : 14.9;
     const int64_t nMB = (p.BQ() + 7) / 8;
     // The search is a few thousand steps; its result is kept per shape.
     static std::mutex mu;
