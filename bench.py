@@ -83,8 +83,8 @@ def _kernel_flops(name: str, b: int, h: int, w: int, c: int, d: int) -> float:
 # DRAM bytes (read + write) per launch from the committed ncu captures,
 # keyed by (kernel, case, batch): value and the profile summary it comes from.
 _TRAFFIC = {
-    ("tc_bwd_kernel", "56x56x128/local0", 128): (1051.8e6, "profiles/tc_bwd_kernel_56x56x128_local0.md"),
-    ("tc_bwd_kernel", "14x14x512/local0", 128): (212.1e6, "profiles/tc_bwd_kernel_14x14x512_local0.md"),
+    ("tc_bwd_kernel", "56x56x128/local0", 128): (1100.8e6, "profiles/tc_bwd_kernel_56x56x128_local0.md"),
+    ("tc_bwd_kernel", "14x14x512/local0", 128): (214.3e6, "profiles/tc_bwd_kernel_14x14x512_local0.md"),
 }
 
 
