@@ -4,10 +4,12 @@ Workload (the operator sweep the metric is quoted on):
 B=128 per GPU, bf16 compute with fp32 accumulation, forward + backward
 (dX and all weight gradients) of every stage shape {56x56x128 d64,
 28x28x256 d64, 14x14x512 d128, 7x7x1024 d128} under each of the local,
-shifted and radix routes.  One step = those 12 fwd+bwd calls.  Inputs are
-seeded synthetic tensors (x, dY ~ N(0,1), default-init weights cast to bf16,
-seed order of scripts/benchmark.py:56-110); the per-step working set
-(~1 GB) is far larger than the 126 MB L2, so every step streams from HBM.
+shifted and radix routes, radix at levels 0, 1 and 2 (levels 1 and 2 gather
+channel groups with stride Q_c).  One step = those 20 fwd+bwd calls.  Inputs
+are seeded synthetic tensors in config 2's order: ``torch.manual_seed(1)``,
+an fp32 ``OmniWeaveBlock`` with default init, then x and dY ~ N(0,1) (drawn
+on the device), all cast to bf16.  The per-step working set (~2 GB) is far
+larger than the 126 MB L2, so every step streams from HBM.
 
 ``value`` = algorithmic FLOPs of all ranks / max-over-ranks device time
 (CUDA events, inputs resident in HBM).  FLOPs per tile follow the operator
@@ -16,19 +18,25 @@ definition: fwd = 4g^2 d + 2g^2 rd + 6 g d rd over padded tiles, bwd = 2x fwd.
 copied from pinned host memory and outputs and gradients copied back inside
 the timed region.
 
-``--impl reference`` times the CPU restatement of the reference algorithm
-(``oracle``, numpy float32, all host cores) on a bounded sample of the same
-workload.  Under torchrun only rank 0 runs it.
+``--impl reference`` times the reference's own implementation of the path,
+``bigemm_delta_reference`` plus torch autograd (omniweave/ops/reference.py,
+from the unmodified install under baseline/_ref), on the host cores with
+every thread, in bf16 on a B=8 sample of each of the 20 cases per step.
+Under torchrun only rank 0 runs it.  ``cpu_baseline`` in the main line is
+the same measurement, bounded to ~10 s.
 
 Multi-GPU: one process per GPU; the batch is sharded (each rank runs its own
 B=128 sweep, no data-path collective), so scaling is weak.
 
-The same line carries ``omniweave_t``: OmniWeave-T (random init broadcast
-from rank 0, synthetic N(0,1) images, per-rank seeds) measured as BASELINE
-configs 3-5 -- bf16 inference at 256 images per GPU, batch-sharded with no
-communication, and the DDP training step at 128 images per GPU (bf16
-autocast, cross-entropy on uniform labels, NCCL gradient all-reduce, AdamW
-lr 1e-3 wd 0.05).  Images/s are whole-job totals over max-over-ranks time.
+The same line carries ``omniweave_t``: the reference's own OmniWeave-T
+(``omniweave.models.registry.create_model``) with ``backend="cuda"``
+installed by ``omniwave_b200.integration`` (random init broadcast from rank
+0, synthetic N(0,1) images, per-rank seeds) measured as BASELINE configs
+3-5 -- bf16 inference at 256 images per GPU, batch-sharded with no
+communication, and the training step at 128 images per GPU (bf16 autocast,
+cross-entropy on uniform labels, AdamW lr 1e-3 wd 0.05; one CUDA graph per
+step on one GPU, DDP with NCCL gradient all-reduce on several).  Images/s
+are whole-job totals over max-over-ranks time.
 """
 
 from __future__ import annotations
@@ -50,10 +58,11 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 SHAPES = [(56, 56, 128, 64), (28, 28, 256, 64), (14, 14, 512, 128), (7, 7, 1024, 128)]
-ROUTES = [("local", 0), ("shifted", 0), ("radix", 0)]
+ROUTES = [("local", 0), ("shifted", 0), ("radix", 0), ("radix", 1), ("radix", 2)]
 BATCH = 128
 G = 16
 METRIC = "BiGEMM TFLOP/s (fwd+bwd, bf16, operator sweep B=128)"
+REF_SITE = os.path.join(ROOT, "baseline", "_ref")
 
 
 def fwd_flops(b: int, h: int, w: int, c: int, d: int) -> float:
@@ -80,11 +89,12 @@ def _kernel_flops(name: str, b: int, h: int, w: int, c: int, d: int) -> float:
     return 2.0 * fwd_flops(b, h, w, c, d) - mixes
 
 
-# DRAM bytes (read + write) per launch from the committed ncu captures,
-# keyed by (kernel, case, batch): value and the profile summary it comes from.
+# DRAM bytes (read + write) per launch of the dominant kernel, from one ncu
+# capture of the same kernel and case (dram__bytes_read.sum +
+# dram__bytes_write.sum), keyed by (kernel, case, batch).
 _TRAFFIC = {
-    ("tc_bwd_kernel", "56x56x128/local0", 128): (1100.8e6, "profiles/tc_bwd_kernel_56x56x128_local0.md"),
-    ("tc_bwd_kernel", "14x14x512/local0", 128): (214.3e6, "profiles/tc_bwd_kernel_14x14x512_local0.md"),
+    ("tc_bwd_kernel", "56x56x128/local0", 128): 1100.8e6,
+    ("tc_bwd_kernel", "14x14x512/local0", 128): 214.3e6,
 }
 
 
@@ -104,31 +114,20 @@ def _dist():
     return world, rank, local
 
 
-def _make_case(h, w, c, d, batch, dev, seed):
-    """Seeded operator tensors (scripts/benchmark.py:56-110 scales)."""
-    import torch.nn as nn
-
-    from omniwave_b200 import build_route_plan
+def _make_case(h, w, c, d, route, level, batch, dev, seed):
+    """Operator tensors in BASELINE config 2's order: seed, an fp32
+    ``OmniWeaveBlock`` with default init (orthogonal A_u/A_v, identity A_o,
+    xavier B, gamma 1e-5), then x and dY ~ N(0,1), all cast to bf16
+    (scripts/benchmark.py:56-110)."""
+    from omniwave_b200 import OmniWeaveBlock
 
     torch.manual_seed(seed)
-    qc = math.ceil(c / d)
-    rd = 2 * d
-
-    def init(shape, fn):
-        t = torch.empty(shape, dtype=torch.float32, device=dev)
-        fn(t)
-        return t.to(torch.bfloat16)
-
-    tensors = dict(
-        x=torch.randn(batch, h, w, c, device=dev, dtype=torch.bfloat16),
-        a_u=init((G, G), nn.init.orthogonal_), a_v=init((G, G), nn.init.orthogonal_),
-        a_o=init((G, G), nn.init.eye_),
-        b_u=init((qc, d, rd), nn.init.xavier_uniform_), b_v=init((qc, d, rd), nn.init.xavier_uniform_),
-        b_o=init((qc, rd, d), nn.init.xavier_uniform_),
-        gamma=torch.full((c,), 1e-5, device=dev, dtype=torch.bfloat16),
-    )
-    dout = torch.randn(batch, h, w, c, device=dev, dtype=torch.bfloat16)
-    return tensors, dout
+    blk = OmniWeaveBlock(h, w, c, d, route, level)
+    tensors = {k: getattr(blk, k).detach().to(dev, torch.bfloat16)
+               for k in ("a_u", "a_v", "a_o", "b_u", "b_v", "b_o", "gamma")}
+    tensors["x"] = torch.randn(batch, h, w, c, device=dev).to(torch.bfloat16)
+    dout = torch.randn(batch, h, w, c, device=dev).to(torch.bfloat16)
+    return blk.plan, tensors, dout
 
 
 class _Clocks:
@@ -186,7 +185,7 @@ class _Clocks:
 
 # ---------------------------------------------------------------------------
 def run_ours(args) -> None:
-    from omniwave_b200 import _lib, bigemm, build_route_plan
+    from omniwave_b200 import _lib, bigemm
 
     world, rank, local = _dist()
     dev = torch.device("cuda", local)
@@ -206,8 +205,7 @@ def run_ours(args) -> None:
         for ri, (route, lvl) in enumerate(ROUTES):
             if only is not None and f"{h}x{w}x{c}/{route}{lvl}" not in only:
                 continue
-            tensors, dout = _make_case(h, w, c, d, batch, dev, seed=1 + 1000 * rank + 10 * si + ri)
-            plan = build_route_plan(h, w, c, G, d, route, lvl)
+            plan, tensors, dout = _make_case(h, w, c, d, route, lvl, batch, dev, seed=1 + 1000 * rank)
             leaves = {k: v.detach().requires_grad_(True) for k, v in tensors.items()}
             cases.append(dict(shape=(h, w, c, d), route=f"{route}{lvl}", plan=plan,
                               leaves=leaves, dout=dout))
@@ -261,6 +259,8 @@ def run_ours(args) -> None:
     t1.record()
     torch.cuda.synchronize()
     launches = lib.ow_launch_count() - launches0
+    # Every wait in the kernels is bounded; a run in which one gave up is void.
+    _lib.check_device_fault(dev.index, reset=False)
     if world > 1:
         torch.distributed.barrier()
     ms = t0.elapsed_time(t1)
@@ -293,6 +293,7 @@ def run_ours(args) -> None:
 
     # --- end-to-end through the public API with host buffers -----------------
     e2e = None if args.no_e2e else _e2e(args, cases, names, dev, world, sweep_flops)
+    ref_gpu = None if args.no_ref_gpu else _ref_gpu_bench(args, cases, names, dev, batch)
     del cases
     torch.cuda.empty_cache()
 
@@ -340,19 +341,27 @@ def run_ours(args) -> None:
                 "peak_source": peaks["source"],
                 "launch_ms": round(dom_ms, 4),
                 "algorithmic_flops_per_launch": dom_flops,
-                "traffic": None if traffic is None else traffic[0],
-                "traffic_source": None if traffic is None else traffic[1],
+                "traffic": traffic,
+                "traffic_source": None if traffic is None else
+                "one ncu capture of this kernel and case (dram__bytes_read.sum + dram__bytes_write.sum)",
             },
             "per_call_ms": {f"{k[0][0]}x{k[0][1]}x{k[0][2]}/{k[1]}": [round(v[0], 4), round(v[1], 4)]
                             for k, v in per.items()},
+            "per_call_ms_note": "[forward call, backward call] per case; radix1/radix2 gather "
+                                "channel groups with stride Q_c",
+            "route_totals_ms": {r: round(sum(v[0] + v[1] for k, v in per.items() if k[1] == r), 4)
+                                for r in sorted({k[1] for k in per})},
             "per_kernel_ms": {f"{k[0][0]}x{k[0][1]}x{k[0][2]}/{k[1]}": {n: round(t, 4) for n, t in v.items()}
                               for k, v in kern.items()},
             "e2e": e2e,
             "gpu_launches": int(launches),
+            "device_fault": _lib.device_fault(dev.index),
             "clocks": clk.summary(),
         }
         if model_line is not None:
             line["omniweave_t"] = model_line
+        if ref_gpu is not None:
+            line["reference_gpu"] = ref_gpu
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -438,6 +447,70 @@ def _e2e(args, cases, names, dev, world, sweep_flops):
             "d2h_bytes_per_step": d2h // steps, "copies": "pinned host, pipelined on two copy streams"}
 
 
+def _ref_gpu_bench(args, cases, names, dev, batch):
+    """The reference's own GPU paths on this B200, same cases and inputs:
+    its Triton forward (``_TritonBiGEMM``, ops/triton.py:90-292, with the
+    fp32 reference backward it ships) and its ``reference`` backend
+    (einsums, bf16) forward + backward.  A secondary point of comparison."""
+    try:
+        _reference_package()
+        from omniweave.ops.reference import bigemm_delta_reference
+        from omniweave.ops.triton import _TRITON_AVAILABLE, bigemm_delta_triton
+    except ImportError as exc:
+        return {"unavailable": f"reference package not installed ({exc})"}
+    if not _TRITON_AVAILABLE:
+        return {"unavailable": "triton is not importable"}
+    reps = 2
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / reps
+
+    out = {"batch": batch, "dtype": "bf16", "per_case_ms": {}}
+    tot = {"triton_fwd": 0.0, "triton_fwd_bwd": 0.0, "reference_fwd_bwd": 0.0}
+    fw = fb = 0.0
+    try:
+        for cs in cases:
+            t = {k: v.detach() for k, v in cs["leaves"].items()}
+            plan, dy = cs["plan"], cs["dout"]
+            h, w, c, d = cs["shape"]
+            f1 = fwd_flops(batch, h, w, c, d)
+
+            def tri_fwd():
+                with torch.no_grad():
+                    bigemm_delta_triton(plan=plan, **t)
+
+            def fwd_bwd(fn):
+                lv = {k: v.requires_grad_(True) for k, v in ((k, t[k].clone()) for k in names)}
+                o = fn(plan=plan, **lv)
+                torch.autograd.grad(o, [lv[k] for k in names], dy.to(o.dtype))
+
+            ms = (timed(tri_fwd), timed(lambda: fwd_bwd(bigemm_delta_triton)),
+                  timed(lambda: fwd_bwd(bigemm_delta_reference)))
+            key = f"{h}x{w}x{c}/{cs['route']}"
+            out["per_case_ms"][key] = [round(m, 3) for m in ms]
+            for k, m in zip(tot, ms):
+                tot[k] += m
+            fw += f1
+            fb += 3.0 * f1
+            torch.cuda.empty_cache()
+    except Exception as exc:  # the reference's GPU code, not ours: record and go on
+        out["error"] = f"{type(exc).__name__}: {exc}"[:300]
+        return out
+    out["per_case_ms_note"] = "[triton fwd, triton fwd + its fp32 reference bwd, reference backend fwd+bwd]"
+    out["triton_fwd_tflops"] = round(fw / (tot["triton_fwd"] * 1e-3) / 1e12, 3)
+    out["triton_fwd_bwd_tflops"] = round(fb / (tot["triton_fwd_bwd"] * 1e-3) / 1e12, 3)
+    out["reference_fwd_bwd_tflops"] = round(fb / (tot["reference_fwd_bwd"] * 1e-3) / 1e12, 3)
+    return out
+
+
 MODEL_FWD_GFLOP_PER_IMG = 3.757  # OmniWeave-T at 224x224: 2.895 BiGEMM + 0.863 Linear
 
 
@@ -462,14 +535,35 @@ def _timed(fn, steps, warmup, dev, world):
     return float(ms.item())
 
 
+def _reference_package():
+    """Import the unmodified reference package from baseline/_ref (or the
+    environment); raises ImportError when it is not installed."""
+    if os.path.isdir(os.path.join(REF_SITE, "omniweave")) and REF_SITE not in sys.path:
+        sys.path.append(REF_SITE)
+    import omniweave  # noqa: F401
+
+    return omniweave
+
+
 def _model_bench(args, dev, world, rank, lib):
-    from omniwave_b200 import create_model
+    """BASELINE configs 3-5 on the reference's own OmniWeave-T with the cuda backend."""
+    from omniwave_b200 import _lib
     from omniwave_b200.train import TrainStep, broadcast_parameters
 
-    out = {"model": "omniweave_t", "input": "224x224", "data": "synthetic N(0,1), per-rank seeds"}
+    try:
+        _reference_package()
+    except ImportError as exc:
+        return {"model": "omniweave_t", "unavailable": f"reference package not installed ({exc})"}
+    from omniwave_b200 import integration
+
+    integration.install()
+    from omniweave.models.registry import create_model
+
+    out = {"model": "omniweave_t (reference modules, backend='cuda' via omniwave_b200.integration)",
+           "input": "224x224", "data": "synthetic N(0,1), per-rank seeds"}
     # ---- inference (configs 3/4): bf16 weights, 256 images per GPU
     torch.manual_seed(0)
-    model = create_model("omniweave_t").to(dev)
+    model = create_model("omniweave_t", backend="cuda").to(dev)
     broadcast_parameters(model)
     model = model.to(torch.bfloat16).eval()
     bi = 256
@@ -484,25 +578,33 @@ def _model_bench(args, dev, world, rank, lib):
     out["infer_batch_per_gpu"] = bi
     out["infer_img_per_s"] = round(bi * world * args.model_steps / (ms * 1e-3), 1)
     out["infer_ms_per_step"] = round(ms / args.model_steps, 3)
+    out["infer_tflops"] = round(bi * world * args.model_steps / (ms * 1e-3) * MODEL_FWD_GFLOP_PER_IMG / 1e3, 2)
     del model, imgs
     torch.cuda.empty_cache()
-    # ---- training step (config 5): DDP, AdamW, bf16 autocast, 128 per GPU
+    # ---- training step (config 5): AdamW, bf16 autocast, 128 per GPU; one
+    # CUDA graph per step on one GPU, DDP (NCCL all-reduce) on several
     torch.manual_seed(0)
-    model = create_model("omniweave_t").to(dev)
-    ts = TrainStep(model, lr=1e-3, weight_decay=0.05, amp_dtype=torch.bfloat16)
+    model = create_model("omniweave_t", backend="cuda").to(dev)
+    graph = world == 1 and not args.no_graph
+    ts = TrainStep(model, lr=1e-3, weight_decay=0.05, amp_dtype=torch.bfloat16, cuda_graph=graph,
+                   graph_warmup=2)
     bt = 128
     x = torch.randn(bt, 3, 224, 224, device=dev, generator=g)
     y = torch.randint(0, 1000, (bt,), device=dev, generator=g)
     launches0 = lib.ow_launch_count()
-    ms = _timed(lambda: ts.step(x, y), args.model_steps, args.warmup, dev, world)
+    ms = _timed(lambda: ts.step(x, y), args.model_steps, max(args.warmup, 3), dev, world)
     ts.check_finite()
+    _lib.check_device_fault(dev.index, reset=False)
     img_s = bt * world * args.model_steps / (ms * 1e-3)
     out["train_batch_per_gpu"] = bt
     out["train_img_per_s"] = round(img_s, 1)
     out["train_ms_per_step"] = round(ms / args.model_steps, 3)
     out["train_tflops"] = round(img_s * 3 * MODEL_FWD_GFLOP_PER_IMG * 1e9 / 1e12, 2)
     out["train_parallelism"] = f"DDP x{world} (NCCL bucketed all-reduce)" if world > 1 else "single GPU"
-    out["bigemm_launches_in_train_region"] = int(lib.ow_launch_count() - launches0)
+    out["train_cuda_graph"] = graph
+    out["bigemm_launches_in_train_region"] = (
+        int(lib.ow_launch_count() - launches0) if not graph else
+        "inside one CUDA graph per step (launch counter counts host-side launches only)")
     del ts, model, x, y
     torch.cuda.empty_cache()
     return out
@@ -520,47 +622,10 @@ def _peaks():
 
 
 # ---------------------------------------------------------------------------
-# CPU legs (the oracle restatement of the reference algorithm)
+# CPU legs: the reference's own implementation on the host cores
 # ---------------------------------------------------------------------------
-def _cpu_sample_cases(batch):
-    import numpy as np
-
-    from oracle import bigemm as O
-
-    out = []
-    rng = np.random.default_rng(0)
-    for (h, w, c, d) in SHAPES:
-        for route, lvl in ROUTES:
-            p = O.make_plan(h, w, c, G, d, route, lvl)
-            qc = math.ceil(c / d)
-            rd = 2 * d
-            f32 = np.float32
-            ws = [rng.standard_normal((G, G)).astype(f32) / 4 for _ in range(3)]
-            ws += [(rng.standard_normal((qc, d, rd)) / np.sqrt(d)).astype(f32) for _ in range(2)]
-            ws += [(rng.standard_normal((qc, rd, d)) / np.sqrt(rd)).astype(f32),
-                   np.full(c, 1e-5, dtype=f32)]
-            x = rng.standard_normal((batch, h, w, c)).astype(f32)
-            dy = rng.standard_normal((batch, h, w, c)).astype(f32)
-            out.append((p, x, dy, ws, 3.0 * fwd_flops(batch, h, w, c, d)))
-    return out
-
-
-def _cpu_run(cases, seconds):
-    from oracle import bigemm as O
-
-    flops = 0.0
-    t0 = time.perf_counter()
-    reps = 0
-    while True:
-        for p, x, dy, ws, f in cases:
-            O.forward(x, p, *ws)
-            O.backward(dy, x, p, *ws)
-            flops += f
-        reps += 1
-        el = time.perf_counter() - t0
-        if el >= seconds:
-            break
-    return flops, el, reps
+CPU_SAMPLE_BATCH = 8
+_WNAMES = ("a_u", "a_v", "a_o", "b_u", "b_v", "b_o", "gamma")
 
 
 def _cpu_threads():
@@ -570,35 +635,150 @@ def _cpu_threads():
         return os.cpu_count() or 1
 
 
+def _cpu_model_name():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def _cpu_ref_cases(batch, dtype):
+    """The 20 sweep cases at ``batch``, in config 2's seed order, for the
+    reference's ``bigemm_delta_reference``."""
+    from omniweave.models.block import OmniWeaveBlock
+
+    cases = []
+    for (h, w, c, d) in SHAPES:
+        for route, lvl in ROUTES:
+            torch.manual_seed(1)
+            blk = OmniWeaveBlock(h, w, c, d, route, lvl)
+            x = torch.randn(batch, h, w, c).to(dtype).requires_grad_(True)
+            dy = torch.randn(batch, h, w, c).to(dtype)
+            ws = {k: getattr(blk, k).detach().to(dtype).requires_grad_(True) for k in _WNAMES}
+            cases.append((blk.plan, x, ws, dy, 3.0 * fwd_flops(batch, h, w, c, d)))
+    return cases
+
+
+def _cpu_ref_sweep(cases):
+    """One step: forward + autograd backward of every case (returns FLOPs)."""
+    from omniweave.ops.reference import bigemm_delta_reference
+
+    flops = 0.0
+    for plan, x, ws, dy, f in cases:
+        out = bigemm_delta_reference(x=x, plan=plan, **ws)
+        torch.autograd.grad(out, [x] + list(ws.values()), dy.to(out.dtype))
+        flops += f
+    return flops
+
+
+def _cpu_info(threads):
+    return {"cores": threads, "nproc": os.cpu_count(), "cpu_model": _cpu_model_name(),
+            "torch_threads": torch.get_num_threads()}
+
+
 def _cpu_baseline(seconds):
-    batch = 2
-    cases = _cpu_sample_cases(batch)
-    flops, el, reps = _cpu_run(cases, seconds)
-    return {"value": round(flops / el / 1e12, 5), "unit": "TFLOP/s", "cores": _cpu_threads(),
-            "kind": "port",
-            "sample": f"oracle numpy float32 fwd+bwd of the 12-case sweep at B={batch} "
-                      f"(x{reps} repetitions, {el:.1f} s)"}
+    """Bounded CPU baseline for the main line: the reference implementation
+    (bf16, every host thread) on a B=8 sample of the 20-case sweep."""
+    threads = _cpu_threads()
+    torch.set_num_threads(threads)
+    try:
+        _reference_package()
+    except ImportError as exc:
+        return {"value": None, "unit": "TFLOP/s", "cores": threads, "kind": "reference",
+                "sample": f"unavailable: reference package not installed ({exc})"}
+    cases = _cpu_ref_cases(CPU_SAMPLE_BATCH, torch.bfloat16)
+    _cpu_ref_sweep(cases[:1])
+    flops, reps = 0.0, 0
+    t0 = time.perf_counter()
+    while True:
+        flops += _cpu_ref_sweep(cases)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    out = {"value": round(flops / el / 1e12, 5), "unit": "TFLOP/s", "kind": "reference",
+           "sample": f"reference bigemm_delta_reference + autograd (torch CPU, bf16) fwd+bwd of the "
+                     f"20-case sweep at B={CPU_SAMPLE_BATCH} (x{reps} repetitions, {el:.1f} s)"}
+    out.update(_cpu_info(threads))
+    return out
+
+
+def _cpu_model_bench():
+    """BASELINE's CPU model plan: the reference OmniWeave-T (reference backend)
+    at B=8 -- inference fp32 and bf16 autocast, and an AdamW train step under
+    bf16 autocast; min of 3 after 1 warm-up."""
+    from omniweave.models.registry import create_model
+
+    b = 8
+    torch.manual_seed(0)
+    model = create_model("omniweave_t")
+    x = torch.randn(b, 3, 224, 224)
+    y = torch.randint(0, 1000, (b,))
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-3, weight_decay=0.05)
+
+    def best(fn):
+        fn()
+        ts = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return min(ts)
+
+    def infer(amp):
+        model.eval()
+        with torch.no_grad(), torch.autocast("cpu", dtype=torch.bfloat16, enabled=amp):
+            model(x)
+
+    def train():
+        model.train()
+        with torch.autocast("cpu", dtype=torch.bfloat16):
+            loss = torch.nn.functional.cross_entropy(model(x), y)
+        opt.zero_grad(set_to_none=True)
+        loss.backward()
+        opt.step()
+
+    return {"batch": b, "infer_fp32_img_per_s": round(b / best(lambda: infer(False)), 2),
+            "infer_bf16_img_per_s": round(b / best(lambda: infer(True)), 2),
+            "train_bf16_img_per_s": round(b / best(train), 2)}
 
 
 def run_reference(args) -> None:
     world, rank, _ = _dist()
     if rank != 0:
         return
-    batch = 2
-    cases = _cpu_sample_cases(batch)
-    _cpu_run(cases[:1], 0.0)  # warm the BLAS threads
+    threads = _cpu_threads()
+    torch.set_num_threads(threads)
+    try:
+        _reference_package()
+    except ImportError as exc:
+        print(json.dumps({"impl": "reference", "unavailable": f"reference package not installed: {exc}"}),
+              flush=True)
+        return
+    cases = _cpu_ref_cases(CPU_SAMPLE_BATCH, torch.bfloat16)
     for _ in range(args.warmup):
-        _cpu_run(cases, 0.0)
+        _cpu_ref_sweep(cases)
     t0 = time.perf_counter()
     flops = 0.0
     for _ in range(args.steps):
-        f, _, _ = _cpu_run(cases, 0.0)
-        flops += f
+        flops += _cpu_ref_sweep(cases)
     el = time.perf_counter() - t0
     val = flops / el / 1e12
-    cores = _cpu_threads()
-    sample = f"oracle numpy float32 fwd+bwd of the 12-case sweep at B={batch} per step"
-    print(json.dumps({
+    # fp32 once (the reference's default dtype), for the record.
+    c32 = _cpu_ref_cases(CPU_SAMPLE_BATCH, torch.float32)
+    t1 = time.perf_counter()
+    f32 = _cpu_ref_sweep(c32)
+    f32_val = f32 / (time.perf_counter() - t1) / 1e12
+    del c32
+    model = None if args.no_model else _cpu_model_bench()
+    info = _cpu_info(threads)
+    sample = (f"reference bigemm_delta_reference + autograd (torch CPU, bf16, {threads} threads) fwd+bwd "
+              f"of the 20-case sweep at B={CPU_SAMPLE_BATCH} per step")
+    line = {
         "impl": "reference",
         "metric": METRIC,
         "value": round(val, 5),
@@ -610,16 +790,21 @@ def run_reference(args) -> None:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "f32",
-        "data": "synthetic (seeded N(0,1))",
-        "config": {"workload": "bigemm_sweep_fwd_bwd", "batch_per_step": batch,
+        "dtype": "bf16",
+        "data": "synthetic (config 2 seed order: seed 1, default-init block, x and dY ~ N(0,1))",
+        "config": {"workload": "bigemm_sweep_fwd_bwd", "batch_per_case_per_step": CPU_SAMPLE_BATCH,
+                   "batch_note": "B=8 sample of the B=128 sweep (TFLOP/s is per-FLOP normalised)",
                    "shapes": [f"{h}x{w}x{c}/d{d}" for (h, w, c, d) in SHAPES],
                    "routes": [f"{r}{l}" for r, l in ROUTES]},
-        "cpu_baseline": {"value": round(val, 5), "unit": "TFLOP/s", "cores": cores, "kind": "port",
-                         "sample": sample},
+        "cpu_baseline": dict({"value": round(val, 5), "unit": "TFLOP/s", "kind": "reference",
+                              "sample": sample}, **info),
+        "fp32_value": round(f32_val, 5),
         "e2e": {"value": round(val, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
-    }), flush=True)
+    }
+    if model is not None:
+        line["omniweave_t_cpu"] = model
+    print(json.dumps(line), flush=True)
 
 
 def main(argv=None) -> None:
@@ -636,6 +821,8 @@ def main(argv=None) -> None:
     ap.add_argument("--cases", default="",
                     help="comma-separated subset of the sweep, e.g. 56x56x128/local0 (profiling runs)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--no-graph", action="store_true", help="train step without CUDA-graph capture")
+    ap.add_argument("--no-ref-gpu", action="store_true", help="skip timing the reference's own GPU paths")
     args = ap.parse_args(argv)
     if args.impl == "reference":
         run_reference(args)

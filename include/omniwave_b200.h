@@ -18,14 +18,19 @@
  * Conventions
  *  - All tensor pointers are device pointers owned by the caller; the library
  *    only borrows them for the duration of the call.  It keeps no state
- *    between calls except immutable per-device kernel attributes.
+ *    between calls except immutable per-device kernel attributes, the
+ *    per-device fault word (ow_device_fault) and, for
+ *    ow_bigemm_fwd_noalloc only, that entry point's fixed scratch array and
+ *    its cached device address (see its comment).
  *  - ``stream`` is a ``cudaStream_t`` passed as ``void*``.  Calls are
  *    asynchronous on that stream and never synchronise the device.
  *  - Every entry point returns OW_OK (0) or an error code; no C++ exception
  *    crosses the ABI.  ``ow_last_error()`` returns a thread-local message for
  *    the last failing call made by the calling thread.
  *  - Functions are reentrant: concurrent calls on different streams are safe
- *    as long as their workspaces do not overlap.
+ *    as long as their workspaces do not overlap.  The exception is
+ *    ow_bigemm_fwd_noalloc, whose calls share one scratch array and must not
+ *    overlap on the GPU (see its comment).
  */
 #ifndef OMNIWAVE_B200_H
 #define OMNIWAVE_B200_H
@@ -163,11 +168,26 @@ OW_API const char* ow_last_error(void);
 OW_API int ow_device_supported(int device);
 
 /*
- * Fault word of the tensor-core kernels on ``device``: 0 when no kernel ever
- * gave up on a bounded wait, otherwise a nonzero code.  Synchronises with the
- * device.  ``reset`` != 0 clears the word after reading it.
+ * Fault word of this library's kernels on ``device``: 0 when no kernel ever
+ * gave up on a bounded wait (every wait on the GPU is bounded at 2 s), else a
+ * nonzero code (1: a wait ran out; the outputs of that call are undefined).
+ * One word per device is shared by every kernel of the library.  Calls are
+ * asynchronous, so a fault surfaces here, not in the failing call's status:
+ * this function synchronises the device first.  ``reset`` != 0 clears the
+ * word after reading it.  Returns -1 if the device cannot be queried.
  */
 OW_API int ow_device_fault(int device, int reset);
+
+/*
+ * Wait-timeout self-check, a test aid with no counterpart in the reference.
+ * While ``probe_ns`` is nonzero (at most 1e9), every mbarrier-pipelined
+ * kernel launched afterwards first waits ``probe_ns`` nanoseconds on a
+ * barrier that nothing arrives on, before it issues any copy or MMA; the
+ * wait runs out, the kernel skips its work and records code 1 in the fault
+ * word.  Outputs of calls made while it is set are undefined.  Pass 0 to
+ * turn it off.  Returns OW_ERR_INVALID above the limit.
+ */
+OW_API int ow_debug_wait_probe(uint32_t probe_ns);
 
 /*
  * Bytes of workspace a forward (``for_backward == 0``) or backward

@@ -5,10 +5,12 @@ route tables on the device, tile gathers folded into the kernels' loads,
 sm_100a kernels for the forward and backward, RMSNorm and residual fused in
 block mode.  The compute lives in ``libomniwave_b200.so`` (C ABI in
 ``include/omniwave_b200.h``); this package is the host-side mirror of the
-reference's Python interface.
+reference's Python interface.  ``omniwave_b200.integration.install()`` plugs
+the backend into the reference package itself, so its own ``OmniWeaveBlock``,
+``OmniWeaveBackbone`` and training engine run on these kernels with
+``backend="cuda"``.
 """
 
-from omniwave_b200.backbone import OmniWeaveBackbone, create_model, space_to_depth_nhwc
 from omniwave_b200.block import OmniWeaveBlock
 from omniwave_b200.ops import bigemm, bigemm_delta_cuda, cuda_is_supported, select_backend
 from omniwave_b200.routing import RoutePlan, build_route_plan, build_stage_schedule
@@ -16,15 +18,12 @@ from omniwave_b200.routing import RoutePlan, build_route_plan, build_stage_sched
 __version__ = "0.1.0"
 
 __all__ = [
-    "OmniWeaveBackbone",
     "OmniWeaveBlock",
     "RoutePlan",
     "bigemm",
     "bigemm_delta_cuda",
     "build_route_plan",
     "build_stage_schedule",
-    "create_model",
     "cuda_is_supported",
     "select_backend",
-    "space_to_depth_nhwc",
 ]

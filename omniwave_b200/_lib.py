@@ -67,7 +67,7 @@ EXPORTS = (
     "ow_abi_version", "ow_last_error", "ow_device_supported", "ow_device_fault",
     "ow_launch_count", "ow_bigemm_workspace_size",
     "ow_rmsnorm_rstd", "ow_bigemm_fwd", "ow_bigemm_bwd", "ow_bigemm_fwd_noalloc",
-    "ow_noalloc_scratch_limit", "ow_profile_events",
+    "ow_noalloc_scratch_limit", "ow_profile_events", "ow_debug_wait_probe",
 )
 
 _lock = threading.Lock()
@@ -98,6 +98,8 @@ def load() -> ctypes.CDLL:
         lib.ow_device_fault.argtypes = [ctypes.c_int, ctypes.c_int]
         lib.ow_device_fault.restype = ctypes.c_int
         lib.ow_launch_count.restype = ctypes.c_uint64
+        lib.ow_debug_wait_probe.argtypes = [ctypes.c_uint32]
+        lib.ow_debug_wait_probe.restype = ctypes.c_int
         lib.ow_profile_events.argtypes = [ctypes.c_int, _vp, _vp]
         lib.ow_profile_events.restype = ctypes.c_int
         lib.ow_bigemm_workspace_size.argtypes = [ctypes.POINTER(Args), ctypes.c_int]
@@ -123,6 +125,23 @@ def check(status: int, what: str) -> None:
     if status != OW_OK:
         msg = load().ow_last_error().decode(errors="replace")
         raise NativeLibraryError(f"{what} failed ({_ERR_NAMES.get(status, status)}): {msg}")
+
+
+class DeviceFaultError(RuntimeError):
+    """A kernel of the library gave up on a bounded wait (its outputs are undefined)."""
+
+
+def device_fault(device: int, reset: bool = False) -> int:
+    """The device fault word (0: no kernel gave up on a wait).  Synchronises the device."""
+    return int(load().ow_device_fault(int(device), 1 if reset else 0))
+
+
+def check_device_fault(device: int, reset: bool = True) -> None:
+    """Raise ``DeviceFaultError`` if a kernel on ``device`` gave up on a bounded wait."""
+    v = device_fault(device, reset)
+    if v != 0:
+        raise DeviceFaultError(f"omniwave_b200 kernel on device {device} reported fault code {v} "
+                               f"(a bounded wait ran out; outputs of that call are undefined)")
 
 
 def ptr(t: torch.Tensor | None) -> int | None:

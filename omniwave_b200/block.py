@@ -15,7 +15,7 @@ import torch
 import torch.nn as nn
 from torch import Tensor
 
-from omniwave_b200.ops import block_forward, cuda_is_supported, select_backend
+from omniwave_b200.ops import block_forward, cuda_is_supported, drop_path_scale, select_backend
 from omniwave_b200.routing import RoutePlan, build_route_plan
 
 
@@ -68,19 +68,6 @@ class OmniWeaveBlock(nn.Module):
         nn.init.xavier_uniform_(self.b_v)
         nn.init.xavier_uniform_(self.b_o)
 
-    def _sample_scale(self, x: Tensor) -> Tensor | None:
-        """Per-sample drop-path scale; same RNG draw as block.py:99-107."""
-        if not (self.training and self.drop_path_rate):
-            return None
-        keep = 1.0 - self.drop_path_rate
-        dtype = torch.promote_types(
-            torch.promote_types(
-                torch.get_autocast_dtype("cuda") if torch.is_autocast_enabled("cuda") else x.dtype,
-                self.gamma.dtype),
-            x.dtype)
-        mask = torch.empty((x.shape[0], 1, 1, 1), dtype=dtype, device=x.device).bernoulli_(keep)
-        return (mask / keep).reshape(-1)
-
     def forward(self, x: Tensor) -> Tensor:
         """``x``: ``[B, H, W, C]`` -> ``[B, H, W, C]``."""
         chosen, _ = select_backend(x, self.backend, lambda t: cuda_is_supported(t, self.plan, self.b_u))
@@ -91,5 +78,6 @@ class OmniWeaveBlock(nn.Module):
             )
         return block_forward(
             x, self.plan, self.norm_weight, self.a_u, self.a_v, self.a_o,
-            self.b_u, self.b_v, self.b_o, self.gamma, self._sample_scale(x),
+            self.b_u, self.b_v, self.b_o, self.gamma,
+            drop_path_scale(x, self.gamma, self.drop_path_rate, self.training),
         )

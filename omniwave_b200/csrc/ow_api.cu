@@ -9,6 +9,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "ow_common.cuh"
 #include "ow_internal.h"
@@ -27,6 +28,38 @@ void profile_mark(int kernel, bool after, cudaStream_t st) {
   void* e = g_prof[kernel][after ? 1 : 0].load(std::memory_order_acquire);
   if (e) cudaEventRecord((cudaEvent_t)e, st);
 }
+
+// The device fault word: one int in every device's copy of this library's
+// device memory.  Kernels of every file receive its address as an argument,
+// so a bounded wait that gives up anywhere is reported in this one place.
+static __device__ int g_fault_word = 0;
+constexpr int kMaxDevices = 64;
+static std::mutex g_fault_mu;
+static int* g_fault_ptr[kMaxDevices] = {};
+static std::atomic<uint32_t> g_probe_ns{0};
+
+int fault_word(int** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    set_error("fault word: no usable current device (%s)", cudaGetErrorString(e));
+    return OW_ERR_CUDA;
+  }
+  std::lock_guard<std::mutex> lk(g_fault_mu);
+  if (!g_fault_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_fault_word);
+    if (e != cudaSuccess || !p) {
+      set_error("fault word: cudaGetSymbolAddress failed on device %d: %s", dev, cudaGetErrorString(e));
+      return OW_ERR_CUDA;
+    }
+    g_fault_ptr[dev] = (int*)p;
+  }
+  *out = g_fault_ptr[dev];
+  return OW_OK;
+}
+
+uint32_t wait_probe_ns() { return g_probe_ns.load(std::memory_order_relaxed); }
 
 void set_error(const char* fmt, ...) {
   va_list ap;
@@ -130,7 +163,35 @@ int ow_device_supported(int device) {
   return (major == 10 && minor == 0) ? 1 : 0;
 }
 
-int ow_device_fault(int device, int reset) { return tc_fault(device, reset); }
+int ow_device_fault(int device, int reset) {
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return -1;
+  if (cudaSetDevice(device) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  int v = -1;
+  if (cudaDeviceSynchronize() == cudaSuccess &&
+      cudaMemcpyFromSymbol(&v, g_fault_word, sizeof(int)) == cudaSuccess) {
+    if (reset && v != 0) {
+      const int z = 0;
+      if (cudaMemcpyToSymbol(g_fault_word, &z, sizeof(int)) != cudaSuccess) v = -1;
+    }
+  } else {
+    v = -1;
+  }
+  cudaSetDevice(prev);
+  return v;
+}
+
+int ow_debug_wait_probe(uint32_t probe_ns) {
+  if (probe_ns > 1000000000u) {
+    set_error("ow_debug_wait_probe: %u ns is longer than the 1 s limit of the self-check", probe_ns);
+    return OW_ERR_INVALID;
+  }
+  g_probe_ns.store(probe_ns, std::memory_order_relaxed);
+  return OW_OK;
+}
 
 size_t ow_bigemm_workspace_size(const ow_bigemm_args_t* args, int for_backward) {
   Prob p;

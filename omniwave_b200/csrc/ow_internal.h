@@ -76,7 +76,13 @@ int tc_forward(const ow_bigemm_args_t* a, const Prob& p, void* stream, Carver& w
 // The forward's pre-pass: [P_u | P_v] operand images per item (ow_tc_bwd.cu).
 int tc_pack_forward(const ow_bigemm_args_t* a, const Prob& p, const uint16_t* amat, const float* nwc,
                     const int* contig, unsigned char* packed, void* stream);
-int tc_fault(int device, int reset);
+
+// The library's device fault word on the current device (one int per device,
+// shared by every kernel file; kernels get its address as an argument).
+// The first call on a device looks the address up.
+int fault_word(int** out);
+// Wait-timeout self-check setting (ow_debug_wait_probe); 0 when off.
+uint32_t wait_probe_ns();
 
 // RMSNorm backward of block mode from the f32 gradient w.r.t. the normalised
 // input (CUDA cores, row-wise).  norm_bwd_take() carves its partials from

@@ -17,33 +17,6 @@
 namespace ow {
 namespace sm100 {
 
-// Device-wide fault word of the including translation unit: set when a
-// bounded wait gives up (never expected in a correct run).  Read back on the
-// host through ow_device_fault().
-static __device__ int g_fault = 0;
-
-constexpr int kFaultWait = 1;
-
-// Optional timeline tracing (builds with -DOW_TRACE only): OW_TR(slot, ev)
-// records %globaltimer into a per-translation-unit table indexed by
-// (CTA, slot, event) for the first kTraceCtas CTAs.  Compiles to nothing in
-// the product build.
-#ifdef OW_TRACE
-constexpr int kTraceEvents = 96, kTraceSlots = 3, kTraceCtas = 160;
-static __device__ unsigned long long g_trace[kTraceCtas * kTraceSlots * kTraceEvents];
-#define OW_TR(slot, ev)                                                                             \
-  do {                                                                                              \
-    if ((ev) < ::ow::sm100::kTraceEvents && blockIdx.x < ::ow::sm100::kTraceCtas) {                 \
-      unsigned long long t_;                                                                        \
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                        \
-      ::ow::sm100::g_trace[(blockIdx.x * ::ow::sm100::kTraceSlots + (slot)) * ::ow::sm100::kTraceEvents + \
-                           (ev)] = t_;                                                              \
-    }                                                                                               \
-  } while (0)
-#else
-#define OW_TR(slot, ev) ((void)0)
-#endif
-
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -86,12 +59,18 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 }
 
 // Wait for the phase with the given parity to complete.  Gives up after
-// kWaitLimitNs of wall time, records a fault and sets *abort so the caller's
-// loops wind down instead of hanging; once *abort is set every wait returns
-// false immediately.
+// ``limit_ns`` of wall time (kWaitLimitNs unless told otherwise) and sets
+// *abort (a flag in the CTA's shared memory) so that the caller's loops wind
+// down instead of hanging; once *abort is set every wait returns false
+// immediately.  The kernel reports an aborted CTA through report_abort().
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+// Code a kernel writes into the library's device fault word when one of its
+// bounded waits gave up.
+constexpr int kFaultWait = 1;
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (*abort) return false;
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
@@ -99,12 +78,26 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     for (int i = 0; i < 256; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
-      atomicExch(&g_fault, kFaultWait);
+    if (globaltimer_ns() - t0 > limit_ns) {
       *abort = 1;
       return false;
     }
   }
+}
+
+// Wait-timeout self-check: with ``probe_ns`` > 0 the calling thread waits
+// that long on ``bar``, a barrier nothing arrives on, before any copy or MMA
+// of the kernel is issued.  The wait runs out, the CTA's abort flag is set,
+// and every role skips its work.  Lets a test exercise the bounded-wait and
+// fault-reporting path without a copy or MMA in flight.
+__device__ __forceinline__ void wait_probe(uint64_t* bar, volatile int* abort, uint32_t probe_ns) {
+  if (probe_ns) mbar_wait(bar, 0, abort, probe_ns);
+}
+
+// Called by every thread after the kernel's final __syncthreads: the first
+// thread of an aborted CTA records kFaultWait in the device fault word.
+__device__ __forceinline__ void report_abort(volatile int* abort, int* fault) {
+  if (threadIdx.x == 0 && *abort && fault) atomicOr(fault, kFaultWait);
 }
 
 // ---------------------------------------------------------------- bulk copy

@@ -79,7 +79,7 @@ struct Cfg {
   static constexpr int STG_WARP = 8 * ST_LD * 4;           // per compute warp: 8 rows x 64 channels
   static constexpr int OFF_STG = OFF_ROWS + 2 * ROWS_BYTES;
   static constexpr int OFF_BAR = OFF_STG + 8 * STG_WARP;
-  static constexpr int NBAR = 22;
+  static constexpr int NBAR = 23;
   static constexpr int BAR_BYTES = NBAR * 8 + 16;
   static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024;  // + alignment slack
   // TMEM columns: U/V of two chunks, Y of two items.
@@ -175,10 +175,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict__ packed,
               const unsigned char* __restrict__ img, const uint16_t* __restrict__ amat,
               const float* __restrict__ gg, const int* __restrict__ contig, const float* __restrict__ scale,
-              int residual, TO* __restrict__ out, int vec_ok) {
+              int residual, TO* __restrict__ out, int vec_ok, int* fault, uint32_t probe_ns) {
   using C = Cfg<D>;
   constexpr bool EARLY = C::RES;  // next item's first gate before this item's epilogue
-  constexpr bool QUIET_Y = false;  // early order: hold Y(item, 0) until the previous epilogue is done
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   unsigned char* sZ = sm + C::OFF_Z;
@@ -194,6 +193,7 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict_
   uint64_t* bar_wres = bars + 16;   // [2] resident: chunk images of group buffer b loaded (tx)
   uint64_t* bar_wfree = bars + 18;  // [2] resident: group buffer b no longer read (commit)
   uint64_t* bar_m = bars + 20;      // [2] output rows of row slot b loaded (tx)
+  uint64_t* bar_probe = bars + 22;  // wait-timeout self-check: nothing arrives on it
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + C::NBAR);
   volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
 
@@ -220,8 +220,10 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict_
       mbar_init(bar_wfree + s, 1);
       mbar_init(bar_m + s, 1);
     }
+    mbar_init(bar_probe, 1);
     *sAbort = 0;
     fence_mbar_init();
+    wait_probe(bar_probe, sAbort, probe_ns);
   }
   if (warp == MMA_WARP) tmem_alloc(sTmem, TMEM_COLS);
   tc_fence_before();
@@ -229,7 +231,9 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict_
   tc_fence_after();
   const uint32_t tbase = *sTmem;
 
-  if (warp == PROD_WARP) {
+  if (*sAbort) {
+    // The wait-timeout self-check ran out before any work was issued.
+  } else if (warp == PROD_WARP) {
     // ------------------------------------------------ producer (bulk copies)
     if (lane == 0 && nit > 0) {
       auto load_p = [&](int it) {
@@ -313,13 +317,8 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict_
       auto issue_y = [&](int x) {  // Y(item) (+)= Z_x B_o[x]
         const int s = x & 1, ix = x / C::NQ, q = x - ix * C::NQ, yb = ix & 1;
         const uint32_t ph = (x >> 1) & 1;
-        // Y buffer yb was last read by the epilogue of item ix - 2.  With the
-        // early gate order the wait is for item ix - 1 instead: the tensor
-        // pipe then idles while that epilogue's warp MMAs run (their latency
-        // rises tenfold behind queued tcgen05 work), and the MMAs held back
-        // (this Y, the next item's first U/V) are not needed before it ends.
-        constexpr int YD = EARLY && QUIET_Y ? 1 : 2;
-        if (q == 0 && ix >= YD) mbar_wait(bar_epd + ((ix - YD) & 1), ((ix - YD) >> 1) & 1, sAbort);
+        // Y buffer yb was last read by the epilogue of item ix - 2.
+        if (q == 0 && ix >= 2) mbar_wait(bar_epd + (ix & 1), ((ix - 2) >> 1) & 1, sAbort);
         mbar_wait(bar_z + s, ph, sAbort);
         if (!C::RES) mbar_wait(bar_wo + s, ph, sAbort);
         tc_fence_after();
@@ -348,16 +347,13 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict_
           ((it & 1) ? wb1 : wb0) = s0 + C::OFF_W + (e & 1) * C::GRP_BYTES;
           if (it == 0 || newgrp) mbar_wait(bar_wres + (e & 1), (e >> 1) & 1, sAbort);
         }
-        if (it < 3) OW_TR(1, it * 32 + 0);
         mbar_wait(bar_p + it % C::NB, (it / C::NB) & 1, sAbort);
-        if (it < 3) OW_TR(1, it * 32 + 1);
         tc_fence_after();
         const uint32_t aPu = s0 + C::OFF_P + (it % C::NB) * C::PP_BYTES, aPv = aPu + C::P_BYTES;
         for (int q = 0; q < C::NQ; ++q, ++c) {
           const int s = c & 1;
           const uint32_t ph = (c >> 1) & 1;
           if (!C::RES) mbar_wait(bar_wuv + s, ph, sAbort);
-          if (it < 3 && q < 4) OW_TR(1, it * 32 + 2 + q);
           tc_fence_after();
           if (!*sAbort) {
             const uint32_t aBu = C::RES ? ((it & 1) ? wb1 : wb0) + q * C::IMG_BYTES : s0 + C::OFF_WUV + s * C::WUV_BYTES;
@@ -374,7 +370,6 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict_
           if (q == C::NQ - 1) umma_commit(bar_pf + it % C::NB);
           if (c > 0 && (EARLY || q > 0)) {
             issue_y(c - 1);
-            if (it < 3 && q < 4) OW_TR(1, it * 32 + 8 + q);
             // The previous item's last Y was the last reader of its group buffer.
             if (q == 0 && newgrp) umma_commit(bar_wfree + ((e - 1) & 1));
           }
@@ -421,7 +416,6 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict_
       const uint32_t ph = (cx >> 1) & 1;
       const int it = cx / C::NQ, q = cx - it * C::NQ;
       mbar_wait(bar_uv + s, ph, sAbort);
-      if (tid == 0 && it < 3 && q < 4) OW_TR(0, it * 32 + 2 + 2 * q);
       __syncwarp();
       tc_fence_after();
       uint32_t ur[32], vr[32];
@@ -445,7 +439,6 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict_
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      if (tid == 0 && it < 3 && q < 4) OW_TR(0, it * 32 + 3 + 2 * q);
       mbar_arrive(bar_z + s);
     };
 
@@ -478,6 +471,7 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict_
       const int sl = it & 1;
       set_group(qc_of(it));
       mbar_wait(bar_m + sl, (it >> 1) & 1, sAbort);
+      if (*sAbort) return;  // the rows never arrived: no load or store may use them
       sRowsE = reinterpret_cast<const int*>(sm + C::OFF_ROWS + sl * C::ROWS_BYTES);
 #pragma unroll
       for (int hr = 0; hr < 2; ++hr) {
@@ -494,9 +488,8 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict_
     // 128-byte row segment (bf16) with the residual added on the way out.
     auto epilogue = [&](int it) {
       const int yb = it & 1, cl = it * C::NQ + C::NQ - 1;
-      if (tid == 0 && it < 3) OW_TR(0, it * 32 + 12);
       mbar_wait(bar_yz + (cl & 1), (cl >> 1) & 1, sAbort);
-      if (tid == 0 && it < 3) OW_TR(0, it * 32 + 13);
+      if (*sAbort) return;
       __syncwarp();
       tc_fence_after();
       const int* sRows = sRowsE;
@@ -505,7 +498,6 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict_
 #pragma unroll
       for (int np = 0; np < NP; ++np) tmem_ld16x256_x2(ta + np * 16, yv[np]);
       tmem_ld_wait();
-      if (tid == 0 && it < 3) OW_TR(0, it * 32 + 15);
       const bool res_vec = cont && residual;
 #pragma unroll
       for (int hf = 0; hf < NH; ++hf) {
@@ -594,16 +586,13 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict_
             }
         }
       }
-      if (tid == 0 && it < 3) OW_TR(0, it * 32 + 16);
       tc_fence_before();
       mbar_arrive(bar_epd + (it & 1));
-      if (tid == 0 && it < 3) OW_TR(0, it * 32 + 14);
     };
 
     if constexpr (EARLY) {
       if (nit > 0) gate(0);
       for (int it = 0; it < nit; ++it) {
-        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 0);
         for (int q = 1; q < C::NQ; ++q) gate(it * C::NQ + q);
         epi_prepare(it);
         if (it + 1 < nit) gate((it + 1) * C::NQ);
@@ -611,7 +600,6 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict_
       }
     } else {
       for (int it = 0; it < nit; ++it) {
-        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 0);
         for (int q = 0; q < C::NQ; ++q) gate(it * C::NQ + q);
         epi_prepare(it);
         epilogue(it);
@@ -621,6 +609,7 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict_
 
   __syncwarp();
   __syncthreads();
+  report_abort(sAbort, fault);
   if (*sAbort) {
     // A wait gave up: give in-flight copies and MMAs time to land before
     // the shared memory and TMEM they target are released.
@@ -674,6 +663,8 @@ int tc_forward_t(const ow_bigemm_args_t* a, const Prob& p, cudaStream_t st, Carv
   TcWs<D> w(p);
   unsigned char* base = (unsigned char*)ws.take(w.total);
   if (!ws.base) return OW_OK;
+  int* fault = nullptr;
+  OW_RETURN_IF(fault_word(&fault));
   OW_RETURN_IF((tc_prep<D, BF16>(a, p, w, base, st)));
   profile_mark(OW_PROF_FPACK, false, st);
   OW_RETURN_IF((tc_pack_forward(a, p, (const uint16_t*)(base + w.amat), (const float*)(base + w.nwc),
@@ -697,7 +688,7 @@ int tc_forward_t(const ow_bigemm_args_t* a, const Prob& p, cudaStream_t st, Carv
     launch(kern, grid, TC_THREADS, Cfg<D>::SMEM, st, p, (const TX*)a->x,
            (const unsigned char*)(base + w.packed), (const unsigned char*)(base + w.img),
            (const uint16_t*)(base + w.amat), (const float*)(base + w.gg), (const int*)(base + w.contig),
-           a->sample_scale, a->residual, (TO*)a->out, vec_ok);
+           a->sample_scale, a->residual, (TO*)a->out, vec_ok, fault, wait_probe_ns());
     profile_mark(OW_PROF_FWD, true, st);
     OW_CHECK_LAUNCH("tc_fwd_kernel");
     return OW_OK;
@@ -715,19 +706,6 @@ int tc_forward_t(const ow_bigemm_args_t* a, const Prob& p, cudaStream_t st, Carv
 
 }  // namespace
 
-int tc_fault(int device, int reset) {
-  int prev = 0, v = 0;
-  cudaGetDevice(&prev);
-  if (cudaSetDevice(device) != cudaSuccess) return -1;
-  if (cudaMemcpyFromSymbol(&v, sm100::g_fault, sizeof(int)) != cudaSuccess) v = -1;
-  if (reset && v > 0) {
-    int z = 0;
-    cudaMemcpyToSymbol(sm100::g_fault, &z, sizeof(int));
-  }
-  cudaSetDevice(prev);
-  return v;
-}
-
 bool tc_supported(const ow_bigemm_args_t* a, const Prob& p, const char** why) {
   auto no = [&](const char* m) {
     if (why) *why = m;
@@ -738,7 +716,9 @@ bool tc_supported(const ow_bigemm_args_t* a, const Prob& p, const char** why) {
   if (!((p.d == 64 || p.d == 128) && p.rd == 2 * p.d)) return no("tile shape");
   const int c16 = a->compute_dtype;
   if (a->x_dtype != c16 && a->x_dtype != OW_DTYPE_F32) return no("x dtype");
-  if (a->out_dtype != c16 && a->out_dtype != OW_DTYPE_F32 && a->out != nullptr) return no("out dtype");
+  // out_dtype is the forward's output type and the backward's dout type; the
+  // sizing call reads it too, so the check never depends on ``out``.
+  if (a->out_dtype != c16 && a->out_dtype != OW_DTYPE_F32) return no("out dtype");
   if (a->rstd && a->compute_dtype == OW_DTYPE_F64) return no("rstd dtype");
   return true;
 }
@@ -751,14 +731,3 @@ int tc_forward(const ow_bigemm_args_t* a, const Prob& p, void* stream, Carver& w
 }
 
 }  // namespace ow
-
-#ifdef OW_TRACE
-extern "C" __attribute__((visibility("default"))) int ow_trace_fwd(void* host, size_t bytes, int clear) {
-  if (clear) {
-    void* dev = nullptr;
-    cudaGetSymbolAddress(&dev, ow::sm100::g_trace);
-    return (int)cudaMemset(dev, 0, sizeof(ow::sm100::g_trace));
-  }
-  return (int)cudaMemcpyFromSymbol(host, ow::sm100::g_trace, bytes);
-}
-#endif

@@ -533,6 +533,8 @@ struct BwdArgs {
   float* puv;     // [nH*Qc*nUVq][2][128][D]
   float* po;      // [Qc*nOq][RD][D]
   int nD, nUVq, nOq, nH;
+  int* fault;         // device fault word (bounded waits that gave up)
+  uint32_t probe_ns;  // wait-timeout self-check (0: off)
 };
 
 // ---------------------------------------------------------------------------
@@ -691,6 +693,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
   uint64_t* bar_yd = bars + 23;   // O: Y of the item complete (commit)
   uint64_t* bar_epd = bars + 24;  // epilogue done (DGRAD: T; O: H, G' and the staging buffer)
   uint64_t* bar_gl = bars + 25;   // O: H and G' loaded (tx)
+  uint64_t* bar_probe = bars + 26;  // wait-timeout self-check: nothing arrives on it
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + C::NBARS);
   volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
 
@@ -763,8 +766,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
     mbar_init(bar_yd, 1);
     mbar_init(bar_epd, NCOMP);
     mbar_init(bar_gl, 1);
+    mbar_init(bar_probe, 1);
     *sAbort = 0;
     fence_mbar_init();
+    wait_probe(bar_probe, sAbort, a.probe_ns);
   }
   if (warp == MMA_WARP) tmem_alloc(sTmem, TMEM_COLS);
   tc_fence_before();
@@ -786,7 +791,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
   };
   auto buf_col = [&](int b) { return HALVES ? b * 32 : 0; };
 
-  if (warp == PROD_WARP) {
+  if (*sAbort) {
+    // The wait-timeout self-check ran out before any work was issued.
+  } else if (warp == PROD_WARP) {
     // ------------------------------------------------ producer (bulk copies)
     if (lane == 0 && nit > 0) {
       if (role == R_DGRAD) {
@@ -795,7 +802,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           bulk_g2s(sm, item_src(it), 3 * C::P_BYTES, bar_p);
         };
         auto load_w = [&](int c) {
-          { const int i_ = c / nsub, j_ = c % nsub; if (i_ < 3 && j_ < 6) OW_TR(2, i_ * 32 + 26 + j_); }
           const int st = c % C::D_NST;
           mbar_arrive_expect_tx(bar_wf + st, C::A_BYTES);
           bulk_g2s(sm + C::D_W + st * C::A_BYTES, stage_src(c), C::A_BYTES, bar_wf + st);
@@ -816,7 +822,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           int epoch = 0;
           for (int it = 0; it + 1 < nit && !*sAbort; ++it) {
             if (mbar_wait(bar_pf, it & 1, sAbort)) {
-              if (it < 3) OW_TR(2, it * 32 + 24);
               load_item(it + 1);
             }
             if (item_of(it + 1) / nMB != item_of(it) / nMB && mbar_wait(bar_we, epoch & 1, sAbort)) {
@@ -824,7 +829,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
               load_all(it + 1);
             }
             if (mbar_wait(bar_epd, it & 1, sAbort)) {
-              if (it < 3) OW_TR(2, it * 32 + 25);
               load_t(it + 1);
             }
           }
@@ -833,13 +837,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           for (int c = 0; c < total && !*sAbort; ++c) {
             const int it = c / nsub, j = c - it * nsub;
             if (j == nsub - 1 && it + 1 < nit && mbar_wait(bar_pf, it & 1, sAbort)) {
-              if (it < 3) OW_TR(2, it * 32 + 24);
               load_item(it + 1);
             }
             if (c + C::D_NST < total && mbar_wait(bar_we + c % C::D_NST, (c / C::D_NST) & 1, sAbort))
               load_w(c + C::D_NST);
             if (j == nsub - 1 && mbar_wait(bar_tf, it & 1, sAbort)) {
-              if (it < 3) OW_TR(2, it * 32 + 25);
               load_t(it);
             }
           }
@@ -851,7 +853,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           bulk_g2s(sm + bf * 3 * C::P_BYTES, item_src(it), 3 * C::P_BYTES, bar_p + bf);
         };
         auto load_w = [&](int c) {
-          { const int i_ = c / nsub, j_ = c % nsub; if (i_ < 3 && j_ < 6) OW_TR(2, i_ * 32 + 26 + j_); }
           const int st = c & 1;
           mbar_arrive_expect_tx(bar_wf + st, C::A_BYTES);
           bulk_g2s(sm + C::U_W + st * C::A_BYTES, stage_src(c), C::A_BYTES, bar_wf + st);
@@ -868,7 +869,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           const int it = c / nsub, j = c - it * nsub;
           if (!C::RES && c + 2 < total && mbar_wait(bar_a + (c & 1), (c >> 1) & 1, sAbort)) load_w(c + 2);
           if (j == nsub - 1 && it + NB_UV < nit && mbar_wait(bar_w, it & 1, sAbort)) {
-            if (it < 3) OW_TR(2, it * 32 + 24);
             load_item(it + NB_UV);
           }
         }
@@ -883,7 +883,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           bulk_g2s(sm + C::OFF_X1, item_src(it) + C::PK_H * C::P_BYTES, 2 * C::P_BYTES, bar_gl);
         };
         auto load_w1 = [&](int c) {
-          { const int i_ = c / nsub, j_ = c % nsub; if (i_ < 3 && j_ < 6) OW_TR(2, i_ * 32 + 26 + j_); }
           const int st = c & 1;
           mbar_arrive_expect_tx(bar_wf + st, 2 * C::SUB_BYTES);
           bulk_g2s(sm + C::O_W1 + st * 2 * C::SUB_BYTES, stage_src(c), 2 * C::SUB_BYTES, bar_wf + st);
@@ -912,7 +911,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           if (!C::RES && c + 2 < total && mbar_wait(bar_a + (c & 1), (c >> 1) & 1, sAbort)) load_w1(c + 2);
           const bool last = j == nsub - 1 && it + 1 < nit;
           if (last && mbar_wait(bar_pf, it & 1, sAbort)) {
-            if (it < 3) OW_TR(2, it * 32 + 24);
             load_p(it + 1);
           }
           if (!C::RES && c % C::SPC == C::SPC - 1) {
@@ -920,7 +918,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
             if (kc + 2 < nck && mbar_wait(bar_boe + (kc & 1), (kc >> 1) & 1, sAbort)) load_bo(kc + 2);
           }
           if (last && mbar_wait(bar_epd, it & 1, sAbort)) {
-            if (it < 3) OW_TR(2, it * 32 + 25);
             load_g(it + 1);
           }
         }
@@ -985,13 +982,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
             if (it == 0 || item_of(it) / nMB != item_of(it - 1) / nMB) mbar_wait(bar_wf, epoch & 1, sAbort);
           }
           mbar_wait(bar_p, it & 1, sAbort);
-          if (it < 3) OW_TR(1, it * 32 + 20);
           tc_fence_after();
           for (int j = 0; j < nsub; ++j, ++c) {
             const int b = c & 1;
             if (j == 1 && it > 0) mbar_wait(bar_epd, (it - 1) & 1, sAbort);
             if (!C::RES) mbar_wait(bar_wf + c % C::D_NST, (c / C::D_NST) & 1, sAbort);
-            if (it < 3 && j < 3) OW_TR(1, it * 32 + 21 + j);
             tc_fence_after();
             if (!*sAbort) {
               const uint32_t aSt = s0 + C::D_W + (C::RES ? sub_of(j) : c % C::D_NST) * C::A_BYTES;
@@ -1001,7 +996,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
               kmma(tb + 2 * SC, aDY, BM, 0, aSt + 2 * C::SUB_BYTES, SC, 0, D / 16, ID_N, false);
             }
             umma_commit(bar_a + b);
-            if (it < 3 && j < 8) OW_TR(1, it * 32 + 8 + j);
             if (j == nsub - 1) umma_commit(bar_pf);
             if (j > 0) dp(c - 1);
           }
@@ -1022,7 +1016,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
         int c = 0;
         for (int it = 0; it < nit; ++it) {
           mbar_wait(bar_p + it % NB_UV, (it / NB_UV) & 1, sAbort);
-          if (it < 3) OW_TR(1, it * 32 + 20);
           tc_fence_after();
           const uint32_t aP = s0 + (it % NB_UV) * 3 * C::P_BYTES;
           if (C::RES && it == 0) mbar_wait(bar_wf, 0, sAbort);
@@ -1030,7 +1023,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
             const int b = c & 1;
             if (c >= 2) mbar_wait(bar_du + b, ((c - 2) >> 1) & 1, sAbort);  // TMEM buffer b read out
             if (!C::RES) mbar_wait(bar_wf + b, (c >> 1) & 1, sAbort);
-            if (it < 3 && j < 3) OW_TR(1, it * 32 + 21 + j);
             tc_fence_after();
             if (!*sAbort) {
               const uint32_t aSt = s0 + C::U_W + (C::RES ? sub_of(j) : b) * C::A_BYTES;
@@ -1040,7 +1032,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
               kmma(tb + 2 * SC, aP + 2 * C::P_BYTES, BM, 0, aSt + 2 * C::SUB_BYTES, SC, 0, D / 16, ID_N, false);
             }
             umma_commit(bar_a + b);
-            if (it < 3 && j < 8) OW_TR(1, it * 32 + 8 + j);
             if (NB_UV == 2 && j == 0 && it > 0) products(it - 1);
           }
           if (NB_UV == 1) products(it);
@@ -1078,13 +1069,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           // reuse of the Z pair buffer), the rest waits below.
           if (C::RES && it == 0) mbar_wait(bar_wf, 0, sAbort);
           mbar_wait(bar_p, it & 1, sAbort);
-          if (it < 3) OW_TR(1, it * 32 + 20);
           tc_fence_after();
           for (int j = 0; j < nsub; ++j, ++c) {
             const int b = c & 1;
             if (j == 1 && it > 0) mbar_wait(bar_epd, (it - 1) & 1, sAbort);
             if (!C::RES) mbar_wait(bar_wf + b, (c >> 1) & 1, sAbort);
-            if (it < 3 && j < 3) OW_TR(1, it * 32 + 21 + j);
             tc_fence_after();
             if (!*sAbort) {
               const uint32_t aSt = s0 + C::O_W1 + (C::RES ? sub_of(j) : b) * 2 * C::SUB_BYTES;
@@ -1093,7 +1082,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
               kmma(tb + SC, aPv, BM, 0, aSt + C::SUB_BYTES, SC, 0, D / 16, ID_N, false);
             }
             umma_commit(bar_a + b);
-            if (it < 3 && j < 8) OW_TR(1, it * 32 + 8 + j);
             if (j == nsub - 1) umma_commit(bar_pf);
             if (j > 0) y(c - 1);
           }
@@ -1144,7 +1132,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
       for (int j = 0; j < nsub; ++j, ++c) {
         const int b = c & 1;
         mbar_wait(bar_a + b, (c >> 1) & 1, sAbort);
-        if (tid == 0 && it < 3 && j < 8) OW_TR(0, it * 32 + j);
         __syncwarp();
         tc_fence_after();
         if (role != R_O) {
@@ -1154,7 +1141,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           tmem_ld_cols<HC>(trow + tcol + SC, vr);
           tmem_ld_cols<HC>(trow + tcol + 2 * SC, zr);
           tmem_ld_wait();
-          if (tid == 0 && it < 3 && j < 4) OW_TR(0, it * 32 + 24 + j);
           unsigned char* du_at;
           int col0;
           int dv_off;
@@ -1223,15 +1209,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           }
           if (fo + SC == 128) ++pc;
         }
-        if (tid == 0 && it < 3 && j < 4) OW_TR(0, it * 32 + 28 + j);
         fence_proxy_async_smem();
         tc_fence_before();
-        if (tid == 0 && it < 3 && j < 8) OW_TR(0, it * 32 + 8 + j);
         mbar_arrive(bar_du + b);
       }
 
       // ---- per-item epilogue
-      if (tid == 0 && it < 3) OW_TR(0, it * 32 + 16);
       if (role == R_DGRAD) {
         // Metadata of this item for the dX scatter.
         if (tid < BM) sRow[tid] = mreg.valid && mreg.tok < p.N ? mreg.b * p.N + mreg.tok : -1;
@@ -1241,7 +1224,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
         if (it + 1 < nit) mreg = meta_issue(it + 1);
         const bool cont = *sCont != 0;
         mbar_wait(bar_b + ((c - 1) & 1), ((c - 1) >> 1) & 1, sAbort);  // last dP of the item done
-        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 17);
         __syncwarp();
         tc_fence_after();
         // Warp (lq, hw): tiles 2lq, 2lq+1 (TMEM lanes 32lq..32lq+31), channels
@@ -1270,7 +1252,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
               tmem_ld16x256_x2(tl_addr + C::T_DPV + k0, pv[n4]);
             }
             tmem_ld_wait();
-            if (tid == 0 && it < 3) OW_TR(0, it * 32 + 20 + 2 * hf);
             float cc[4][2][4];  // [16-channel step][channel block nb][C fragment]
 #pragma unroll
             for (int n4 = 0; n4 < 4; ++n4) {
@@ -1340,12 +1321,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
                   }
                 }
             }
-            if (tid == 0 && it < 3) OW_TR(0, it * 32 + 21 + 2 * hf);
           }
         }
         // Pass 2: dA_u += dP_u T^T, dA_v += dP_v T^T with T from its image.
         mbar_wait(bar_t, it & 1, sAbort);
-        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 18);
         __syncwarp();
         {
           const uint32_t aT = smem_u32(sm + C::D_TT);
@@ -1381,7 +1360,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
             }
           }
         }
-        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 19);
         tc_fence_before();
         mbar_arrive(bar_epd);  // T region free for the next item's T
         comp_sync();  // T and the metadata are read out
@@ -1389,7 +1367,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
         mbar_wait(bar_yd, it & 1, sAbort);        // Y complete
         mbar_wait(bar_w, (pc - 1) & 1, sAbort);   // last M_o done with the pair buffer
         mbar_wait(bar_gl, it & 1, sAbort);        // H and G' of this item present
-        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 17);
         __syncwarp();
         tc_fence_after();
         unsigned char* stY = sm + C::O_ZP;
@@ -1416,7 +1393,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           gram16<BF16>(accA[0], rowG, rowY, lane);
           comp_sync();
         }
-        if (tid == 0 && it < 3) OW_TR(0, it * 32 + 19);
         tc_fence_before();
         mbar_arrive(bar_epd);
       }
@@ -1491,6 +1467,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
 
   __syncwarp();
   __syncthreads();
+  report_abort(sAbort, a.fault);
   if (*sAbort) {
     for (int i = 0; i < 1000; ++i) __nanosleep(1000);
   }
@@ -1625,6 +1602,8 @@ int tc_backward_t(const ow_bigemm_args_t* ar, const ow_bigemm_grads_t* gr, const
   if (block) nbw = norm_bwd_take((int64_t)p.B * p.N, p.C, ws);
   if (!ws.base) return OW_OK;
   BwdArgs a{};
+  OW_RETURN_IF(fault_word(&a.fault));
+  a.probe_ns = wait_probe_ns();
   a.p = p;
   a.x = ar->x;
   a.dout = gr->dout;
@@ -1800,14 +1779,3 @@ int tc_backward(const ow_bigemm_args_t* a, const ow_bigemm_grads_t* gr, const Pr
 }
 
 }  // namespace ow
-
-#ifdef OW_TRACE
-extern "C" __attribute__((visibility("default"))) int ow_trace_bwd(void* host, size_t bytes, int clear) {
-  if (clear) {
-    void* dev = nullptr;
-    cudaGetSymbolAddress(&dev, ow::sm100::g_trace);
-    return (int)cudaMemset(dev, 0, sizeof(ow::sm100::g_trace));
-  }
-  return (int)cudaMemcpyFromSymbol(host, ow::sm100::g_trace, bytes);
-}
-#endif

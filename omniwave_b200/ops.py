@@ -36,6 +36,7 @@ __all__ = [
     "bigemm_delta_cuda",
     "block_forward",
     "cuda_is_supported",
+    "drop_path_scale",
     "select_backend",
     "VALID_BACKENDS",
 ]
@@ -234,7 +235,8 @@ class _CudaBiGEMM(torch.autograd.Function):
         args = _make_args(x_c, plan, tok, ch, weights, w_dtype, compute, None, None, None,
                           False, out, out_dtype)
         ws = _workspace(lib, args, x.device, backward=False)
-        _lib.check(lib.ow_bigemm_fwd(args, _lib.stream_handle(x.device)), "ow_bigemm_fwd")
+        with torch.cuda.device(x.device):  # the library launches on the current device
+            _lib.check(lib.ow_bigemm_fwd(args, _lib.stream_handle(x.device)), "ow_bigemm_fwd")
         del ws
         ctx.save_for_backward(x_c, *weights)
         ctx.plan, ctx.compute, ctx.w_dtype, ctx.out_dtype = plan, compute, w_dtype, out_dtype
@@ -254,7 +256,8 @@ class _CudaBiGEMM(torch.autograd.Function):
         dx = torch.empty_like(x)
         gw, _ = _grad_buffers(x, weights, ctx.w_dtype, False)
         grads = _lib.Grads(dout.data_ptr(), dx.data_ptr(), *[g.data_ptr() for g in gw], None)
-        _lib.check(lib.ow_bigemm_bwd(args, grads, _lib.stream_handle(x.device)), "ow_bigemm_bwd")
+        with torch.cuda.device(x.device):
+            _lib.check(lib.ow_bigemm_bwd(args, grads, _lib.stream_handle(x.device)), "ow_bigemm_bwd")
         del ws
         out = [dx] + gw
         out = [o.to(dt) for o, dt in zip(out, ctx.in_dtypes)]
@@ -270,6 +273,20 @@ def bigemm_delta_cuda(*, x, plan, a_u, a_v, a_o, b_u, b_v, b_o, gamma) -> Tensor
     return _CudaBiGEMM.apply(x, plan, _compute_dtype(x), a_u, a_v, a_o, b_u, b_v, b_o, gamma)
 
 
+def _reference_bigemm():
+    """The reference package's own ``bigemm`` (for its reference/compile/triton backends)."""
+    try:
+        from omniweave.ops import bigemm as ref_mod
+    except ImportError as exc:
+        raise RuntimeError(
+            "the 'reference', 'compile' and 'triton' backends belong to the omniweave package, "
+            "which is not importable here; omniwave_b200 implements 'cuda'"
+        ) from exc
+    # After omniwave_b200.integration.install() the module attribute is the
+    # patched dispatcher; it passes these names on to the reference function.
+    return ref_mod.bigemm
+
+
 def bigemm(
     *,
     x: Tensor,
@@ -281,13 +298,15 @@ def bigemm(
     b_v: Tensor,
     b_o: Tensor,
     gamma: Tensor,
-    backend: str = "cuda",
+    backend: str = "reference",
 ) -> Tensor:
     """Compute the BiGEMM residual delta (reference ``bigemm``, ops/bigemm.py:24-73).
 
-    ``backend``: ``"cuda"`` (this package's kernels) or ``"auto"`` (``"cuda"``
-    when supported).  ``"reference"``, ``"compile"`` and ``"triton"`` name the
-    reference package's own backends; they are not implemented here and raise.
+    Same signature and default as the reference.  ``"cuda"`` runs this
+    package's kernels; ``"auto"`` picks ``"cuda"`` when it is supported and
+    otherwise applies the reference's own ``"auto"`` policy; ``"reference"``,
+    ``"compile"`` and ``"triton"`` are passed to the installed ``omniweave``
+    package.  Unknown names raise ``ValueError``.
     """
     kwargs = dict(x=x, plan=plan, a_u=a_u, a_v=a_v, a_o=a_o, b_u=b_u, b_v=b_v, b_o=b_o, gamma=gamma)
     if backend not in VALID_BACKENDS:
@@ -296,17 +315,12 @@ def bigemm(
             f"'cuda', or 'auto'"
         )
     if backend == "auto":
-        chosen, reason = select_backend(x, "auto", lambda t: cuda_is_supported(t, plan, b_u))
-        if chosen != "cuda":
-            raise RuntimeError(
-                f"backend 'auto' resolved to {chosen!r} ({reason}); omniwave_b200 computes only "
-                f"the 'cuda' backend"
-            )
-        backend = "cuda"
+        chosen, _ = select_backend(x, "auto", lambda t: cuda_is_supported(t, plan, b_u))
+        if chosen == "cuda":
+            return bigemm_delta_cuda(**kwargs)
+        return _reference_bigemm()(backend="auto", **kwargs)
     if backend != "cuda":
-        raise RuntimeError(
-            f"backend {backend!r} belongs to the omniweave package; omniwave_b200 implements 'cuda'"
-        )
+        return _reference_bigemm()(backend=backend, **kwargs)
     return bigemm_delta_cuda(**kwargs)
 
 
@@ -326,9 +340,10 @@ class _CudaBlock(torch.autograd.Function):
         stat_dtype = torch.float64 if compute == torch.float64 else torch.float32
         rstd = torch.empty(b * h * w, dtype=stat_dtype, device=dev)
         stream = _lib.stream_handle(dev)
-        _lib.check(lib.ow_rmsnorm_rstd(x_c.data_ptr(), _lib.DTYPE_CODE[x.dtype],
-                                       _lib.DTYPE_CODE[compute], b * h * w, c, RMS_EPS,
-                                       rstd.data_ptr(), stream), "ow_rmsnorm_rstd")
+        with torch.cuda.device(dev):
+            _lib.check(lib.ow_rmsnorm_rstd(x_c.data_ptr(), _lib.DTYPE_CODE[x.dtype],
+                                           _lib.DTYPE_CODE[compute], b * h * w, c, RMS_EPS,
+                                           rstd.data_ptr(), stream), "ow_rmsnorm_rstd")
         delta_dtype = torch.promote_types(compute, gamma.dtype)
         out_dtype = torch.promote_types(x.dtype, delta_dtype)
         out = torch.empty(x.shape, dtype=out_dtype, device=dev)
@@ -336,7 +351,8 @@ class _CudaBlock(torch.autograd.Function):
         args = _make_args(x_c, plan, tok, ch, weights, w_dtype, compute, rstd, nw, scale_c,
                           True, out, out_dtype)
         ws = _workspace(lib, args, dev, backward=False)
-        _lib.check(lib.ow_bigemm_fwd(args, stream), "ow_bigemm_fwd")
+        with torch.cuda.device(dev):
+            _lib.check(lib.ow_bigemm_fwd(args, stream), "ow_bigemm_fwd")
         del ws
         ctx.save_for_backward(x_c, rstd, nw, *weights)
         ctx.scale = scale_c
@@ -358,11 +374,28 @@ class _CudaBlock(torch.autograd.Function):
         gw, dnw = _grad_buffers(x, weights, ctx.w_dtype, True)
         grads = _lib.Grads(dout.data_ptr(), dx.data_ptr(), *[g.data_ptr() for g in gw],
                            dnw.data_ptr())
-        _lib.check(lib.ow_bigemm_bwd(args, grads, _lib.stream_handle(x.device)), "ow_bigemm_bwd")
+        with torch.cuda.device(x.device):
+            _lib.check(lib.ow_bigemm_bwd(args, grads, _lib.stream_handle(x.device)), "ow_bigemm_bwd")
         del ws
         out = [dx, dnw] + gw
         out = [o.to(dt) for o, dt in zip(out, ctx.in_dtypes)]
         return (out[0], None, None, None, *out[1:])
+
+
+def drop_path_scale(x: Tensor, gamma: Tensor, rate: float, training: bool) -> Tensor | None:
+    """Per-sample drop-path scale ``keep_mask / keep_probability`` of block.py:99-107.
+
+    Draws the same Bernoulli sample as the reference (a ``[B,1,1,1]`` tensor of
+    the delta's dtype on ``x``'s device), so a seeded run keeps the same
+    samples; ``None`` when drop-path is inactive.
+    """
+    if not (training and rate):
+        return None
+    keep = 1.0 - rate
+    compute = torch.get_autocast_dtype("cuda") if (x.is_cuda and torch.is_autocast_enabled("cuda")) else x.dtype
+    dtype = torch.promote_types(torch.promote_types(compute, gamma.dtype), x.dtype)
+    mask = torch.empty((x.shape[0], 1, 1, 1), dtype=dtype, device=x.device).bernoulli_(keep)
+    return (mask / keep).reshape(-1)
 
 
 def block_forward(x: Tensor, plan: RoutePlan, norm_w: Tensor, a_u: Tensor, a_v: Tensor,

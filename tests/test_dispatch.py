@@ -52,15 +52,29 @@ def test_cpu_tensor_is_unsupported_and_never_computed_on_host():
     assert not ok and reason == "CUDA is unavailable"
     with pytest.raises(RuntimeError, match="CUDA is unavailable"):
         bigemm(x=x, plan=plan, backend="cuda", **_ops_args())
-    with pytest.raises(RuntimeError, match="resolved to 'reference'"):
-        bigemm(x=x, plan=plan, backend="auto", **_ops_args())
 
 
-@pytest.mark.parametrize("name", ["reference", "compile", "triton"])
-def test_reference_backends_are_not_implemented_here(name):
+def test_reference_backends_go_to_the_reference_package(omniweave):
+    """``"reference"`` (the default, as in bigemm.py:35) and an unsupported
+    ``"auto"`` run the reference package's own code, never this package's."""
+    from omniweave.ops.reference import bigemm_delta_reference
+
     plan = build_route_plan(8, 8, 128, 16, 64, "local")
-    with pytest.raises(RuntimeError, match="belongs to the omniweave package"):
-        bigemm(x=torch.randn(1, 8, 8, 128), plan=plan, backend=name, **_ops_args())
+    x = torch.randn(1, 8, 8, 128)
+    ref = bigemm_delta_reference(x=x, plan=plan, **_ops_args())
+    assert torch.equal(bigemm(x=x, plan=plan, **_ops_args()), ref)
+    assert torch.equal(bigemm(x=x, plan=plan, backend="reference", **_ops_args()), ref)
+    assert torch.equal(bigemm(x=x, plan=plan, backend="auto", **_ops_args()), ref)
+
+
+def test_reference_backends_without_the_reference_package(monkeypatch):
+    import sys
+
+    monkeypatch.setitem(sys.modules, "omniweave", None)
+    monkeypatch.setitem(sys.modules, "omniweave.ops", None)
+    plan = build_route_plan(8, 8, 128, 16, 64, "local")
+    with pytest.raises(RuntimeError, match="belong to the omniweave package"):
+        bigemm(x=torch.randn(1, 8, 8, 128), plan=plan, backend="reference", **_ops_args())
 
 
 def test_unknown_backend_in_bigemm():

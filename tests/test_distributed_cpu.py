@@ -117,12 +117,52 @@ def test_shard_range_covers_batch():
             assert max(b - a for a, b in parts) - min(b - a for a, b in parts) <= 1
 
 
-def test_nonfinite_loss_fails_fast():
+def test_nonfinite_loss_skips_the_update_and_fails_fast():
+    """A non-finite loss leaves weights (and the EMA) untouched without a host
+    sync; check_finite then raises, as the reference raises at engine.py:205."""
     from omniwave_b200.train import TrainStep
 
     model = _mlp(0)
-    ts = TrainStep(model, amp_dtype=None)
+    ts = TrainStep(model, amp_dtype=None, ema_decay=0.9)
+    before = [p.detach().clone() for p in model.parameters()]
+    ema_before = {k: v.clone() for k, v in ts.ema.state.items()}
     x = torch.full((4, 12), float("nan"))
     ts.step(x, torch.zeros(4, dtype=torch.long))
+    for p, b in zip(model.parameters(), before):
+        assert torch.equal(p.detach(), b)
+    for k, v in ts.ema.state.items():
+        assert torch.equal(v, ema_before[k]), k
     with pytest.raises(FloatingPointError):
         ts.check_finite()
+    # A later finite step updates normally.
+    g = torch.Generator().manual_seed(1)
+    ts.step(torch.randn(4, 12, generator=g), torch.zeros(4, dtype=torch.long))
+    assert any(not torch.equal(p.detach(), b) for p, b in zip(model.parameters(), before))
+
+
+def test_step_with_clip_and_ema_matches_reference_engine_semantics():
+    """clip_grad_norm_ then AdamW then EMAModel.update, as engine.py:243-257."""
+    from omniwave_b200.train import TrainStep
+
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(6, 12, generator=g) * 10
+    y = torch.randint(0, 5, (6,), generator=g)
+    model = _mlp(3)
+    ts = TrainStep(model, amp_dtype=None, clip_norm=0.5, ema_decay=0.8)
+    ref = _mlp(3)
+    opt = torch.optim.AdamW(ref.parameters(), lr=1e-3, weight_decay=0.05)
+    ema = {k: v.detach().clone() for k, v in ref.state_dict().items()}
+    for _ in range(3):
+        ts.step(x, y)
+        loss = nn.functional.cross_entropy(ref(x), y)
+        opt.zero_grad(set_to_none=True)
+        loss.backward()
+        nn.utils.clip_grad_norm_(ref.parameters(), 0.5)
+        opt.step()
+        with torch.no_grad():
+            for k, p in ref.named_parameters():
+                ema[k].lerp_(p, 1 - 0.8)
+    for p, q in zip(model.parameters(), ref.parameters()):
+        torch.testing.assert_close(p.detach(), q.detach(), rtol=1e-6, atol=1e-7)
+    for k, v in ts.ema.state_dict().items():
+        torch.testing.assert_close(v, ema[k], rtol=1e-6, atol=1e-7)

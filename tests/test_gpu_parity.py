@@ -9,6 +9,8 @@ through the C ABI of libomniwave_b200.so.
 
 from __future__ import annotations
 
+import json
+import os
 import zlib
 
 import numpy as np
@@ -114,7 +116,7 @@ ROUTES = [("local", 0), ("shifted", 0), ("radix", 0), ("radix", 1), ("radix", 2)
 
 @pytest.mark.parametrize("shape", STAGES, ids=lambda s: f"{s[0]}x{s[1]}x{s[2]}")
 @pytest.mark.parametrize("route", ROUTES, ids=lambda r: f"{r[0]}{r[1]}")
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 def test_stage_shapes_vs_oracle(cuda_device, shape, route, dtype):
     """Every BASELINE stage shape and route (B=2) against the fp64 oracle."""
     from omniwave_b200 import build_route_plan
@@ -159,22 +161,54 @@ def test_autocast_bf16_matches_oracle(cuda_device):
         assert rel_err(g.cpu().numpy(), ref_g[k]) <= 2e-2, k
 
 
-def test_full_size_stage3_bf16(cuda_device):
-    """The headline case at full size: B=128, 14x14x512, bf16, fwd + bwd."""
-    from omniwave_b200 import build_route_plan
+def config2_case(h, w, c, d, route, level, batch=128):
+    """BASELINE config 2's inputs: ``torch.manual_seed(1)``, an fp32
+    ``OmniWeaveBlock`` with default init (orthogonal A_u/A_v, identity A_o,
+    xavier B, gamma 1e-5), then ``x`` and ``dY`` ~ N(0,1), all cast to bf16
+    (the order of scripts/benchmark.py:56-110)."""
+    from omniwave_b200 import OmniWeaveBlock
 
-    arrays, dout = _rand_case(14, 14, 512, 128, 128, seed=9)
-    arrays = {k: _round(v, torch.bfloat16) for k, v in arrays.items()}
-    dout = _round(dout, torch.bfloat16)
-    plan = build_route_plan(14, 14, 512, 16, 128, "local", 0)
-    p = O.Plan(plan.token_indices.numpy(), plan.channel_indices.numpy(),
-               plan.token_mask.numpy(), plan.channel_mask.numpy(), 14, 14, 512)
-    wargs = [arrays[k] for k in NAMES[1:]]
+    torch.manual_seed(1)
+    blk = OmniWeaveBlock(h, w, c, d, route, level)
+    x = torch.randn(batch, h, w, c)
+    dy = torch.randn(batch, h, w, c)
+    t = {"x": x}
+    t.update({k: getattr(blk, k).detach() for k in NAMES[1:]})
+    return blk.plan, {k: v.to(torch.bfloat16) for k, v in t.items()}, dy.to(torch.bfloat16)
+
+
+FULL_SIZE_ERRORS: dict[str, dict[str, float]] = {}
+
+
+@pytest.mark.parametrize("shape", STAGES, ids=lambda s: f"{s[0]}x{s[1]}x{s[2]}")
+@pytest.mark.parametrize("route", ROUTES, ids=lambda r: f"{r[0]}{r[1]}")
+def test_full_size_config2_bf16(cuda_device, shape, route, record_property):
+    """Every benchmarked case at full size (B=128, bf16, fwd + bwd) on BASELINE
+    config 2's inputs against the oracle on the bf16-rounded operands.  The
+    oracle runs in float32 here (its own error, ~1e-6 of max|ref|, is far
+    below the 2e-2 bf16 tolerance) to keep the host time and memory of the
+    largest case to seconds and a few GB."""
+    h, w, c, d = shape
+    plan, t16, dy16 = config2_case(h, w, c, d, *route)
+    arrays = {k: v.float().numpy() for k, v in t16.items()}
+    dout = dy16.float().numpy()
     res = run_cuda(plan, arrays, dout, torch.bfloat16, cuda_device)
-    assert rel_err(res["out"], O.forward(arrays["x"], p, *wargs)) <= 2e-2
+    p = O.Plan(plan.token_indices.numpy(), plan.channel_indices.numpy(),
+               plan.token_mask.numpy(), plan.channel_mask.numpy(), h, w, c)
+    wargs = [arrays[k] for k in NAMES[1:]]
+    errs = {"out": rel_err(res["out"], O.forward(arrays["x"], p, *wargs))}
     ref_g = O.backward(dout, arrays["x"], p, *wargs)
-    for k in NAMES:
-        assert rel_err(res[k], ref_g[k]) <= 2e-2, k
+    errs.update({f"d{k}": rel_err(res[k], ref_g[k]) for k in NAMES})
+    case = f"{h}x{w}x{c}/{route[0]}{route[1]}"
+    FULL_SIZE_ERRORS[case] = errs
+    record_property("max_rel_err", errs)
+    print(case, " ".join(f"{k}={v:.2e}" for k, v in errs.items()))
+    report = os.environ.get("OW_PARITY_REPORT")
+    if report:
+        with open(report, "w") as f:
+            json.dump(FULL_SIZE_ERRORS, f, indent=1)
+    for k, v in errs.items():
+        assert v <= 2e-2, (k, v)
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])

@@ -5,8 +5,11 @@ plugin host that hands over only input and output buffers, code that must not
 enter the process's allocator) use this entry point: its scratch is a fixed
 array inside the library, not a caller workspace.  These tests call it through
 the C ABI and check, on two calls in a row, that it gives the same result as
-ow_bigemm_fwd with a workspace, within the tolerance the other parity tests
-use (2e-2 relative for bf16 compute, 1e-4 for fp32).  The file is named so that
+ow_bigemm_fwd with a workspace: within the tolerance the other parity tests
+use (2e-2 relative for bf16 compute, 1e-4 for fp32), and in fact bitwise,
+since both run the same kernels on the same inputs.  Between the two checked
+calls a call on a different problem leaves other data in the shared scratch,
+so nothing relies on the scratch starting out zeroed or unchanged.  The file is named so that
 pytest collects it last.
 """
 
@@ -44,33 +47,54 @@ def _case(dev, h, w, c, d, b, dtype, route="shifted", level=0, seed=0):
     return make_args, keep
 
 
+def _workspace_forward(lib, make_args, out, stream):
+    from omniwave_b200 import _lib
+
+    a = make_args(out)
+    n = lib.ow_bigemm_workspace_size(ctypes.byref(a), 0)
+    wsb = torch.empty(n, dtype=torch.uint8, device=out.device)
+    a.workspace, a.workspace_bytes = wsb.data_ptr(), n
+    _lib.check(lib.ow_bigemm_fwd(ctypes.byref(a), stream), "ow_bigemm_fwd")
+    return wsb
+
+
+def _noalloc_forward(lib, make_args, out, stream):
+    from omniwave_b200 import _lib
+
+    a = make_args(out)
+    _lib.check(lib.ow_bigemm_fwd_noalloc(ctypes.byref(a), stream), "ow_bigemm_fwd_noalloc")
+
+
 def _run_pair(dev, dtype, shape, tol):
     from omniwave_b200 import _lib
 
     lib = _lib.load()
     h, w, c, d, b = shape
     make_args, keep = _case(dev, h, w, c, d, b, dtype)
+    # A different problem (batch, route, weights) whose call leaves other data
+    # in the shared scratch between the two checked calls.
+    other_args, other_keep = _case(dev, h, w, c, d, max(1, b // 2), dtype, route="radix", level=1, seed=7)
     stream = _lib.stream_handle(dev)
     ref = torch.empty(b, h, w, c, device=dev, dtype=dtype)
-    a = make_args(ref)
-    n = lib.ow_bigemm_workspace_size(ctypes.byref(a), 0)
-    wsb = torch.empty(n, dtype=torch.uint8, device=dev)
-    a.workspace, a.workspace_bytes = wsb.data_ptr(), n
-    _lib.check(lib.ow_bigemm_fwd(ctypes.byref(a), stream), "ow_bigemm_fwd")
+    wsb = _workspace_forward(lib, make_args, ref, stream)
     outs = []
-    for _ in range(2):  # two calls in a row share (and reuse) the static scratch
+    for i in range(2):  # two checked calls in a row share the static scratch
         o = torch.full((b, h, w, c), float("nan"), device=dev, dtype=dtype)
-        a2 = make_args(o)
-        _lib.check(lib.ow_bigemm_fwd_noalloc(ctypes.byref(a2), stream), "ow_bigemm_fwd_noalloc")
+        _noalloc_forward(lib, make_args, o, stream)
         outs.append(o)
+        if i == 0:
+            junk = torch.full((max(1, b // 2), h, w, c), float("nan"), device=dev, dtype=dtype)
+            _noalloc_forward(lib, other_args, junk, stream)
     torch.cuda.synchronize(dev)
     r = ref.double().cpu().numpy()
     for o in outs:
         on = o.double().cpu().numpy()
         assert np.isfinite(on).all()
         assert rel_err(on, r) <= tol
+        # Same kernels on the same inputs: the results are bitwise equal.
+        assert torch.equal(o, ref)
     assert lib.ow_device_fault(dev.index or 0, 0) == 0
-    del keep
+    del keep, other_keep, wsb
 
 
 def test_noalloc_matches_workspace_forward_bf16(cuda_device):
