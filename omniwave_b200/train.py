@@ -180,9 +180,9 @@ class TrainStep:
         self._params = [p for p in model.parameters() if p.requires_grad]
         # 1.0 when this step saw a non-finite loss or gradient (fused AdamW's
         # found_inf input), and a sticky flag over all steps for check_finite.
-        self._found = torch.zeros(1, dtype=torch.float32, device=self.device)
+        self._found = torch.zeros((), dtype=torch.float32, device=self.device)
         self._bad = torch.zeros((), dtype=torch.bool, device=self.device)
-        self._one = torch.ones(1, dtype=torch.float32, device=self.device)
+        self._one = torch.ones((), dtype=torch.float32, device=self.device)
         self._graph = None
         self._graph_warmup = graph_warmup if cuda_graph else -1
         self._nsteps = 0
@@ -198,7 +198,7 @@ class TrainStep:
         self.optimizer.zero_grad(set_to_none=True)
         loss.backward()
         loss = loss.detach()
-        self._found.copy_((~torch.isfinite(loss)).reshape(1).to(torch.float32))
+        self._found.copy_((~torch.isfinite(loss)).to(torch.float32))
         grads = [p.grad for p in self._params if p.grad is not None]
         if self.device.type == "cuda":
             # One multi-tensor pass: sets _found when any gradient is inf/nan.
@@ -220,7 +220,7 @@ class TrainStep:
                     p.copy_(torch.where(keep, old, p))
         if self.ema is not None:
             self.ema.update(self.module, skip=self._found)
-        self._bad |= self._found.bool().reshape(())
+        self._bad |= self._found.bool()
         return loss
 
     def step(self, images: Tensor, labels: Tensor) -> Tensor:

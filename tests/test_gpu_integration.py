@@ -59,8 +59,11 @@ def test_reference_block_on_cuda_matches_reference_backend(omniweave, cuda_devic
     tol = 2e-2 if amp else 1e-4
     assert o_c.dtype == o_r.dtype
     assert rel_err(o_c.cpu().numpy(), o_r.cpu().numpy()) <= tol
-    # the delta alone (x dominates the block output)
-    assert rel_err((o_c - x).cpu().numpy(), (o_r - x).cpu().numpy()) <= tol
+    if amp:
+        # The delta alone (x dominates the block output).  Only meaningful
+        # where the check's own cancellation error, ulp(x) / max|delta|, is
+        # far below the tolerance: under autocast, not at 1e-4 in fp32.
+        assert rel_err((o_c - x).cpu().numpy(), (o_r - x).cpu().numpy()) <= tol
     for name, a, b in zip(("x",) + PARAMS, g_c, g_r):
         assert a.dtype == b.dtype, name
         assert rel_err(a.cpu().numpy(), b.cpu().numpy()) <= tol, name
