@@ -26,20 +26,35 @@ struct Prob {
 };
 
 #ifdef __CUDACC__
-// contig[qc] = 1 when channel group qc is one run of D consecutive channels
-// starting on a multiple of 8 (and C % 8 == 0), so 16-byte vector accesses
-// apply; one warp per group, called by every thread of the grid.
+// Channel layout of group qc, one int per group (``layout[qc]``):
+//   0            generic: channels gathered one by one through the table;
+//   S + 16 * c0  the group's channels are c0, c0 + S, ..., c0 + S (D - 1)
+//                with S in {1, 2, 4, 8} and C % 8 == 0, where
+//                S == 1: one aligned run (c0 % 8 == 0, c0 + D <= C), so
+//                        16-byte vector accesses apply directly;
+//                S > 1:  c0 < S and S D <= C, so every 64-channel half of
+//                        the group lies in the aligned span [64 S h, 64 S (h+1))
+//                        of the row, read with 16-byte vectors and
+//                        de-interleaved (the stride-Q_c groups of radix
+//                        routes at levels 1 and 2, routing.py:107-121).
+// One warp per group, called by every thread of the grid.
+__host__ __device__ constexpr int layout_stride(int v) { return v & 15; }
+__host__ __device__ constexpr int layout_c0(int v) { return v >> 4; }
+
 template <int D>
-__device__ __forceinline__ void contig_flags(const Prob& p, int* contig) {
+__device__ __forceinline__ void contig_flags(const Prob& p, int* layout) {
   const int lane = threadIdx.x & 31;
   const int gw = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
   const int nw = (int)((gridDim.x * blockDim.x) >> 5);
   for (int qc = gw; qc < p.Qc; qc += nw) {
     const int c0 = p.ch[qc * D];
-    bool ok = true;
-    for (int k = lane; k < D; k += 32) ok &= p.ch[qc * D + k] == c0 + k;
-    ok = __all_sync(0xffffffffu, ok);
-    if (lane == 0) contig[qc] = ok && (c0 % 8 == 0) && (c0 + D <= p.C) && (p.C % 8 == 0);
+    const int S = D > 1 ? p.ch[qc * D + 1] - c0 : 1;
+    bool ok = S == 1 || S == 2 || S == 4 || S == 8;
+    for (int k = lane; k < D && ok; k += 32) ok &= p.ch[qc * D + k] == c0 + S * k;
+    ok = __all_sync(0xffffffffu, ok) && (p.C % 8 == 0);
+    if (S == 1) ok = ok && (c0 % 8 == 0) && (c0 + D <= p.C);
+    else ok = ok && (c0 < S) && (S * D <= p.C);
+    if (lane == 0) layout[qc] = ok ? S + 16 * c0 : 0;
   }
 }
 #endif

@@ -396,14 +396,16 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict_
 
     // Channel-group state, reloaded when the group changes (rarely: items
     // are walked group-major).
-    int cur_qc = -1, ch0 = 0;
+    int cur_qc = -1, ch0 = 0, sstr = 0;
     bool cont = false;
     float gam[NP][4];  // gamma of channels np 16 + nb 8 + 2 t4 + e at [np][2 nb + e]
     auto set_group = [&](int qc) {
       if (qc == cur_qc) return;
       cur_qc = qc;
       ch0 = p.ch[qc * D];
-      cont = vec_ok && contig[qc] != 0;
+      const int lay = vec_ok ? contig[qc] : 0;
+      cont = layout_stride(lay) == 1;
+      sstr = layout_stride(lay) > 1 ? layout_stride(lay) : 0;  // channels ch0 + sstr k
 #pragma unroll
       for (int np = 0; np < NP; ++np)
 #pragma unroll
@@ -515,7 +517,43 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict_
             mma16816<BF16>(cc[n4][nb], fo, movm_trans(ay[2 * nb]), movm_trans(ay[2 * nb + 1]));
           }
         }
-        if (cont) {
+        if (sstr) {
+          // Strided group: the same staging, then 16 lanes store 16
+          // consecutive k of one row (sstr elements apart in the output),
+          // reading the residual at the same positions.
+#pragma unroll
+          for (int hr = 0; hr < 2; ++hr) {
+            const float sc = scf[hr];
+#pragma unroll
+            for (int n4 = 0; n4 < 4; ++n4)
+#pragma unroll
+              for (int nb = 0; nb < 2; ++nb) {
+                const float* gm = gam[hf * 4 + n4] + 2 * nb;
+                *reinterpret_cast<float2*>(stg + g * C::ST_LD + n4 * 16 + nb * 8 + 2 * t4) =
+                    make_float2(cc[n4][nb][2 * hr] * gm[0] * sc, cc[n4][nb][2 * hr + 1] * gm[1] * sc);
+              }
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int r8 = (i * 32 + lane) >> 4;
+              const int rw = sRows[tile_e * 16 + hr * 8 + r8];
+              const int64_t rowoff = (int64_t)(rw >= 0 ? rw : 0) * p.C + ch0 + (int64_t)sstr * hf * 64;
+              float xr[4] = {0.f, 0.f, 0.f, 0.f};
+              if (residual) {
+#pragma unroll
+                for (int m = 0; m < 4; ++m) xr[m] = load_as<float>(x, rowoff + (int64_t)sstr * ((lane & 15) + 16 * m));
+              }
+              if (rw >= 0) {
+#pragma unroll
+                for (int m = 0; m < 4; ++m) {
+                  const int k = (lane & 15) + 16 * m;
+                  out[rowoff + (int64_t)sstr * k] = Elem<TO>::from(stg[r8 * C::ST_LD + k] + xr[m]);
+                }
+              }
+            }
+            __syncwarp();  // the staging tile is rewritten by the next half-pass
+          }
+        } else if (cont) {
 #pragma unroll
           for (int hr = 0; hr < 2; ++hr) {
             const int sp = hf * 2 + hr;

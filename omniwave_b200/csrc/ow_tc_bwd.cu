@@ -307,7 +307,8 @@ struct GatherCtx {
   const int* row;   // [BM] b * N + token, or -1 for a pad row
   const int* ch;    // [D] channel indices
   int N, C;
-  bool cont;
+  bool cont;        // one aligned run of channels
+  int stride, c0;   // stride > 1: channels c0 + stride * k (layout_stride), else 0
 };
 
 // Gather one 64-channel half of the M-block (128 rows) into 16-bit storage.
@@ -464,6 +465,85 @@ __device__ __forceinline__ void rows_store(const RowRegs<TS, NHF>& R, int h, int
   }
 }
 
+// Gather of one 64-channel half of a strided group (channels c0 + S k,
+// S = gc.stride in {2, 4, 8}, c0 < S) into the row-major staging layout.
+// The half's channels lie in the aligned span [64 S hf, 64 S (hf + 1)) of the
+// row: consecutive threads read consecutive 16-byte vectors of it (the
+// sibling groups of the same rows read the rest, so the extra bytes come from
+// L2), and each vector contributes its 8 / S elements of this group.  Same
+// arithmetic as rows_store: x mode round(round(v * rstd) * nw[c]), gradient
+// mode v * scale[b]; pad rows are zero.
+template <typename TS, bool BF16, int S>
+__device__ __forceinline__ void gather_half_strided_t(const GatherCtx& gc, const TS* __restrict__ src, int hf,
+                                                      bool xnorm, const float* __restrict__ rstd,
+                                                      const float* __restrict__ nw, int x_dt,
+                                                      const float* __restrict__ scale, unsigned char* stg,
+                                                      int tid) {
+  constexpr int VW = sizeof(TS) == 2 ? 1 : 2;  // 16-byte vectors per 8 elements
+  constexpr int VPR = 8 * S;                   // vectors of 8 elements per row span
+  constexpr int UNITS = BM * VPR;              // 4 S units per thread
+  constexpr int UPP = 4;                       // units whose loads are in flight together
+  const int c0 = gc.c0;
+  const int64_t span0 = (int64_t)S * hf * 64;
+#pragma unroll 1
+  for (int u0 = 0; u0 < UNITS; u0 += UPP * NCOMP) {
+    uint4 v[UPP][VW];
+    float rs[UPP];
+#pragma unroll
+    for (int j = 0; j < UPP; ++j) {
+      const int unit = u0 + j * NCOMP + tid;
+      const int r = unit / VPR, vi = unit % VPR;
+      // Pad rows load row 0 (always valid) and are zeroed below.
+      const int rw = gc.row[r] >= 0 ? gc.row[r] : 0;
+      const uint4* p = reinterpret_cast<const uint4*>(src + (int64_t)rw * gc.C + span0 + vi * 8);
+#pragma unroll
+      for (int w = 0; w < VW; ++w) v[j][w] = __ldg(p + w);
+      rs[j] = xnorm ? rstd[rw] : (scale ? scale[rw / gc.N] : 1.f);
+    }
+#pragma unroll
+    for (int j = 0; j < UPP; ++j) {
+      const int unit = u0 + j * NCOMP + tid;
+      const int r = unit / VPR, vi = unit % VPR;
+      const bool pad = gc.row[r] < 0;
+#pragma unroll
+      for (int t = 0; t < 8 / S; ++t) {
+        const int i = c0 + S * t;  // this group's elements of the vector
+        const uint32_t w32 = (i >> 1) == 0 ? v[j][0].x : (i >> 1) == 1 ? v[j][0].y : (i >> 1) == 2 ? v[j][0].z : v[j][0].w;
+        float f;
+        if constexpr (sizeof(TS) == 2) {
+          const float2 t2 = unpack2<std::is_same_v<TS, __nv_bfloat16>>(w32);
+          f = (i & 1) ? t2.y : t2.x;
+        } else {
+          const uint4 q = i < 4 ? v[j][0] : v[j][VW - 1];  // selects, no dynamic register indexing
+          const int e = i & 3;
+          f = __uint_as_float(e == 0 ? q.x : e == 1 ? q.y : e == 2 ? q.z : q.w);
+        }
+        const int k = vi * (8 / S) + t;
+        if (xnorm) {
+          f = round_through(f * rs[j], x_dt);
+          f = round_through(f * nw[span0 + vi * 8 + i], x_dt);
+        } else {
+          f *= rs[j];
+        }
+        const uint32_t pk = pack2<BF16>(pad ? 0.f : f, 0.f);
+        *reinterpret_cast<uint16_t*>(stg + (r * STG_LD + k) * 2) = (uint16_t)(pk & 0xFFFF);
+      }
+    }
+  }
+}
+
+template <typename TS, bool BF16>
+__device__ __forceinline__ void gather_half_strided(const GatherCtx& gc, const TS* __restrict__ src, int hf,
+                                                    bool xnorm, const float* __restrict__ rstd,
+                                                    const float* __restrict__ nw, int x_dt,
+                                                    const float* __restrict__ scale, unsigned char* stg, int tid) {
+  switch (gc.stride) {
+    case 2: gather_half_strided_t<TS, BF16, 2>(gc, src, hf, xnorm, rstd, nw, x_dt, scale, stg, tid); break;
+    case 4: gather_half_strided_t<TS, BF16, 4>(gc, src, hf, xnorm, rstd, nw, x_dt, scale, stg, tid); break;
+    default: gather_half_strided_t<TS, BF16, 8>(gc, src, hf, xnorm, rstd, nw, x_dt, scale, stg, tid); break;
+  }
+}
+
 // Token mix of one 64-channel half: dst[rows of tile ``warp``] = A * staging,
 // written in SW128 K-major layout at channel offset hf*64.
 template <bool BF16>
@@ -585,7 +665,9 @@ __global__ void __launch_bounds__(NCOMP) tc_pack_kernel(BwdArgs a) {
   }
   for (int k = tid; k < D; k += NCOMP) sCh[k] = p.ch[qc * D + k];
   __syncthreads();
-  GatherCtx gc{sRow, sCh, p.N, p.C, a.vec_ok && a.contig[qc] != 0};
+  const int lay = a.contig[qc];
+  const int lst = a.vec_ok ? layout_stride(lay) : 0;
+  GatherCtx gc{sRow, sCh, p.N, p.C, lst == 1, lst > 1 ? lst : 0, layout_c0(lay)};
   // FWD item: [P_u | P_v | output row of each of the BM token rows (int32, -1: none)].
   unsigned char* out = a.packed + item * (FWD ? 2 * C::P_BYTES + BM * 4 : C::ITEM_BYTES);
   const uint32_t aStg = smem_u32(stg);
@@ -617,6 +699,8 @@ __global__ void __launch_bounds__(NCOMP) tc_pack_kernel(BwdArgs a) {
       rows_issue<TX, 1>(rx, gc, x, hf, a.rstd, nullptr, tid);
       if (!FWD) rows_issue<TO, 1>(rg, gc, dout, hf, nullptr, a.scale, tid);
       rows_store<TX, 1, BF16>(rx, 0, hf, gc, stg, false, a.rstd != nullptr, a.nw, nullptr, a.x_dt, tid);
+    } else if (gc.stride) {
+      gather_half_strided<TX, BF16>(gc, x, hf, a.rstd != nullptr, a.rstd, a.nw, a.x_dt, nullptr, stg, tid);
     } else {
       gather_half<TX, BF16>(gc, x, hf, a.rstd, a.nw, a.x_dt, nullptr, nullptr, stg, false, tid);
     }
@@ -639,6 +723,7 @@ __global__ void __launch_bounds__(NCOMP) tc_pack_kernel(BwdArgs a) {
     }
     if (FWD) continue;
     if (gc.cont) rows_store<TO, 1, BF16>(rg, 0, hf, gc, stg, false, false, nullptr, nullptr, 0, tid);
+    else if (gc.stride) gather_half_strided<TO, BF16>(gc, dout, hf, false, nullptr, nullptr, 0, a.scale, stg, tid);
     else gather_half<TO, BF16>(gc, dout, hf, nullptr, nullptr, 0, a.scale, nullptr, stg, false, tid);
     atoms_free();
     to_atom(atom0);
@@ -1219,10 +1304,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
         // Metadata of this item for the dX scatter.
         if (tid < BM) sRow[tid] = mreg.valid && mreg.tok < p.N ? mreg.b * p.N + mreg.tok : -1;
         if (tid < D) sCh[tid] = mreg.ch;
-        if (tid == 0) *sCont = a.vec_ok && mreg.cont != 0;
+        if (tid == 0) *sCont = a.vec_ok ? mreg.cont : 0;
         comp_sync();
         if (it + 1 < nit) mreg = meta_issue(it + 1);
-        const bool cont = *sCont != 0;
+        const int lay = *sCont;
+        const bool cont = layout_stride(lay) == 1;
+        const int sstride = layout_stride(lay) > 1 ? layout_stride(lay) : 0, sc0 = layout_c0(lay);
         mbar_wait(bar_b + ((c - 1) & 1), ((c - 1) >> 1) & 1, sAbort);  // last dP of the item done
         __syncwarp();
         tc_fence_after();
@@ -1270,7 +1357,38 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
                 mma16816<BF16>(cc[n4][nb], fvT, bv0, bv1);
               }
             }
-            if (cont) {
+            if (sstride) {
+              // Strided group (channels sc0 + S k): the half-tile goes through
+              // the staging tile too; 16 lanes then store 16 consecutive k of
+              // one row, which lie S elements apart in dX.
+#pragma unroll
+              for (int hr = 0; hr < 2; ++hr) {
+#pragma unroll
+                for (int n4 = 0; n4 < 4; ++n4)
+#pragma unroll
+                  for (int nb = 0; nb < 2; ++nb)
+                    *reinterpret_cast<float2*>(stg + g * C::D_ST_LD + n4 * 16 + nb * 8 + 2 * t4) =
+                        make_float2(cc[n4][nb][2 * hr], cc[n4][nb][2 * hr + 1]);
+                __syncwarp();
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  const int r8 = (i * 32 + lane) >> 4;
+                  const int rw = sRow[tile * 16 + hr * 8 + r8];
+                  if (rw >= 0) {
+                    const int64_t rowoff = (int64_t)rw * p.C + sc0 + (int64_t)sstride * hf * 64;
+#pragma unroll
+                    for (int m = 0; m < 4; ++m) {
+                      const int k = (lane & 15) + 16 * m;
+                      const float v = stg[r8 * C::D_ST_LD + k];
+                      const int64_t off = rowoff + (int64_t)sstride * k;
+                      if (a.dxn) a.dxn[off] = v;
+                      else ((TX*)a.dx)[off] = Elem<TX>::from(v);
+                    }
+                  }
+                }
+                __syncwarp();  // the staging tile is rewritten by the next half-tile
+              }
+            } else if (cont) {
 #pragma unroll
               for (int hr = 0; hr < 2; ++hr) {
 #pragma unroll
