@@ -196,6 +196,14 @@ def run_ours(args) -> None:
         torch.distributed.init_process_group("nccl", device_id=dev,
                                              timeout=datetime.timedelta(seconds=120))
     lib = _lib.load()
+    if args.model_only:
+        # Profiling aid: only the OmniWeave-T legs (no operator sweep).
+        m = _model_bench(args, dev, world, rank, lib)
+        if rank == 0:
+            print(json.dumps({"impl": "ours", "model_only": True, "omniweave_t": m}), flush=True)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
     names = ("x", "a_u", "a_v", "a_o", "b_u", "b_v", "b_o", "gamma")
 
     batch = args.batch
@@ -823,6 +831,7 @@ def main(argv=None) -> None:
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-graph", action="store_true", help="train step without CUDA-graph capture")
     ap.add_argument("--no-ref-gpu", action="store_true", help="skip timing the reference's own GPU paths")
+    ap.add_argument("--model-only", action="store_true", help="profiling aid: only the OmniWeave-T legs")
     args = ap.parse_args(argv)
     if args.impl == "reference":
         run_reference(args)

@@ -99,16 +99,16 @@ int fault_word(int** out);
 // Wait-timeout self-check setting (ow_debug_wait_probe); 0 when off.
 uint32_t wait_probe_ns();
 
-// RMSNorm backward of block mode from the f32 gradient w.r.t. the normalised
-// input (CUDA cores, row-wise).  norm_bwd_take() carves its partials from
+// RMSNorm backward of block mode from the gradient w.r.t. the normalised
+// input (``dxn``, f32 or the 16-bit compute type; CUDA cores, row-wise).  norm_bwd_take() carves its partials from
 // the workspace (also in a dry run); norm_bwd_run() launches it.
 struct NormBwd {
   float* part;
-  int grid, nwarps;
+  int grid, nwarps;  // blocks of the norm backward; partial rows it leaves for the column sum
 };
 NormBwd norm_bwd_take(int64_t rows, int C, Carver& ws);
 int norm_bwd_run(const NormBwd& nb, const void* x, int x_dt, const void* dout, int dout_dt, const float* rstd,
-                 const float* nw, const float* dxn, int64_t rows, int C, void* dx, void* dnorm_w, int w_dt,
+                 const float* nw, const void* dxn, int dxn_dt, int64_t rows, int C, void* dx, void* dnorm_w, int w_dt,
                  void* stream);
 int tc_backward(const ow_bigemm_args_t* a, const ow_bigemm_grads_t* gr, const Prob& p,
                 void* stream, Carver& ws);

@@ -333,6 +333,53 @@ __global__ void simt_sum_parts_kernel(const TC* __restrict__ part, int S, int64_
   }
 }
 
+// out[c] = sum_z part[z][c] for c < C: per-warp partials of the RMSNorm
+// weight gradient, S of them.  One 1024-thread block per 32 columns: warp w
+// sums rows w, w + 32, w + 64, ... in that order (eight loads in flight),
+// then warp 0 adds the 32 warp sums in order, so the result is bitwise
+// reproducible while 32 x ceil(C / 32) warps share the rows.
+template <typename TC, typename TW>
+__global__ void __launch_bounds__(1024) simt_col_sum_kernel(const TC* __restrict__ part, int S, int C,
+                                                            TW* __restrict__ out) {
+  __shared__ TC red[32][33];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + lane;
+  const int cc = c < C ? c : C - 1;  // clamped column: loads stay in bounds, result unused
+  TC acc = 0;
+  for (int z0 = w; z0 < S; z0 += 32 * 8) {
+    TC v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int z = z0 + 32 * k;
+      v[k] = part[(int64_t)(z < S ? z : S - 1) * C + cc];
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (z0 + 32 * k < S) acc += v[k];
+  }
+  red[w][lane] = acc;
+  __syncthreads();
+  if (w == 0) {
+    TC t = 0;
+    for (int k = 0; k < 32; ++k) t += red[k][lane];
+    if (c < C) out[c] = Elem<TW>::from(t);
+  }
+}
+
+template <typename TC>
+int launch_col_sum(const TC* part, int S, int C, void* out, int w_dt, cudaStream_t st) {
+  const int g = (C + 31) / 32;
+  switch (w_dt) {
+    case OW_DTYPE_F32: launch(simt_col_sum_kernel<TC, float>, g, 1024, 0, st, part, S, C, (float*)out); break;
+    case OW_DTYPE_F64: launch(simt_col_sum_kernel<TC, double>, g, 1024, 0, st, part, S, C, (double*)out); break;
+    case OW_DTYPE_BF16: launch(simt_col_sum_kernel<TC, __nv_bfloat16>, g, 1024, 0, st, part, S, C, (__nv_bfloat16*)out); break;
+    case OW_DTYPE_F16: launch(simt_col_sum_kernel<TC, __half>, g, 1024, 0, st, part, S, C, (__half*)out); break;
+    default: set_error("unsupported weight dtype"); return OW_ERR_UNSUPPORTED;
+  }
+  OW_CHECK_LAUNCH("norm weight reduction");
+  return OW_OK;
+}
+
 // dgamma[ch[q,k]] = sum over tiles of channel group q of dgg[t][k].
 template <typename TC, typename TW>
 __global__ void simt_dgamma_kernel(const TC* __restrict__ dgg, int64_t BQ, int Qc, int d,
@@ -353,16 +400,29 @@ __global__ void simt_dgamma_kernel(const TC* __restrict__ dgg, int64_t BQ, int Q
 // ---------------------------------------------------------------------------
 template <typename TX, typename TC>
 __global__ void rstd_kernel(const TX* __restrict__ x, int64_t rows, int C, double eps, int x_dt,
-                            TC* __restrict__ rstd) {
+                            TC* __restrict__ rstd, int vec) {
   const int lane = threadIdx.x & 31;
   int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  constexpr int EV = 16 / (int)sizeof(TX);  // elements per 16-byte vector
   for (; row < rows; row += nwarps) {
     const TX* xr = x + row * C;
     double acc = 0;
-    for (int c = lane; c < C; c += 32) {
-      float v = Elem<TX>::to_f(xr[c]);
-      acc += (double)(v * v);
+    if (vec) {  // 16-byte loads (C % EV == 0, row starts aligned)
+      for (int c = lane * EV; c < C; c += 32 * EV) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(xr + c));
+        const TX* e = reinterpret_cast<const TX*>(&u);
+#pragma unroll
+        for (int k = 0; k < EV; ++k) {
+          const float v = Elem<TX>::to_f(e[k]);
+          acc += (double)(v * v);
+        }
+      }
+    } else {
+      for (int c = lane; c < C; c += 32) {
+        float v = Elem<TX>::to_f(xr[c]);
+        acc += (double)(v * v);
+      }
     }
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     // mean in float32 (x.float().square().mean), cast to x's dtype, + eps, rsqrt
@@ -375,14 +435,21 @@ __global__ void rstd_kernel(const TX* __restrict__ x, int64_t rows, int C, doubl
 }
 
 // One warp per row; lane l owns channels l, l+32, ... (J per lane, C <= 32*J).
-// The norm-weight gradient is accumulated per warp and reduced afterwards in
-// a fixed order.
-template <typename TX, typename TO, typename TC, int J>
+// The norm-weight gradient is accumulated per warp; when the block's eight
+// warp sums fit 32 KB of shared memory they are added in warp order and the
+// block writes one partial row (COMBINE), else each warp writes its own.  The
+// partial rows are then summed in a fixed order (simt_col_sum_kernel), so the
+// result is bitwise reproducible.
+template <typename TC, int J>
+constexpr bool norm_combine() { return 8 * 32 * J * sizeof(TC) <= 32768; }
+
+template <typename TX, typename TO, typename TC, typename TD, int J>
 __global__ void __launch_bounds__(256)
 norm_bwd_kernel(const TX* __restrict__ x, const TC* __restrict__ rstd, const TC* __restrict__ nw,
-                const TC* __restrict__ dxn, const TO* __restrict__ dout, int64_t rows, int C,
+                const TD* __restrict__ dxn, const TO* __restrict__ dout, int64_t rows, int C,
                 TX* __restrict__ dx, TC* __restrict__ dw_part) {
-  const int lane = threadIdx.x & 31;
+  constexpr bool COMBINE = norm_combine<TC, J>();
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   const int64_t gw = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   TC acc[J];
@@ -391,13 +458,14 @@ norm_bwd_kernel(const TX* __restrict__ x, const TC* __restrict__ rstd, const TC*
   for (int64_t row = gw; row < rows; row += nwarps) {
     const int64_t base = row * C;
     const TC r = rstd[row];
-    TC xv[J], gn[J];
+    TC xv[J], gn[J], dv[J];
     TC inner = 0;
 #pragma unroll
     for (int j = 0; j < J; ++j) {
       int c = lane + 32 * j;
       xv[j] = c < C ? load_as<TC>(x, base + c) : TC(0);
-      gn[j] = c < C ? dxn[base + c] : TC(0);
+      gn[j] = c < C ? load_as<TC>(dxn, base + c) : TC(0);
+      dv[j] = c < C ? load_as<TC>(dout, base + c) : TC(0);  // requested before the reduction
       inner += c < C ? gn[j] * nw[c] * xv[j] : TC(0);
     }
     for (int o = 16; o > 0; o >>= 1) inner += __shfl_xor_sync(0xffffffffu, inner, o);
@@ -406,27 +474,60 @@ norm_bwd_kernel(const TX* __restrict__ x, const TC* __restrict__ rstd, const TC*
     for (int j = 0; j < J; ++j) {
       int c = lane + 32 * j;
       if (c < C) {
-        TC v = load_as<TC>(dout, base + c) + r * nw[c] * gn[j] - xv[j] * coef;
+        TC v = dv[j] + r * nw[c] * gn[j] - xv[j] * coef;
         dx[base + c] = Elem<TX>::from(v);
         acc[j] += gn[j] * xv[j] * r;
       }
     }
   }
+  if constexpr (COMBINE) {
+    __shared__ TC red[8][32 * J];
 #pragma unroll
-  for (int j = 0; j < J; ++j) {
-    int c = lane + 32 * j;
-    if (c < C) dw_part[gw * C + c] = acc[j];
+    for (int j = 0; j < J; ++j) red[wib][lane + 32 * j] = acc[j];
+    __syncthreads();
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+      TC t = 0;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) t += red[k][c];
+      dw_part[(int64_t)blockIdx.x * C + c] = t;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      int c = lane + 32 * j;
+      if (c < C) dw_part[gw * C + c] = acc[j];
+    }
   }
 }
 
-template <typename TX, typename TO, typename TC>
+// Number of partial rows launch_norm_bwd leaves for the column sum.
+template <typename TC>
+int norm_parts(int grid, int C) {
+  bool comb;
+  if (C <= 128) comb = norm_combine<TC, 4>();
+  else if (C <= 256) comb = norm_combine<TC, 8>();
+  else if (C <= 512) comb = norm_combine<TC, 16>();
+  else if (C <= 1024) comb = norm_combine<TC, 32>();
+  else comb = norm_combine<TC, 64>();
+  return comb ? grid : grid * 8;
+}
+
+// Blocks of the norm backward: one warp per row, enough blocks to fill the
+// GPU several times over, while the partials (8 warps x C per block) stay
+// under 16 MB.
+inline int norm_grid_for(int64_t rows, int C) {
+  const int64_t cap = std::max<int64_t>(296, std::min<int64_t>(1184, (int64_t)(1 << 19) / C));
+  return (int)std::max<int64_t>(1, std::min<int64_t>((rows + 63) / 64, cap));
+}
+
+template <typename TX, typename TO, typename TC, typename TD>
 int launch_norm_bwd(int grid, cudaStream_t st, const TX* x, const TC* rstd, const TC* nw,
-                    const TC* dxn, const TO* dout, int64_t rows, int C, TX* dx, TC* dw_part) {
-  if (C <= 128) launch(norm_bwd_kernel<TX, TO, TC, 4>, grid, 256, 0, st, x, rstd, nw, dxn, dout, rows, C, dx, dw_part);
-  else if (C <= 256) launch(norm_bwd_kernel<TX, TO, TC, 8>, grid, 256, 0, st, x, rstd, nw, dxn, dout, rows, C, dx, dw_part);
-  else if (C <= 512) launch(norm_bwd_kernel<TX, TO, TC, 16>, grid, 256, 0, st, x, rstd, nw, dxn, dout, rows, C, dx, dw_part);
-  else if (C <= 1024) launch(norm_bwd_kernel<TX, TO, TC, 32>, grid, 256, 0, st, x, rstd, nw, dxn, dout, rows, C, dx, dw_part);
-  else if (C <= 2048) launch(norm_bwd_kernel<TX, TO, TC, 64>, grid, 256, 0, st, x, rstd, nw, dxn, dout, rows, C, dx, dw_part);
+                    const TD* dxn, const TO* dout, int64_t rows, int C, TX* dx, TC* dw_part) {
+  if (C <= 128) launch(norm_bwd_kernel<TX, TO, TC, TD, 4>, grid, 256, 0, st, x, rstd, nw, dxn, dout, rows, C, dx, dw_part);
+  else if (C <= 256) launch(norm_bwd_kernel<TX, TO, TC, TD, 8>, grid, 256, 0, st, x, rstd, nw, dxn, dout, rows, C, dx, dw_part);
+  else if (C <= 512) launch(norm_bwd_kernel<TX, TO, TC, TD, 16>, grid, 256, 0, st, x, rstd, nw, dxn, dout, rows, C, dx, dw_part);
+  else if (C <= 1024) launch(norm_bwd_kernel<TX, TO, TC, TD, 32>, grid, 256, 0, st, x, rstd, nw, dxn, dout, rows, C, dx, dw_part);
+  else if (C <= 2048) launch(norm_bwd_kernel<TX, TO, TC, TD, 64>, grid, 256, 0, st, x, rstd, nw, dxn, dout, rows, C, dx, dw_part);
   else {
     set_error("block mode supports at most 2048 channels (got %d)", C);
     return OW_ERR_UNSUPPORTED;
@@ -605,9 +706,9 @@ int simt_backward_t(const ow_bigemm_args_t* a, const ow_bigemm_grads_t* gr, cons
   TC* dw_part = nullptr;
   int norm_grid = 0;
   if (block) {
-    norm_grid = (int)std::min<int64_t>((rows + 63) / 64, 296);
-    nw_warps = norm_grid * 8;
-    dw_part = (TC*)ws.take((size_t)nw_warps * p.C * sizeof(TC));
+    norm_grid = norm_grid_for(rows, p.C);
+    nw_warps = norm_parts<TC>(norm_grid, p.C);
+    dw_part = (TC*)ws.take((size_t)norm_grid * 8 * p.C * sizeof(TC));
   }
   if (!ws.base) return OW_OK;
 
@@ -621,7 +722,7 @@ int simt_backward_t(const ow_bigemm_args_t* a, const ow_bigemm_grads_t* gr, cons
         a->sample_scale, (const TO*)gr->dout, dxn, block ? nullptr : (TX*)gr->dx, s);
     OW_CHECK_LAUNCH("simt_bwd_tile_kernel");
     if (block)
-      return launch_norm_bwd<TX, TO, TC>(norm_grid, st, (const TX*)a->x, (const TC*)a->rstd,
+      return launch_norm_bwd<TX, TO, TC, TC>(norm_grid, st, (const TX*)a->x, (const TC*)a->rstd,
                                          w + wo.nw, dxn, (const TO*)gr->dout, rows, p.C,
                                          (TX*)gr->dx, dw_part);
     return OW_OK;
@@ -636,17 +737,7 @@ int simt_backward_t(const ow_bigemm_args_t* a, const ow_bigemm_grads_t* gr, cons
     case OW_DTYPE_F16: launch(simt_dgamma_kernel<TC, __half>, gsz, 128, 0, st, s.dgg, BQ, p.Qc, d, p.ch, p.C, (__half*)gr->dgamma); break;
   }
   OW_CHECK_LAUNCH("simt_dgamma_kernel");
-  if (block) {
-    int64_t C = p.C;
-    int gs = grid_for(C);
-    switch (a->w_dtype) {
-      case OW_DTYPE_F32: launch(simt_sum_parts_kernel<TC, float>, gs, 256, 0, st, dw_part, nw_warps, C, 1, (float*)gr->dnorm_w); break;
-      case OW_DTYPE_F64: launch(simt_sum_parts_kernel<TC, double>, gs, 256, 0, st, dw_part, nw_warps, C, 1, (double*)gr->dnorm_w); break;
-      case OW_DTYPE_BF16: launch(simt_sum_parts_kernel<TC, __nv_bfloat16>, gs, 256, 0, st, dw_part, nw_warps, C, 1, (__nv_bfloat16*)gr->dnorm_w); break;
-      case OW_DTYPE_F16: launch(simt_sum_parts_kernel<TC, __half>, gs, 256, 0, st, dw_part, nw_warps, C, 1, (__half*)gr->dnorm_w); break;
-    }
-    OW_CHECK_LAUNCH("norm weight reduction");
-  }
+  if (block) return launch_col_sum<TC>(dw_part, nw_warps, p.C, gr->dnorm_w, a->w_dtype, st);
   return OW_OK;
 }
 
@@ -667,51 +758,56 @@ int simt_backward(const ow_bigemm_args_t* a, const ow_bigemm_grads_t* gr, const 
 
 NormBwd norm_bwd_take(int64_t rows, int C, Carver& ws) {
   NormBwd nb;
-  nb.grid = (int)std::min<int64_t>((rows + 63) / 64, 296);
-  nb.nwarps = nb.grid * 8;
-  nb.part = (float*)ws.take((size_t)nb.nwarps * C * sizeof(float));
+  nb.grid = norm_grid_for(rows, C);
+  nb.nwarps = norm_parts<float>(nb.grid, C);
+  nb.part = (float*)ws.take((size_t)nb.grid * 8 * C * sizeof(float));
   return nb;
 }
 
 int norm_bwd_run(const NormBwd& nb, const void* x, int x_dt, const void* dout, int dout_dt, const float* rstd,
-                 const float* nw, const float* dxn, int64_t rows, int C, void* dx, void* dnorm_w, int w_dt,
-                 void* stream) {
+                 const float* nw, const void* dxn, int dxn_dt, int64_t rows, int C, void* dx, void* dnorm_w,
+                 int w_dt, void* stream) {
   cudaStream_t st = (cudaStream_t)stream;
   auto run = [&](auto* tx, auto* to) -> int {
     using TX = std::remove_pointer_t<decltype(tx)>;
     using TO = std::remove_pointer_t<decltype(to)>;
-    return launch_norm_bwd<TX, TO, float>(nb.grid, st, (const TX*)x, rstd, nw, dxn, (const TO*)dout, rows, C,
-                                          (TX*)dx, nb.part);
+    switch (dxn_dt) {
+      case OW_DTYPE_F32:
+        return launch_norm_bwd<TX, TO, float, float>(nb.grid, st, (const TX*)x, rstd, nw, (const float*)dxn,
+                                                     (const TO*)dout, rows, C, (TX*)dx, nb.part);
+      case OW_DTYPE_BF16:
+        return launch_norm_bwd<TX, TO, float, __nv_bfloat16>(nb.grid, st, (const TX*)x, rstd, nw,
+                                                             (const __nv_bfloat16*)dxn, (const TO*)dout, rows, C,
+                                                             (TX*)dx, nb.part);
+      case OW_DTYPE_F16:
+        return launch_norm_bwd<TX, TO, float, __half>(nb.grid, st, (const TX*)x, rstd, nw, (const __half*)dxn,
+                                                      (const TO*)dout, rows, C, (TX*)dx, nb.part);
+      default:
+        set_error("norm backward: unsupported gradient dtype %s", dtype_name(dxn_dt));
+        return OW_ERR_UNSUPPORTED;
+    }
   };
   int rc = dispatch_io<float>(x_dt, dout_dt, run);
   OW_RETURN_IF(rc);
-  const int gs = grid_for(C);
-  switch (w_dt) {
-    case OW_DTYPE_F32: launch(simt_sum_parts_kernel<float, float>, gs, 256, 0, st, (const float*)nb.part, nb.nwarps, (int64_t)C, 1, (float*)dnorm_w); break;
-    case OW_DTYPE_F64: launch(simt_sum_parts_kernel<float, double>, gs, 256, 0, st, (const float*)nb.part, nb.nwarps, (int64_t)C, 1, (double*)dnorm_w); break;
-    case OW_DTYPE_BF16: launch(simt_sum_parts_kernel<float, __nv_bfloat16>, gs, 256, 0, st, (const float*)nb.part, nb.nwarps, (int64_t)C, 1, (__nv_bfloat16*)dnorm_w); break;
-    case OW_DTYPE_F16: launch(simt_sum_parts_kernel<float, __half>, gs, 256, 0, st, (const float*)nb.part, nb.nwarps, (int64_t)C, 1, (__half*)dnorm_w); break;
-    default: set_error("unsupported weight dtype"); return OW_ERR_UNSUPPORTED;
-  }
-  OW_CHECK_LAUNCH("norm weight reduction");
-  return OW_OK;
+  return launch_col_sum<float>(nb.part, nb.nwarps, C, dnorm_w, w_dt, st);
 }
 
 int rmsnorm_rstd(const void* x, int x_dtype, int compute_dtype, int64_t rows, int C, double eps,
                  void* rstd, void* stream) {
   cudaStream_t st = (cudaStream_t)stream;
   int grid = grid_for(rows * 32, 256, 148 * 16);
+  const int vec = ((uintptr_t)x % 16 == 0) && (C * (int)dtype_size(x_dtype) % 16 == 0);
   if (compute_dtype == OW_DTYPE_F64) {
     if (x_dtype != OW_DTYPE_F64) {
       set_error("rmsnorm: float64 compute needs float64 input");
       return OW_ERR_UNSUPPORTED;
     }
-    launch(rstd_kernel<double, double>, grid, 256, 0, st, (const double*)x, rows, C, eps, x_dtype, (double*)rstd);
+    launch(rstd_kernel<double, double>, grid, 256, 0, st, (const double*)x, rows, C, eps, x_dtype, (double*)rstd, vec);
   } else {
     switch (x_dtype) {
-      case OW_DTYPE_F32: launch(rstd_kernel<float, float>, grid, 256, 0, st, (const float*)x, rows, C, eps, x_dtype, (float*)rstd); break;
-      case OW_DTYPE_BF16: launch(rstd_kernel<__nv_bfloat16, float>, grid, 256, 0, st, (const __nv_bfloat16*)x, rows, C, eps, x_dtype, (float*)rstd); break;
-      case OW_DTYPE_F16: launch(rstd_kernel<__half, float>, grid, 256, 0, st, (const __half*)x, rows, C, eps, x_dtype, (float*)rstd); break;
+      case OW_DTYPE_F32: launch(rstd_kernel<float, float>, grid, 256, 0, st, (const float*)x, rows, C, eps, x_dtype, (float*)rstd, vec); break;
+      case OW_DTYPE_BF16: launch(rstd_kernel<__nv_bfloat16, float>, grid, 256, 0, st, (const __nv_bfloat16*)x, rows, C, eps, x_dtype, (float*)rstd, vec); break;
+      case OW_DTYPE_F16: launch(rstd_kernel<__half, float>, grid, 256, 0, st, (const __half*)x, rows, C, eps, x_dtype, (float*)rstd, vec); break;
       default:
         set_error("rmsnorm: unsupported input dtype %s", dtype_name(x_dtype));
         return OW_ERR_UNSUPPORTED;

@@ -204,7 +204,7 @@ struct BPlan {
     puv = take((size_t)nH * p.Qc * nUVq * 2 * 128 * D * 4);
     po = take((size_t)p.Qc * nOq * C::RD * D * 4);
     mo = take((size_t)p.Qc * C::RD * D * 4);
-    dxn = block ? take((size_t)p.B * p.N * p.C * 4) : 0;
+    dxn = block ? take((size_t)p.B * p.N * p.C * 2) : 0;  // 16-bit compute type
     packed = take((size_t)p.Qc * nMB * C::ITEM_BYTES);
     total = o;
   }
@@ -607,7 +607,7 @@ struct BwdArgs {
   int vec_ok;
   unsigned char* packed;  // [items][5][BM x D] SW128 operand images
   void* dx;       // operator mode: x dtype
-  float* dxn;     // block mode
+  void* dxn;      // block mode: gradient w.r.t. the normalised input, 16-bit compute type
   float* pdA;     // [nD][8][2][256]
   float* pdAo;    // [Qc*nOq][8][256]
   float* puv;     // [nH*Qc*nUVq][2][128][D]
@@ -752,6 +752,7 @@ __global__ void __launch_bounds__(NCOMP) tc_pack_kernel(BwdArgs a) {
 template <int D, bool BF16, typename TX, typename TO>
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
   using C = BCfg<D>;
+  using T16 = std::conditional_t<BF16, __nv_bfloat16, __half>;
   constexpr int SC = C::SC;
   constexpr int HC = SC / 2;            // columns of a sub-chunk per compute thread
   constexpr bool HALVES = SC == 32;     // two buffers share one 64-column atom
@@ -1381,7 +1382,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
                       const int k = (lane & 15) + 16 * m;
                       const float v = stg[r8 * C::D_ST_LD + k];
                       const int64_t off = rowoff + (int64_t)sstride * k;
-                      if (a.dxn) a.dxn[off] = v;
+                      if (a.dxn) reinterpret_cast<T16*>(a.dxn)[off] = Elem<T16>::from(v);
                       else ((TX*)a.dx)[off] = Elem<TX>::from(v);
                     }
                   }
@@ -1405,9 +1406,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
                   const int rw = sRow[tile * 16 + hr * 8 + r8];
                   if (rw >= 0) {
                     const int64_t off = (int64_t)rw * p.C + sCh[0] + hf * 64 + c4;
-                    if (a.dxn || std::is_same_v<TX, float>) {
-                      float* dst = a.dxn ? a.dxn + off : (float*)a.dx + off;
-                      *reinterpret_cast<float4*>(dst) = v;
+                    if (a.dxn) {
+                      *reinterpret_cast<uint2*>(reinterpret_cast<T16*>(a.dxn) + off) =
+                          make_uint2(pack2<BF16>(v.x, v.y), pack2<BF16>(v.z, v.w));
+                    } else if constexpr (std::is_same_v<TX, float>) {
+                      *reinterpret_cast<float4*>((float*)a.dx + off) = v;
                     } else {
                       constexpr bool XB = std::is_same_v<TX, __nv_bfloat16>;
                       *reinterpret_cast<uint2*>((TX*)a.dx + off) = make_uint2(pack2<XB>(v.x, v.y), pack2<XB>(v.z, v.w));
@@ -1433,7 +1436,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
                       if (ch >= p.C) continue;
                       const int64_t off = row * p.C + ch;
                       const float dv = cc[n4][nb][2 * hr + e];
-                      if (a.dxn) a.dxn[off] = dv;
+                      if (a.dxn) reinterpret_cast<T16*>(a.dxn)[off] = Elem<T16>::from(dv);
                       else ((TX*)a.dx)[off] = Elem<TX>::from(dv);
                     }
                   }
@@ -1736,7 +1739,7 @@ int tc_backward_t(const ow_bigemm_args_t* ar, const ow_bigemm_grads_t* gr, const
   a.vec_ok = ((uintptr_t)ar->x % 16 == 0) && ((uintptr_t)gr->dout % 16 == 0) && ((uintptr_t)gr->dx % 16 == 0) &&
              (p.C % 8 == 0);
   a.dx = block ? nullptr : gr->dx;
-  a.dxn = block ? (float*)(base + pl.dxn) : nullptr;
+  a.dxn = block ? (void*)(base + pl.dxn) : nullptr;
   a.pdA = (float*)(base + pl.pdA);
   a.pdAo = (float*)(base + pl.pdAo);
   a.puv = (float*)(base + pl.puv);
@@ -1831,7 +1834,8 @@ int tc_backward_t(const ow_bigemm_args_t* ar, const ow_bigemm_grads_t* gr, const
   OW_CHECK_LAUNCH("tc_bwd_reduce_kernel");
   if (block)
     return norm_bwd_run(nbw, ar->x, ar->x_dtype, gr->dout, ar->out_dtype, (const float*)ar->rstd,
-                        (const float*)(base + pl.nw), a.dxn, (int64_t)p.B * p.N, p.C, gr->dx, gr->dnorm_w,
+                        (const float*)(base + pl.nw), a.dxn, BF16 ? OW_DTYPE_BF16 : OW_DTYPE_F16,
+                        (int64_t)p.B * p.N, p.C, gr->dx, gr->dnorm_w,
                         ar->w_dtype, st);
   return OW_OK;
 }
