@@ -82,8 +82,10 @@ def _kernel_flops(name: str, b: int, h: int, w: int, c: int, d: int) -> float:
     mixes = tiles * 3 * 2 * G * G * d
     if name == "tc_pack_fwd_kernel":
         return float(tiles * 4 * G * G * d)
-    if name == "tc_fwd_kernel":
+    if name == "tc_fwd_kernel":  # its pre-pass did the input token mixes (strided channel groups)
         return fwd_flops(b, h, w, c, d) - tiles * 4 * G * G * d
+    if name == "tc_fwd_gather_kernel":  # the TMA-gather forward does the whole forward
+        return fwd_flops(b, h, w, c, d)
     if name == "tc_pack_kernel":
         return float(mixes)
     return 2.0 * fwd_flops(b, h, w, c, d) - mixes
@@ -287,8 +289,10 @@ def run_ours(args) -> None:
     per, kern = {}, {}
     for i, cs in enumerate(cases):
         per[(cs["shape"], cs["route"])] = (mean_ms(i, 0, 1), mean_ms(i, 1, 2))
-        kern[(cs["shape"], cs["route"])] = {"tc_pack_fwd_kernel": mean_ms(i, 9, 10),
-                                            "tc_fwd_kernel": mean_ms(i, 3, 4), "tc_pack_kernel": mean_ms(i, 5, 6),
+        pre = mean_ms(i, 9, 10)
+        fwd_name = "tc_fwd_kernel" if pre > 1e-3 else "tc_fwd_gather_kernel"
+        kern[(cs["shape"], cs["route"])] = {"tc_pack_fwd_kernel": pre,
+                                            fwd_name: mean_ms(i, 3, 4), "tc_pack_kernel": mean_ms(i, 5, 6),
                                             "tc_bwd_kernel": mean_ms(i, 7, 8)}
     # Dominant kernel: the single launch with the largest device time.
     dom_key, dom_name, dom_ms = max(((k, n, t) for k, v in kern.items() for n, t in v.items()),

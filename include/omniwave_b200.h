@@ -42,7 +42,7 @@
 extern "C" {
 #endif
 
-#define OW_ABI_VERSION 1
+#define OW_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define OW_API __attribute__((visibility("default")))
@@ -82,6 +82,15 @@ typedef struct ow_route_t {
   int32_t g, d, rd;                       /* tile tokens (16), channel tile, expanded tile */
   const int32_t* tok_idx;                 /* [q_s * g] */
   const int32_t* ch_idx;                  /* [q_c * d] */
+  /* Channel-layout hint: 0 = unknown (any table); S >= 1 = the caller
+   * states that channel group q is ch_idx[q*d + k] = c0(q) + S*k for every
+   * k (S == 1: one run of d consecutive channels starting on a multiple of 8;
+   * the radix routes at levels 1 and 2 give S = q_c).  The hint only selects
+   * a kernel: with S == 1 the forward gathers the group's rows with TMA
+   * straight from x.  The kernels verify it against the table; a group that
+   * does not match is not computed and the device fault word reports code 2
+   * (ow_device_fault). */
+  int32_t ch_stride;
 } ow_route_t;
 
 /*
@@ -170,7 +179,8 @@ OW_API int ow_device_supported(int device);
 /*
  * Fault word of this library's kernels on ``device``: 0 when no kernel ever
  * gave up on a bounded wait (every wait on the GPU is bounded at 2 s), else a
- * nonzero code (1: a wait ran out; the outputs of that call are undefined).
+ * nonzero code (1: a wait ran out; 2: a channel group did not match the
+ * route's ch_stride hint; the outputs of that call are undefined).
  * One word per device is shared by every kernel of the library.  Calls are
  * asynchronous, so a fault surfaces here, not in the failing call's status:
  * this function synchronises the device first.  ``reset`` != 0 clears the

@@ -16,7 +16,7 @@ import torch
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_PKG, "libomniwave_b200.so")
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 DTYPE_CODE = {
     torch.float32: 0,
@@ -36,7 +36,7 @@ class Route(ctypes.Structure):
     _fields_ = [
         ("batch", _c_i32), ("height", _c_i32), ("width", _c_i32), ("channels", _c_i32),
         ("q_s", _c_i32), ("q_c", _c_i32), ("g", _c_i32), ("d", _c_i32), ("rd", _c_i32),
-        ("tok_idx", _vp), ("ch_idx", _vp),
+        ("tok_idx", _vp), ("ch_idx", _vp), ("ch_stride", _c_i32),
     ]
 
 

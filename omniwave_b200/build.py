@@ -79,7 +79,7 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
     with cf.ThreadPoolExecutor(max_workers=min(8, max(1, len(jobs)))) as ex:
         list(ex.map(run, jobs))
     if force or jobs or _stale(LIB, objects):
-        cmd = [nvcc, *ARCH, "-shared", "-o", LIB, *objects, "-lcudart", "-lcuda"]
+        cmd = [nvcc, *ARCH, "-shared", "-o", LIB, *objects, "-lcudart"]
         run(cmd)
     return LIB
 

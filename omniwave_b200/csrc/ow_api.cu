@@ -91,6 +91,7 @@ static int make_prob(const ow_bigemm_args_t* a, Prob* p, bool need_ptrs) {
                (r.channels + r.d - 1) / r.d);
   OW_CHECK_ARG(valid_dtype(a->x_dtype) && valid_dtype(a->w_dtype) && valid_dtype(a->compute_dtype),
                "invalid dtype code (x=%d w=%d compute=%d)", a->x_dtype, a->w_dtype, a->compute_dtype);
+  OW_CHECK_ARG(r.ch_stride >= 0, "ch_stride hint must be >= 0 (got %d)", r.ch_stride);
   const int64_t tiles = (int64_t)r.batch * r.q_s;
   OW_CHECK_ARG(tiles < (1LL << 31) - 1 && r.q_c < 65535, "grid too large (B*q_s=%lld, q_c=%d)",
                (long long)tiles, r.q_c);
@@ -103,6 +104,7 @@ static int make_prob(const ow_bigemm_args_t* a, Prob* p, bool need_ptrs) {
   p->B = r.batch; p->H = r.height; p->W = r.width; p->C = r.channels; p->N = (int)n;
   p->Qs = r.q_s; p->Qc = r.q_c; p->g = r.g; p->d = r.d; p->rd = r.rd;
   p->tok = r.tok_idx; p->ch = r.ch_idx;
+  p->chs = r.ch_stride;
   return OW_OK;
 }
 

@@ -15,6 +15,7 @@ struct Prob {
   int Qs, Qc, g, d, rd;
   const int32_t* tok;  // [Qs*g]
   const int32_t* ch;   // [Qc*d]
+  int chs;             // channel-layout hint of the route (ow_route_t.ch_stride)
 #ifdef __CUDACC__
   __host__ __device__
 #endif
@@ -87,6 +88,13 @@ int rmsnorm_rstd(const void* x, int x_dtype, int compute_dtype, int64_t rows, in
 
 // Tensor-core path (bf16/f16 compute, g=16, d in {64,128}, rd=2d).
 bool tc_supported(const ow_bigemm_args_t* a, const Prob& p, const char** why);
+// Forward with TMA row gathers and tensor-core token mixes (ow_tcf.cu): true
+// when it covers this call (contiguous channel groups, 16-bit x, operator
+// mode); tcf_forward() then runs it with the weight images the forward prep
+// kernel wrote (``img``, ``amat``, ``gg``, ``layout``).
+bool tcf_covers(const ow_bigemm_args_t* a, const Prob& p);
+int tcf_forward(const ow_bigemm_args_t* a, const Prob& p, const unsigned char* img, const uint16_t* amat,
+                const float* gg, const int* layout, void* stream);
 int tc_forward(const ow_bigemm_args_t* a, const Prob& p, void* stream, Carver& ws);
 // The forward's pre-pass: [P_u | P_v] operand images per item (ow_tc_bwd.cu).
 int tc_pack_forward(const ow_bigemm_args_t* a, const Prob& p, const uint16_t* amat, const float* nwc,

@@ -94,7 +94,9 @@ struct Cfg {
 template <int D>
 struct TcWs {
   size_t img, amat, gg, nwc, contig, packed, total;
-  TcWs(const Prob& p) {
+  // ``gather``: the call runs the TMA-gather forward (ow_tcf.cu), which
+  // needs no packed operand images.
+  TcWs(const Prob& p, bool gather) {
     size_t o = 0;
     auto take = [&](size_t n) { size_t r = o; o = (o + n + 255) / 256 * 256; return r; };
     img = take((size_t)p.Qc * Cfg<D>::NQ * Cfg<D>::IMG_BYTES);
@@ -102,7 +104,7 @@ struct TcWs {
     gg = take((size_t)p.Qc * D * 4);
     nwc = take((size_t)p.C * 4);
     contig = take((size_t)p.Qc * 4);
-    packed = take((size_t)p.Qc * ((p.BQ() + 7) / 8) * Cfg<D>::PK_BYTES);
+    packed = gather ? 0 : take((size_t)p.Qc * ((p.BQ() + 7) / 8) * Cfg<D>::PK_BYTES);
     total = o;
   }
 };
@@ -698,12 +700,20 @@ int tc_prep(const ow_bigemm_args_t* a, const Prob& p, const TcWs<D>& w, unsigned
 
 template <int D, bool BF16>
 int tc_forward_t(const ow_bigemm_args_t* a, const Prob& p, cudaStream_t st, Carver& ws) {
-  TcWs<D> w(p);
+  const bool gather = tcf_covers(a, p);
+  TcWs<D> w(p, gather);
   unsigned char* base = (unsigned char*)ws.take(w.total);
   if (!ws.base) return OW_OK;
   int* fault = nullptr;
   OW_RETURN_IF(fault_word(&fault));
   OW_RETURN_IF((tc_prep<D, BF16>(a, p, w, base, st)));
+  if (gather) {
+    // No pre-pass: its profiling events (if set) bracket nothing.
+    profile_mark(OW_PROF_FPACK, false, st);
+    profile_mark(OW_PROF_FPACK, true, st);
+    return tcf_forward(a, p, base + w.img, (const uint16_t*)(base + w.amat), (const float*)(base + w.gg),
+                       (const int*)(base + w.contig), st);
+  }
   profile_mark(OW_PROF_FPACK, false, st);
   OW_RETURN_IF((tc_pack_forward(a, p, (const uint16_t*)(base + w.amat), (const float*)(base + w.nwc),
                                 (const int*)(base + w.contig), base + w.packed, st)));

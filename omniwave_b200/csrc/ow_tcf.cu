@@ -1,0 +1,714 @@
+// Tensor-core BiGEMM forward with TMA row gathers and tcgen05 token mixes
+// (sm_100a; bf16/f16 compute; g = 16, d in {64, 128}, rd = 2d; channel
+// groups that are runs of d consecutive channels; operator mode).
+//
+// Work unit ("item"): one channel group q and an M-block of 128 token rows
+// (8 tiles of 16).  Per item (reference.py:147-171, with pack_tiles folded
+// into the loads and unpack_tiles into the stores):
+//
+//   T     = x[rows, q d : q d + d]                  TMA tile::gather4 from x itself (pad rows read the
+//                                                   out-of-range fill, 0): no tile is materialised in HBM
+//   P^T_t = T_t^T [A_u^T | A_v^T]   per tile t      tcgen05.mma, M = channels, N = 32, K = 16 tokens
+//   P_u, P_v -> shared memory                       compute warps (MN-major A operands: lanes = channels)
+//   U_c = P_u B_u[:, c],  V_c = P_v B_v[:, c]       tcgen05.mma per 64-feature chunk c, f32 in TMEM
+//   Z_c = silu(U_c) V_c                             compute warps
+//   Y  += Z_c B_o[c, :]                             tcgen05.mma
+//   Y -> shared memory;  Delta^T_t = Y_t^T A_o^T    tcgen05.mma, M = channels, N = 16
+//   out[row, q d + c] = Delta[row, c] gamma[c] s_b  compute warps, lanes = consecutive channels
+//
+// The 16x16 token mixes run on the tensor cores in transposed form: the
+// channels fill the M = 128 rows of the MMA, a tile's 16 tokens are K.  At
+// d = 64 a mix pairs two tiles to fill M = 128: the T (and Y) images hold
+// tile 2j's rows in the first 64-channel atom and tile 2j+1's in the second,
+// each beside 16 zero lines, so two K = 16 steps compute both tiles' mixes
+// (rows 0-63: tile 2j, rows 64-127: tile 2j+1).
+//
+// Roles (320 threads): warps 0-7 compute, warp 8 issues every tcgen05.mma
+// (one thread) and owns the TMEM allocation, warp 9 issues the TMA gathers
+// (all lanes) and the weight copies.  The grid is persistent (one CTA per SM)
+// and walks items channel-group-major, so neighbouring CTAs share a group's
+// weight images through L2.  Every wait is bounded (ow_sm100.cuh).
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+#include <type_traits>
+
+#include "ow_common.cuh"
+#include "ow_internal.h"
+#include "ow_sm100.cuh"
+
+namespace ow {
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128;                 // token rows per item (8 tiles of 16)
+constexpr int NC = 64;                  // rd chunk width
+constexpr int NCW = 8;                  // compute warps
+constexpr int NCT = NCW * 32;
+constexpr int MMA_W = NCW;
+constexpr int PROD_W = NCW + 1;          // TMA row gathers
+constexpr int WGT_W = NCW + 2;           // weight copies
+constexpr int THREADS = (NCW + 3) * 32;
+constexpr int TMEM_COLS = 512;
+constexpr int ATOM = BM * 128;          // 64 channels x 128 lines, 128-byte swizzled (16 KB)
+constexpr int kFaultLayout = 2;         // fault code: a group is not a run of d channels
+
+template <int D>
+struct FC {
+  static constexpr int RD = 2 * D;
+  static constexpr int NQ = RD / NC;             // 64-feature chunks per item
+  static constexpr bool PAIR = D == 64;          // token mixes pair two tiles
+  static constexpr int NBLK = PAIR ? 4 : 8;      // column blocks of a token mix in TMEM
+  static constexpr int T_BYTES = 2 * ATOM;       // T image (d=128: channel halves; d=64: tile parities)
+  static constexpr int PI_ATOM = D * 128;        // P image: one 64-token atom of D channel lines
+  static constexpr int PI_BYTES = 2 * PI_ATOM;   // P image: 128 tokens
+  static constexpr int Z_BYTES = BM * NC * 2;    // one Z chunk (K-major, 128 x 64)
+  static constexpr int Y_BYTES = 2 * ATOM;       // Y image (same arrangement as the T image)
+  static constexpr int BU_BYTES = NC * D * 2;    // one of B_u / B_v of a chunk image
+  static constexpr int WUV_BYTES = 2 * BU_BYTES;
+  static constexpr int WO_BYTES = D * NC * 2;
+  static constexpr int IMG_BYTES = WUV_BYTES + WO_BYTES;  // chunk image [B_u | B_v | B_o] (prep kernel)
+  // Shared memory.  d = 64: T, P images, Z, Y image and the resident weights
+  // of one channel group each have their own region (the T and Y images
+  // keep their zero lines).  d = 128: the Y image overwrites the Z buffers
+  // once the last Y MMA has read them, and the weights stream per chunk,
+  // [B_u | B_v] through two stages and B_o through one.
+  static constexpr int OFF_T = 0;
+  static constexpr int OFF_PU = T_BYTES;
+  static constexpr int OFF_PV = OFF_PU + PI_BYTES;
+  static constexpr int R_END = OFF_PV + PI_BYTES;
+  static constexpr int OFF_Z = R_END;
+  static constexpr int OFF_Y = PAIR ? OFF_Z + 2 * Z_BYTES : OFF_Z;
+  static constexpr int OFF_W = PAIR ? OFF_Y + Y_BYTES : OFF_Z + 2 * Z_BYTES;
+  static constexpr int OFF_WUV = OFF_W;                               // d = 128: 2 x [B_u | B_v]
+  static constexpr int OFF_WO = OFF_WUV + 2 * WUV_BYTES;              // d = 128: B_o
+  static constexpr int W_END = PAIR ? OFF_W + NQ * IMG_BYTES : OFF_WO + WO_BYTES;
+  static constexpr int OFF_BUV = W_END;                               // mix B images (K-major, SW128)
+  static constexpr int OFF_BO = OFF_BUV + 32 * 128;
+  static constexpr int OFF_ROWS = OFF_BO + 16 * 128;                  // 2 x output row of each token row
+  static constexpr int OFF_BAR = OFF_ROWS + 2 * BM * 4;
+  static constexpr int NBAR = 22;
+  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
+  // TMEM columns.
+  static constexpr int T_PM = 0;                                 // P^T blocks (32 columns each)
+  __host__ __device__ static constexpr int T_U(int s) { return 128 * s; }
+  __host__ __device__ static constexpr int T_V(int s) { return 128 * s + 64; }
+  static constexpr int T_Y = 256;
+  static constexpr int T_DT = 256 + D;                           // Delta^T blocks (16 columns each)
+  static_assert(T_PM + 32 * NBLK <= 256 && T_DT + 16 * NBLK <= TMEM_COLS, "TMEM budget");
+  static_assert(PAIR || Y_BYTES <= 2 * Z_BYTES, "d = 128: the Y image fits where the Z buffers go");
+  static_assert(SMEM <= 232448, "shared memory budget");
+};
+
+// Instruction descriptor with the A operand MN-major (B K-major).
+__host__ __device__ constexpr uint32_t idesc_amn(int M, int N, bool bf16) { return idesc_f16(M, N, bf16) | (1u << 15); }
+
+// Descriptor of an SW128 operand read MN-major: 64-element MN atoms ``lbo``
+// bytes apart, 8-line K groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t sdesc_mn(uint32_t addr, uint32_t lbo) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Byte offset of 16-byte chunk ``kc`` (0..7) of line ``ln`` in a 128-byte
+// swizzled region whose 8-line groups are 1024 bytes apart.
+__device__ __forceinline__ uint32_t line_chunk(int ln, int kc) {
+  return (uint32_t)((ln >> 3) * 1024 + (ln & 7) * 128 + ((kc ^ (ln & 7)) << 4));
+}
+
+// TMA: four rows (row0..row3 of a 2-D tensor map), ``col`` .. col + box - 1
+// each, into consecutive 128-byte lines at ``dst``; completes on ``bar``.
+__device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* map, int col, int r0, int r1, int r2,
+                                            int r3, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(col), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Line of token row r (tile r / 16, row r % 16) in a T or Y image, and the
+// 64-channel atom that holds channel column ``c``.  d = 128: atom = c / 64,
+// line = r.  d = 64 (paired tiles): atom = tile parity, line = 32 (tile / 2)
+// + 16 (tile % 2) + r % 16.
+template <int D>
+__device__ __forceinline__ uint32_t img_off(int r, int c) {
+  if constexpr (D == 64) {
+    const int t = r >> 4;
+    return (uint32_t)((t & 1) * ATOM) + line_chunk(32 * (t >> 1) + 16 * (t & 1) + (r & 15), c >> 3);
+  } else {
+    return (uint32_t)((c >> 6) * ATOM) + line_chunk(r, (c & 63) >> 3);
+  }
+}
+
+template <int D, bool BF16, typename TO>
+__global__ void __launch_bounds__(THREADS, 1)
+tcf_kernel(const __grid_constant__ CUtensorMap xmap, Prob p, const unsigned char* __restrict__ img,
+           const uint16_t* __restrict__ amat, const float* __restrict__ gg, const int* __restrict__ layout,
+           const float* __restrict__ scale, TO* __restrict__ out, int* fault, uint32_t probe_ns) {
+  using C = FC<D>;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
+  uint64_t* bar_t = bars + 0;       // T image gathered (tx)
+  uint64_t* bar_pm = bars + 1;      // P^T mix done (commit)
+  uint64_t* bar_p = bars + 2;       // P images written (compute)
+  uint64_t* bar_uv = bars + 3;      // [2] U/V of TMEM buffer s computed (commit)
+  uint64_t* bar_z = bars + 5;       // [2] Z_s written, TMEM buffer s read (compute)
+  uint64_t* bar_yz = bars + 7;      // [2] Y MMA of Z buffer s done (commit)
+  uint64_t* bar_wuv = bars + 9;     // [2] d = 128: [B_u | B_v] stage loaded (tx); d = 64: group loaded (tx)
+  uint64_t* bar_wo = bars + 11;     // d = 128: B_o stage loaded (tx)
+  uint64_t* bar_wfree = bars + 13;  // d = 64: the resident group is no longer read (commit)
+  uint64_t* bar_rfree = bars + 14;  // the T image is read: the region may take the next item (commit)
+  uint64_t* bar_y = bars + 15;      // Y of the item complete (commit)
+  uint64_t* bar_yi = bars + 16;     // Y image written (compute)
+  uint64_t* bar_dt = bars + 17;     // Delta^T mix done (commit)
+  uint64_t* bar_epd = bars + 18;    // epilogue done: Delta^T columns read (compute)
+  uint64_t* bar_probe = bars + 19;  // wait-timeout self-check: nothing arrives on it
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + C::NBAR);
+  volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
+  int* sRows = reinterpret_cast<int*>(sm + C::OFF_ROWS);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t BQ = (int64_t)p.B * p.Qs;
+  const int nMB = (int)((BQ + 7) / 8);
+  const int64_t items = (int64_t)p.Qc * nMB;
+  const int nit = items > blockIdx.x ? (int)((items - 1 - blockIdx.x) / gridDim.x + 1) : 0;
+  const int oob = p.B * p.N;  // a row coordinate past the tensor: TMA fills zeros
+  auto item_of = [&](int it) { return (int64_t)blockIdx.x + (int64_t)it * gridDim.x; };
+  auto qc_of = [&](int it) { return (int)(item_of(it) / nMB); };
+  auto mb_of = [&](int it) { return (int)(item_of(it) - (int64_t)qc_of(it) * nMB); };
+  // Output row (b N + token) of row r of M-block mb, or -1 for a pad row.
+  // (B Q_s < 2^31 is checked on the host, so 32-bit arithmetic suffices.)
+  auto row_of = [&](int mb, int r) -> int {
+    const int tt = mb * 8 + (r >> 4);
+    if (tt >= (int)BQ) return -1;
+    const int b = tt / p.Qs;
+    const int tok = p.tok[(tt - b * p.Qs) * 16 + (r & 15)];
+    return tok < p.N ? b * p.N + tok : -1;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::NBAR; ++i) {
+      const bool comp = bars + i == bar_p || bars + i == bar_yi || bars + i == bar_epd || bars + i == bar_z ||
+                        bars + i == bar_z + 1;
+      mbar_init(bars + i, comp ? NCT : 1);
+    }
+    *sAbort = 0;
+    // The kernel covers channel groups that are one aligned run of d channels.
+    for (int q = 0; q < p.Qc; ++q)
+      if (layout_stride(layout[q]) != 1) {
+        atomicOr(fault, kFaultLayout);
+        *sAbort = 1;
+      }
+    fence_mbar_init();
+    wait_probe(bar_probe, sAbort, probe_ns);
+  }
+  // Mix B operands (K-major, 128-byte swizzled, K = 16): rows 0-15 A_u,
+  // rows 16-31 A_v (BUV, B[k][n] = A[n][k]), and A_o (BO); the 16-element
+  // rows occupy chunks 0-1 of each 128-byte line.  At d = 64 the T and Y
+  // images' zero lines are written once here.
+  if (warp < NCW) {
+    const int tid = threadIdx.x;
+    for (int i = tid; i < 48 * 16; i += NCT) {
+      const int n = i >> 4, k = i & 15;
+      const uint16_t v = n < 16 ? amat[n * 16 + k] : (n < 32 ? amat[256 + (n - 16) * 16 + k] : amat[512 + (n - 32) * 16 + k]);
+      const uint32_t base = n < 32 ? C::OFF_BUV : C::OFF_BO;
+      const int nn = n < 32 ? n : n - 32;
+      *reinterpret_cast<uint16_t*>(sm + base + line_chunk(nn, k >> 3) + (k & 7) * 2) = v;
+    }
+    if constexpr (C::PAIR) {
+      // Zero lines: atom 0 lines 32j + 16 .. +15, atom 1 lines 32j .. +15.
+      for (int i = tid; i < 4 * 16 * 2 * 8; i += NCT) {
+        const int kc = i & 7, ln16 = (i >> 3) & 15, j = (i >> 7) & 3, a = i >> 9;
+        const int ln = 32 * j + (a == 0 ? 16 : 0) + ln16;
+        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(sm + C::OFF_T + a * ATOM + line_chunk(ln, kc)) = z;
+        *reinterpret_cast<uint4*>(sm + C::OFF_Y + a * ATOM + line_chunk(ln, kc)) = z;
+      }
+    }
+    fence_proxy_async_smem();
+  }
+  if (warp == MMA_W) tmem_alloc(sTmem, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *sTmem;
+
+  if (*sAbort) {
+    // The wait-timeout self-check ran out, or a group is not a channel run:
+    // nothing is issued.
+  } else if (warp == PROD_W) {
+    // ------------------------------------------------ producer: TMA row gathers
+    for (int it = 0; it < nit && !*sAbort; ++it) {
+      const int qc = qc_of(it), mb = mb_of(it);
+      // The T region is free once the previous item's mix has read it.
+      if (it >= 1 && !mbar_wait(bar_rfree, (it - 1) & 1, sAbort)) break;
+      int rw[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int r = row_of(mb, 4 * lane + j);
+        rw[j] = r >= 0 ? r : oob;
+      }
+      if (lane == 0) mbar_arrive_expect_tx(bar_t, BM * D * 2);
+      __syncwarp();
+      const int ch0 = p.ch[qc * D];  // first channel of the group's run
+      if constexpr (C::PAIR) {
+        const int t = lane >> 2;
+        const uint32_t dst = C::OFF_T + (t & 1) * ATOM + (32 * (t >> 1) + 16 * (t & 1) + 4 * (lane & 3)) * 128;
+        tma_gather4(sm + dst, &xmap, ch0, rw[0], rw[1], rw[2], rw[3], bar_t);
+      } else {
+#pragma unroll
+        for (int a = 0; a < 2; ++a)
+          tma_gather4(sm + C::OFF_T + a * ATOM + 4 * lane * 128, &xmap, ch0 + 64 * a, rw[0], rw[1], rw[2], rw[3],
+                      bar_t);
+      }
+    }
+  } else if (warp == WGT_W) {
+    // ------------------------------------------------ weight copies
+    if (lane == 0) {
+      int wq = -1, ge = 0;  // d = 64: resident group and number of group loads
+      for (int it = 0; it < nit && !*sAbort; ++it) {
+        const int qc = qc_of(it);
+        if constexpr (C::PAIR) {
+          if (qc != wq) {
+            if (ge > 0 && !mbar_wait(bar_wfree, (ge - 1) & 1, sAbort)) break;
+            mbar_arrive_expect_tx(bar_wuv, C::NQ * C::IMG_BYTES);
+            bulk_g2s(sm + C::OFF_W, img + (int64_t)qc * C::NQ * C::IMG_BYTES, C::NQ * C::IMG_BYTES, bar_wuv);
+            wq = qc;
+            ++ge;
+          }
+        } else {
+          break;  // d = 128: the chunk stream below
+        }
+      }
+      if constexpr (!C::PAIR) {
+        // [B_u | B_v] of chunk c into stage c & 1 once U/V(c - 2) is done,
+        // two chunks ahead; B_o into its single stage once Y(c - 1) is done.
+        const int total = nit * C::NQ;
+        auto src_of = [&](int c) {
+          return img + ((int64_t)qc_of(c / C::NQ) * C::NQ + c % C::NQ) * C::IMG_BYTES;
+        };
+        auto load_uv = [&](int c) {
+          mbar_arrive_expect_tx(bar_wuv + (c & 1), C::WUV_BYTES);
+          bulk_g2s(sm + C::OFF_WUV + (c & 1) * C::WUV_BYTES, src_of(c), C::WUV_BYTES, bar_wuv + (c & 1));
+        };
+        for (int c = 0; c < 2 && c < total; ++c) load_uv(c);
+        for (int c = 0; c < total && !*sAbort; ++c) {
+          if (c >= 1 && !mbar_wait(bar_yz + ((c - 1) & 1), ((c - 1) >> 1) & 1, sAbort)) break;
+          mbar_arrive_expect_tx(bar_wo, C::WO_BYTES);
+          bulk_g2s(sm + C::OFF_WO, src_of(c) + C::WUV_BYTES, C::WO_BYTES, bar_wo);
+          if (c + 2 < total) {
+            if (!mbar_wait(bar_uv + (c & 1), (c >> 1) & 1, sAbort)) break;
+            load_uv(c + 2);
+          }
+        }
+      }
+    }
+  } else if (warp == MMA_W) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t ID_MUV = idesc_amn(BM, 32, BF16);
+      constexpr uint32_t ID_MO = idesc_amn(BM, 16, BF16);
+      constexpr uint32_t ID_UV = idesc_amn(BM, NC, BF16);
+      constexpr uint32_t ID_Y = idesc_f16(BM, D, BF16);
+      const uint32_t s0 = smem_u32(sm);
+      const uint64_t dBUV = sdesc_sw128(s0 + C::OFF_BUV), dBO = sdesc_sw128(s0 + C::OFF_BO);
+      int wq = -1, ge = 0;
+      // Token mix of an image (T or Y) into TMEM column blocks of width nb.
+      auto mix = [&](uint32_t img_addr, uint32_t tcol, int nb, uint64_t bdesc, uint32_t id) {
+        for (int blk = 0; blk < C::NBLK; ++blk) {
+          if constexpr (C::PAIR) {
+            for (int k2 = 0; k2 < 2; ++k2)
+              umma_f16(tbase + tcol + nb * blk, sdesc_mn(img_addr + (32 * blk + 16 * k2) * 128, ATOM), bdesc, id,
+                       k2 ? 1u : 0u);
+          } else {
+            umma_f16(tbase + tcol + nb * blk, sdesc_mn(img_addr + blk * 2048, ATOM), bdesc, id, 0u);
+          }
+        }
+      };
+      // The mix of item it + 1 goes between the chunks of item it and its
+      // Delta mix, so the compute warps turn it into P images while this
+      // item's Delta mix runs, and the next item's first U/V chunks run
+      // while they store this item's outputs.
+      auto item_mix = [&](int it) {
+        mbar_wait(bar_t, it & 1, sAbort);
+        tc_fence_after();
+        if (!*sAbort) mix(s0 + C::OFF_T, C::T_PM, 32, dBUV, ID_MUV);
+        umma_commit(bar_pm);
+        umma_commit(bar_rfree);  // the T image is read
+      };
+      if (nit > 0) item_mix(0);
+      for (int it = 0; it < nit && !*sAbort; ++it) {
+        const int qc = qc_of(it);
+        const bool newgrp = qc != wq;
+        const int c0 = it * C::NQ;
+        if (C::PAIR && newgrp) {
+          mbar_wait(bar_wuv, ge & 1, sAbort);
+          wq = qc;
+          ++ge;
+        }
+        mbar_wait(bar_p, it & 1, sAbort);
+        tc_fence_after();
+        auto wuv = [&](int c) -> uint32_t {
+          return C::PAIR ? s0 + C::OFF_W + (c - c0) * C::IMG_BYTES : s0 + C::OFF_WUV + (c & 1) * C::WUV_BYTES;
+        };
+        auto wo = [&](int c) -> uint32_t {
+          return C::PAIR ? s0 + C::OFF_W + (c - c0) * C::IMG_BYTES + C::WUV_BYTES : s0 + C::OFF_WO;
+        };
+        auto issue_y = [&](int c) {  // Y (+)= Z_c B_o[c]
+          const int s = c & 1;
+          mbar_wait(bar_z + s, (c >> 1) & 1, sAbort);
+          if (!C::PAIR) mbar_wait(bar_wo, c & 1, sAbort);
+          tc_fence_after();
+          if (!*sAbort) {
+            const uint32_t aZ = s0 + C::OFF_Z + s * C::Z_BYTES, aW = wo(c);
+#pragma unroll
+            for (int kk = 0; kk < NC / 16; ++kk)
+              umma_f16(tbase + C::T_Y, sdesc_sw128(sw128_kstep(aZ, kk, BM)), sdesc_sw128(sw128_kstep(aW, kk, D)), ID_Y,
+                       (c > c0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(bar_yz + s);
+        };
+        for (int q = 0; q < C::NQ; ++q) {
+          const int c = c0 + q, s = c & 1;
+          // TMEM buffer s was last read by the gate of chunk c - 2.
+          if (c >= 2) mbar_wait(bar_z + s, ((c - 2) >> 1) & 1, sAbort);
+          if (!C::PAIR) mbar_wait(bar_wuv + s, (c >> 1) & 1, sAbort);
+          tc_fence_after();
+          if (!*sAbort) {
+            const uint32_t aBu = wuv(c), aBv = aBu + C::BU_BYTES;
+            const uint32_t aPu = s0 + C::OFF_PU, aPv = s0 + C::OFF_PV;
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              umma_f16(tbase + C::T_U(s), sdesc_mn(aPu + kk * 2048, C::PI_ATOM), sdesc_sw128(sw128_kstep(aBu, kk, NC)),
+                       ID_UV, kk > 0 ? 1u : 0u);
+              umma_f16(tbase + C::T_V(s), sdesc_mn(aPv + kk * 2048, C::PI_ATOM), sdesc_sw128(sw128_kstep(aBv, kk, NC)),
+                       ID_UV, kk > 0 ? 1u : 0u);
+            }
+          }
+          umma_commit(bar_uv + s);
+          if (q > 0) issue_y(c - 1);
+        }
+        issue_y(c0 + C::NQ - 1);  // waits for the item's last gate: TMEM columns 0-255 are free
+        umma_commit(bar_y);
+        if (C::PAIR && (it + 1 == nit || qc_of(it + 1) != qc)) umma_commit(bar_wfree);
+        if (it + 1 < nit) item_mix(it + 1);
+        // Delta^T = Y^T A_o^T once the Y image is written and the previous
+        // epilogue has read its Delta^T columns.
+        mbar_wait(bar_yi, it & 1, sAbort);
+        if (it >= 1) mbar_wait(bar_epd, (it - 1) & 1, sAbort);
+        tc_fence_after();
+        if (!*sAbort) mix(s0 + C::OFF_Y, C::T_DT, 16, dBO, ID_MO);
+        umma_commit(bar_dt);
+      }
+    }
+  } else {
+    // ------------------------------------------------ compute warps
+    const int tid = threadIdx.x;
+    const int quad = warp & 3, half = warp >> 2;
+    const uint32_t tq = tbase + ((uint32_t)(quad * 32) << 16);  // this warp's TMEM lanes
+    const int r = quad * 32 + lane;                               // token row (gate, Y image) or lane
+    // Channel and tile parity of this thread's TMEM lane in a mix result.
+    const int mc = C::PAIR ? (r & 63) : r;
+    const int mpar = C::PAIR ? (r >> 6) : 0;
+    // ---- output rows of item it and its P images from P^T (lanes =
+    // channels).  Two row buffers: the other may still be read by a warp
+    // finishing the previous epilogue; the barrier publishes the rows.
+    int nrow = -1;  // output row of token row tid of the next item, loaded an item ahead
+    auto pconv = [&](int it) {
+      int* rows = sRows + (it & 1) * BM;
+      if (tid < BM) rows[tid] = it == 0 ? row_of(mb_of(0), tid) : nrow;
+      asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "memory");
+      mbar_wait(bar_pm, it & 1, sAbort);
+      __syncwarp();
+      tc_fence_after();
+#pragma unroll
+      for (int bb = 0; bb < C::NBLK / 2; ++bb) {
+        const int blk = half * (C::NBLK / 2) + bb;
+        const int t = C::PAIR ? 2 * blk + mpar : blk;  // tile of this lane's column block
+        uint32_t v[32];
+        tmem_ld32(tq + C::T_PM + 32 * blk, v);
+        tmem_ld_wait();
+        // tokens 16 t .. 16 t + 15: atom t / 4, chunks 2 (t % 4) and 2 (t % 4) + 1 of line mc
+#pragma unroll
+        for (int uv = 0; uv < 2; ++uv) {
+          unsigned char* base = sm + (uv ? C::OFF_PV : C::OFF_PU) + (t >> 2) * C::PI_ATOM;
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const uint32_t* e = v + 16 * uv + 8 * j;
+            uint4 w;
+            w.x = pack2<BF16>(__uint_as_float(e[0]), __uint_as_float(e[1]));
+            w.y = pack2<BF16>(__uint_as_float(e[2]), __uint_as_float(e[3]));
+            w.z = pack2<BF16>(__uint_as_float(e[4]), __uint_as_float(e[5]));
+            w.w = pack2<BF16>(__uint_as_float(e[6]), __uint_as_float(e[7]));
+            *reinterpret_cast<uint4*>(base + line_chunk(mc, 2 * (t & 3) + j)) = w;
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(bar_p);
+    };
+    // ---- gates: Z_c = silu(U_c) V_c (lanes = tokens)
+    auto gates = [&](int it) {
+      const int c0 = it * C::NQ;
+      for (int q = 0; q < C::NQ; ++q) {
+        const int c = c0 + q, s = c & 1;
+        mbar_wait(bar_uv + s, (c >> 1) & 1, sAbort);
+        __syncwarp();
+        tc_fence_after();
+        uint32_t ur[32], vr[32];
+        tmem_ld32(tq + C::T_U(s) + 32 * half, ur);
+        tmem_ld32(tq + C::T_V(s) + 32 * half, vr);
+        tmem_ld_wait();
+        if (c >= 2) mbar_wait(bar_yz + s, ((c - 2) >> 1) & 1, sAbort);  // Z buffer s read by Y(c - 2)
+        unsigned char* Zs = sm + C::OFF_Z + s * C::Z_BYTES;
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          uint4 w;
+          uint32_t* wp = &w.x;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int i0 = jj * 8 + 2 * e;
+            const uint32_t u2 = pack2<BF16>(__uint_as_float(ur[i0]), __uint_as_float(ur[i0 + 1]));
+            const uint32_t v2 = pack2<BF16>(__uint_as_float(vr[i0]), __uint_as_float(vr[i0 + 1]));
+            wp[e] = silu_mul2<BF16>(u2, v2);
+          }
+          *reinterpret_cast<uint4*>(Zs + sw128_off(r, 32 * half + jj * 8, BM)) = w;
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(bar_z + s);
+      }
+    };
+    // ---- Y image (lanes = tokens): channels [half D / 2, (half + 1) D / 2)
+    auto yimg = [&](int it) {
+      mbar_wait(bar_y, it & 1, sAbort);
+      __syncwarp();
+      tc_fence_after();
+#pragma unroll
+      for (int cb = 0; cb < D / 64; ++cb) {
+        const int cbase = half * (D / 2) + 32 * cb;
+        uint32_t v[32];
+        tmem_ld32(tq + C::T_Y + cbase, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const uint32_t* e = v + 8 * m;
+          uint4 w;
+          w.x = pack2<BF16>(__uint_as_float(e[0]), __uint_as_float(e[1]));
+          w.y = pack2<BF16>(__uint_as_float(e[2]), __uint_as_float(e[3]));
+          w.z = pack2<BF16>(__uint_as_float(e[4]), __uint_as_float(e[5]));
+          w.w = pack2<BF16>(__uint_as_float(e[6]), __uint_as_float(e[7]));
+          *reinterpret_cast<uint4*>(sm + C::OFF_Y + img_off<D>(r, cbase + 8 * m)) = w;
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(bar_yi);
+    };
+    // ---- epilogue: out[row, c0 + c] = Delta[row, c] gamma[c] s_b.  Delta^T
+    // arrives with lanes = channels; the tile goes through shared memory (the
+    // Z region, free until the next item's gates) so that the global stores
+    // are whole row segments (D channels per row, 16 bytes per lane).  f32
+    // outputs at d = 128 take two passes of 64 tokens.
+    auto epilogue = [&](int it) {
+      mbar_wait(bar_dt, it & 1, sAbort);
+      __syncwarp();
+      tc_fence_after();
+      if (*sAbort) return;
+      const int qc = qc_of(it);
+      const int* rows = sRows + (it & 1) * BM;
+      const float gm = gg[(int64_t)qc * D + mc];
+      const int c0ch = p.ch[qc * D];
+      constexpr int NCOL = C::PAIR ? 32 : 64;  // Delta^T columns of this warp half
+      constexpr int STG_ROWS = (BM * D * (int)sizeof(TO) <= 2 * C::Z_BYTES) ? BM : BM / 2;
+      constexpr int NPASS = BM / STG_ROWS;
+      TO* stg = reinterpret_cast<TO*>(sm + C::OFF_Z);  // [STG_ROWS][D]
+      uint32_t v[NCOL];
+#pragma unroll
+      for (int cc = 0; cc < NCOL; cc += 32) tmem_ld32(tq + C::T_DT + NCOL * half + cc, *reinterpret_cast<uint32_t(*)[32]>(v + cc));
+      tmem_ld_wait();
+#pragma unroll 1
+      for (int pass = 0; pass < NPASS; ++pass) {
+        // Delta^T column k of this thread holds token tok(k) of channel mc.
+        // The per-sample scale (block mode) is a separate loop: its row ->
+        // sample division must not run when there is no scale.
+        auto tok_of = [&](int k) {
+          const int col = NCOL * half + k;  // block col / 16, token col % 16
+          const int t = C::PAIR ? 2 * (col >> 4) + mpar : (col >> 4);
+          return 16 * t + (col & 15);
+        };
+        if (scale) {
+#pragma unroll
+          for (int k = 0; k < NCOL; ++k) {
+            const int tok = tok_of(k);
+            if (tok / STG_ROWS == pass) {
+              const int rw = rows[tok];
+              const float sc = rw >= 0 ? scale[rw / p.N] : 0.f;
+              stg[(tok % STG_ROWS) * D + mc] = Elem<TO>::from(__uint_as_float(v[k]) * gm * sc);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < NCOL; ++k) {
+            const int tok = tok_of(k);
+            if (tok / STG_ROWS == pass) stg[(tok % STG_ROWS) * D + mc] = Elem<TO>::from(__uint_as_float(v[k]) * gm);
+          }
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "memory");
+        // Row stores: 16 bytes per thread, consecutive threads along a row.
+        constexpr int VPR = D * (int)sizeof(TO) / 16;  // 16-byte vectors per row segment
+        for (int u = tid; u < STG_ROWS * VPR; u += NCT) {
+          const int rl = u / VPR, vi = u - rl * VPR;
+          const int rw = rows[pass * STG_ROWS + rl];
+          if (rw >= 0) {
+            const uint4 val = *reinterpret_cast<const uint4*>(stg + rl * D + vi * (16 / (int)sizeof(TO)));
+            *reinterpret_cast<uint4*>(out + (int64_t)rw * p.C + c0ch + vi * (16 / (int)sizeof(TO))) = val;
+          }
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "memory");  // staging reused by the next pass / the gates
+      }
+      tc_fence_before();
+      mbar_arrive(bar_epd);
+    };
+    // Order: gates(it), Y image(it), P images(it + 1), epilogue(it) -- the
+    // tensor pipe runs the Delta mix of it and the first U/V chunks of it + 1
+    // while the epilogue stores.
+    if (nit > 0) pconv(0);
+    for (int it = 0; it < nit && !*sAbort; ++it) {
+      // The next item's row indices: the table load overlaps the gates.
+      if (tid < BM && it + 1 < nit) nrow = row_of(mb_of(it + 1), tid);
+      gates(it);
+      yimg(it);
+      if (it + 1 < nit) pconv(it + 1);
+      epilogue(it);
+    }
+  }
+
+  __syncwarp();
+  __syncthreads();
+  report_abort(sAbort, fault);
+  if (*sAbort) {
+    // A wait gave up: give in-flight copies and MMAs time to land before
+    // the shared memory and TMEM they target are released.
+    for (int i = 0; i < 1000; ++i) __nanosleep(1000);
+  }
+  if (warp == MMA_W) {
+    tc_fence_after();
+    tmem_dealloc(tbase, TMEM_COLS);
+  }
+}
+
+int num_sms_f() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!cached[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+// cuTensorMapEncodeTiled, looked up through the runtime once (the library
+// does not link the driver library, so it loads on machines without one).
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
+// 2-D tensor map of x viewed as [B N rows, C channels] (16-bit), box of 64
+// channels x 1 row, 128-byte swizzle: the row-gather source of the kernel.
+int make_xmap(CUtensorMap* map, const void* x, const Prob& p, bool bf16) {
+  auto encode = encode_fn();
+  if (!encode) {
+    set_error("tc forward: cuTensorMapEncodeTiled is not available from the CUDA driver");
+    return OW_ERR_CUDA;
+  }
+  const cuuint64_t dims[2] = {(cuuint64_t)p.C, (cuuint64_t)p.B * p.N};
+  const cuuint64_t strides[1] = {(cuuint64_t)p.C * 2};
+  const cuuint32_t box[2] = {64, 1};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                            const_cast<void*>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("tc forward: cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
+    return OW_ERR_CUDA;
+  }
+  return OW_OK;
+}
+
+template <int D, bool BF16>
+int tcf_forward_t(const ow_bigemm_args_t* a, const Prob& p, const unsigned char* img, const uint16_t* amat,
+                  const float* gg, const int* layout, cudaStream_t st) {
+  CUtensorMap map;
+  OW_RETURN_IF(make_xmap(&map, a->x, p, BF16));
+  int* fault = nullptr;
+  OW_RETURN_IF(fault_word(&fault));
+  const int64_t items = (int64_t)p.Qc * ((p.BQ() + 7) / 8);
+  const int grid = (int)std::min<int64_t>(items, num_sms_f());
+  if (grid == 0) return OW_OK;
+  auto go = [&](auto* to) -> int {
+    using TO = std::remove_pointer_t<decltype(to)>;
+    auto kern = tcf_kernel<D, BF16, TO>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FC<D>::SMEM);
+    if (e != cudaSuccess) {
+      set_error("tc forward: cannot reserve %d bytes of shared memory: %s", FC<D>::SMEM, cudaGetErrorString(e));
+      return OW_ERR_CUDA;
+    }
+    profile_mark(OW_PROF_FWD, false, st);
+    launch(kern, grid, THREADS, FC<D>::SMEM, st, map, p, img, amat, gg, layout, a->sample_scale, (TO*)a->out,
+           fault, wait_probe_ns());
+    profile_mark(OW_PROF_FWD, true, st);
+    OW_CHECK_LAUNCH("tcf_kernel");
+    return OW_OK;
+  };
+  using T16 = std::conditional_t<BF16, __nv_bfloat16, __half>;
+  if (a->out_dtype == (BF16 ? OW_DTYPE_BF16 : OW_DTYPE_F16)) return go((T16*)nullptr);
+  return go((float*)nullptr);
+}
+
+}  // namespace
+
+bool tcf_covers(const ow_bigemm_args_t* a, const Prob& p) {
+  const int c16 = a->compute_dtype;
+  return (c16 == OW_DTYPE_BF16 || c16 == OW_DTYPE_F16) && a->x_dtype == c16 && !a->rstd && !a->residual &&
+         p.chs == 1 && (p.d == 64 || p.d == 128) && p.rd == 2 * p.d && p.C % 8 == 0 &&
+         (uintptr_t)a->x % 16 == 0 && (uintptr_t)a->out % 16 == 0 &&
+         (a->out_dtype == c16 || a->out_dtype == OW_DTYPE_F32) &&
+         (int64_t)p.B * p.N < (1LL << 31) - 1;
+}
+
+int tcf_forward(const ow_bigemm_args_t* a, const Prob& p, const unsigned char* img, const uint16_t* amat,
+                const float* gg, const int* layout, void* stream) {
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool bf = a->compute_dtype == OW_DTYPE_BF16;
+  if (p.d == 64)
+    return bf ? tcf_forward_t<64, true>(a, p, img, amat, gg, layout, st)
+              : tcf_forward_t<64, false>(a, p, img, amat, gg, layout, st);
+  return bf ? tcf_forward_t<128, true>(a, p, img, amat, gg, layout, st)
+            : tcf_forward_t<128, false>(a, p, img, amat, gg, layout, st);
+}
+
+}  // namespace ow

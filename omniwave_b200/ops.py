@@ -132,6 +132,27 @@ def _validate_plan(plan: RoutePlan) -> None:
         raise ValueError("route plan must visit every token and channel exactly once")
 
 
+def channel_stride_hint(plan: RoutePlan) -> int:
+    """The route's channel-layout hint for the C ABI (``ow_route_t.ch_stride``):
+    S when every channel group is ``c0 + S*k`` (S = 1: one run starting on a
+    multiple of 8; S in {2, 4, 8}: the stride-Q_c groups of radix levels 1
+    and 2 with c0 < S), else 0 (unknown)."""
+    ch = plan.channel_indices
+    q_c, d = ch.shape
+    if plan.channels % 8 or not bool(plan.channel_mask.all()):
+        return 0
+    c0 = ch[:, :1]
+    if d == 1:
+        return 0
+    steps = ch[:, 1:] - ch[:, :-1]
+    s = int(steps[0, 0])
+    if s not in (1, 2, 4, 8) or not bool((steps == s).all()):
+        return 0
+    if s == 1:
+        return 1 if bool((c0 % 8 == 0).all()) else 0
+    return s if bool((c0 < s).all()) and s * d <= plan.channels else 0
+
+
 def route_tables(plan: RoutePlan, device: torch.device) -> tuple[Tensor, Tensor]:
     """int32 device copies of ``plan.token_indices`` / ``plan.channel_indices``."""
     key = (id(plan), str(device))
@@ -147,6 +168,18 @@ def route_tables(plan: RoutePlan, device: torch.device) -> tuple[Tensor, Tensor]
         ch = plan.channel_indices.to(torch.int32).reshape(-1).to(device)
         _tables[key] = (plan, tok, ch)  # keeps ``plan`` alive, so its id stays unique
         return tok, ch
+
+
+_hints: dict[int, tuple[RoutePlan, int]] = {}
+
+
+def _stride_hint(plan: RoutePlan) -> int:
+    hit = _hints.get(id(plan))
+    if hit is not None and hit[0] is plan:
+        return hit[1]
+    v = channel_stride_hint(plan)
+    _hints[id(plan)] = (plan, v)  # keeps ``plan`` alive, so its id stays unique
+    return v
 
 
 # ---------------------------------------------------------------------------
@@ -171,7 +204,7 @@ def _make_args(x, plan, tok, ch, weights, w_dtype, compute, rstd, norm_w, scale,
     a_u, a_v, a_o, b_u, b_v, b_o, gamma = weights
     q_c, d, rd = b_u.shape
     q_s, g = plan.token_indices.shape
-    r = _lib.Route(b, h, w, c, q_s, q_c, g, d, rd, tok.data_ptr(), ch.data_ptr())
+    r = _lib.Route(b, h, w, c, q_s, q_c, g, d, rd, tok.data_ptr(), ch.data_ptr(), _stride_hint(plan))
     return _lib.Args(
         r, x.data_ptr(), _lib.DTYPE_CODE[x.dtype], _lib.DTYPE_CODE[compute],
         _lib.ptr(rstd), _lib.ptr(norm_w),
