@@ -419,10 +419,21 @@ tcf_kernel(const __grid_constant__ CUtensorMap xmap, Prob p, const unsigned char
     // ---- output rows of item it and its P images from P^T (lanes =
     // channels).  Two row buffers: the other may still be read by a warp
     // finishing the previous epilogue; the barrier publishes the rows.
-    int nrow = -1;  // output row of token row tid of the next item, loaded an item ahead
+    // Output row of token row tid of the next item: the route-table load is
+    // issued an item ahead (from a clamped index, so nothing waits for it)
+    // and the row is formed when the item's P images are built.
+    int ntok = 0, nb = 0, nvalid = 0;
+    auto row_issue = [&](int it) {
+      const int tt = mb_of(it) * 8 + (tid >> 4);
+      nvalid = tt < (int)BQ;
+      const int ttc = nvalid ? tt : 0;
+      nb = ttc / p.Qs;
+      ntok = p.tok[(ttc - nb * p.Qs) * 16 + (tid & 15)];
+    };
     auto pconv = [&](int it) {
       int* rows = sRows + (it & 1) * BM;
-      if (tid < BM) rows[tid] = it == 0 ? row_of(mb_of(0), tid) : nrow;
+      if (it == 0 && tid < BM) row_issue(0);
+      if (tid < BM) rows[tid] = nvalid && ntok < p.N ? nb * p.N + ntok : -1;
       asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "memory");
       mbar_wait(bar_pm, it & 1, sAbort);
       __syncwarp();
@@ -583,7 +594,7 @@ tcf_kernel(const __grid_constant__ CUtensorMap xmap, Prob p, const unsigned char
     if (nit > 0) pconv(0);
     for (int it = 0; it < nit && !*sAbort; ++it) {
       // The next item's row indices: the table load overlaps the gates.
-      if (tid < BM && it + 1 < nit) nrow = row_of(mb_of(it + 1), tid);
+      if (tid < BM && it + 1 < nit) row_issue(it + 1);
       gates(it);
       yimg(it);
       if (it + 1 < nit) pconv(it + 1);
