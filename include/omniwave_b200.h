@@ -42,7 +42,7 @@
 extern "C" {
 #endif
 
-#define OW_ABI_VERSION 2
+#define OW_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define OW_API __attribute__((visibility("default")))
@@ -249,6 +249,46 @@ OW_API size_t ow_noalloc_scratch_limit(void);
  * are bitwise reproducible run to run.
  */
 OW_API int ow_bigemm_bwd(const ow_bigemm_args_t* args, const ow_bigemm_grads_t* grads, void* stream);
+
+/*
+ * Space-to-depth + Linear, the OmniWeave-T stem and downsamples
+ * (omniweave/models/backbone.py:14-27 ``space_to_depth_nhwc`` followed by the
+ * bias-free ``nn.Linear`` of :121 and :128-132, as called at :176-187), as one
+ * tensor-core GEMM that reads the rearranged rows straight from x:
+ *
+ *   out[b, i, j, n] = sum_{dy, dx, c} s(b, i, j, dy, dx, c) * weight[n, (dy f + dx) C + c]
+ *   s = x[b, f i + dy, f j + dx, c]    layout OW_LAYOUT_NHWC (downsample)
+ *   s = x[b, c, f i + dy, f j + dx]    layout OW_LAYOUT_NCHW (stem: the image
+ *                                      batch before its NHWC permute, :173)
+ *
+ * ``out`` is NHWC [batch, height/factor, width/factor, out_features] in
+ * ``out_dtype`` (bf16 or f16), which is also the dtype the products are
+ * taken in (f32 accumulation), as under the reference's autocast.  weight is
+ * [out_features, factor^2 channels] row-major (f32 or out_dtype; f32 is
+ * rounded).  Supported: NHWC with x_dtype == out_dtype, channels % 64 == 0,
+ * width/factor <= 128 and out_features % 256 == 0; NCHW with channels == 3,
+ * factor == 4, x f32 or out_dtype and out_features a multiple of 128 up to
+ * 512.  x and out 16-byte aligned.  Anything else returns OW_ERR_UNSUPPORTED.
+ */
+#define OW_LAYOUT_NHWC 0
+#define OW_LAYOUT_NCHW 1
+typedef struct ow_s2d_linear_t {
+  const void* x;
+  int32_t x_dtype;
+  int32_t layout;          /* OW_LAYOUT_NHWC or OW_LAYOUT_NCHW */
+  int32_t batch, height, width, channels, factor;
+  const void* weight;
+  int32_t w_dtype;
+  int32_t out_features;
+  void* out;
+  int32_t out_dtype;
+  void* workspace;         /* ow_s2d_linear_workspace_size() bytes */
+  size_t workspace_bytes;
+} ow_s2d_linear_t;
+
+/* Workspace bytes ow_s2d_linear_fwd needs (0 if the arguments are unsupported). */
+OW_API size_t ow_s2d_linear_workspace_size(const ow_s2d_linear_t* args);
+OW_API int ow_s2d_linear_fwd(const ow_s2d_linear_t* args, void* stream);
 
 #ifdef __cplusplus
 }

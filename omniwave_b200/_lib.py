@@ -16,7 +16,7 @@ import torch
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_PKG, "libomniwave_b200.so")
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 DTYPE_CODE = {
     torch.float32: 0,
@@ -63,11 +63,26 @@ class Grads(ctypes.Structure):
     ]
 
 
+class S2dLinear(ctypes.Structure):
+    _fields_ = [
+        ("x", _vp), ("x_dtype", _c_i32), ("layout", _c_i32),
+        ("batch", _c_i32), ("height", _c_i32), ("width", _c_i32), ("channels", _c_i32),
+        ("factor", _c_i32),
+        ("weight", _vp), ("w_dtype", _c_i32), ("out_features", _c_i32),
+        ("out", _vp), ("out_dtype", _c_i32),
+        ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+LAYOUT_NHWC = 0
+LAYOUT_NCHW = 1
+
 EXPORTS = (
     "ow_abi_version", "ow_last_error", "ow_device_supported", "ow_device_fault",
     "ow_launch_count", "ow_bigemm_workspace_size",
     "ow_rmsnorm_rstd", "ow_bigemm_fwd", "ow_bigemm_bwd", "ow_bigemm_fwd_noalloc",
     "ow_noalloc_scratch_limit", "ow_profile_events", "ow_debug_wait_probe",
+    "ow_s2d_linear_workspace_size", "ow_s2d_linear_fwd",
 )
 
 _lock = threading.Lock()
@@ -114,6 +129,10 @@ def load() -> ctypes.CDLL:
         lib.ow_noalloc_scratch_limit.restype = ctypes.c_size_t
         lib.ow_bigemm_bwd.argtypes = [ctypes.POINTER(Args), ctypes.POINTER(Grads), _vp]
         lib.ow_bigemm_bwd.restype = ctypes.c_int
+        lib.ow_s2d_linear_workspace_size.argtypes = [ctypes.POINTER(S2dLinear)]
+        lib.ow_s2d_linear_workspace_size.restype = ctypes.c_size_t
+        lib.ow_s2d_linear_fwd.argtypes = [ctypes.POINTER(S2dLinear), _vp]
+        lib.ow_s2d_linear_fwd.restype = ctypes.c_int
         v = lib.ow_abi_version()
         if v != ABI_VERSION:
             raise NativeLibraryError(f"ABI version mismatch: library {v}, binding {ABI_VERSION}")

@@ -106,6 +106,14 @@ int tc_pack_forward(const ow_bigemm_args_t* a, const Prob& p, const uint16_t* am
 int fault_word(int** out);
 // Wait-timeout self-check setting (ow_debug_wait_probe); 0 when off.
 uint32_t wait_probe_ns();
+// Streaming multiprocessors of the current device (cached per device).
+int device_sm_count();
+// cuTensorMapEncodeTiled for a 16-bit tensor of ``rank`` dimensions (dims and
+// byte strides of dimensions 1.. innermost first), 128-byte swizzle, zero
+// fill out of range; ``map`` points at a CUtensorMap.  ``who`` prefixes the
+// error message.
+int encode_tiled_map(void* map, bool bf16, int rank, const void* base, const uint64_t* dims,
+                     const uint64_t* strides, const uint32_t* box, const char* who);
 
 // RMSNorm backward of block mode from the gradient w.r.t. the normalised
 // input (``dxn``, f32 or the 16-bit compute type; CUDA cores, row-wise).  norm_bwd_take() carves its partials from

@@ -661,19 +661,6 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict_
   }
 }
 
-int num_sms() {
-  static int cached[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
-  if (!cached[dev]) {
-    int n = 0;
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cached[dev] = n > 0 ? n : 148;
-  }
-  return cached[dev];
-}
-
 template <int D, bool BF16>
 int tc_prep(const ow_bigemm_args_t* a, const Prob& p, const TcWs<D>& w, unsigned char* base,
             cudaStream_t st) {
@@ -719,7 +706,7 @@ int tc_forward_t(const ow_bigemm_args_t* a, const Prob& p, cudaStream_t st, Carv
                                 (const int*)(base + w.contig), base + w.packed, st)));
   profile_mark(OW_PROF_FPACK, true, st);
   const int64_t items = (int64_t)p.Qc * ((p.BQ() + 7) / 8);
-  const int grid = (int)std::min<int64_t>(items, num_sms());
+  const int grid = (int)std::min<int64_t>(items, device_sm_count());
   // 16-byte vector loads/stores need aligned bases (channel runs are checked
   // per group by the prep kernel).
   const int vec_ok = ((uintptr_t)a->x % 16 == 0) && ((uintptr_t)a->out % 16 == 0) && (p.C % 8 == 0);

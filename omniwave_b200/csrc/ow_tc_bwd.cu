@@ -1700,24 +1700,11 @@ __global__ void tc_bwd_reduce_small_kernel(Prob p, BwdArgs a, const TW* __restri
   }
 }
 
-int num_sms_b() {
-  static int cached[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
-  if (!cached[dev]) {
-    int n = 0;
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cached[dev] = n > 0 ? n : 148;
-  }
-  return cached[dev];
-}
-
 template <int D, bool BF16>
 int tc_backward_t(const ow_bigemm_args_t* ar, const ow_bigemm_grads_t* gr, const Prob& p, cudaStream_t st,
                   Carver& ws) {
   const bool block = ar->rstd != nullptr;
-  BPlan<D> pl(p, block, num_sms_b());
+  BPlan<D> pl(p, block, device_sm_count());
   unsigned char* base = (unsigned char*)ws.take(pl.total);
   NormBwd nbw{};
   if (block) nbw = norm_bwd_take((int64_t)p.B * p.N, p.C, ws);

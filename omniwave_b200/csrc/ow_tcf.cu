@@ -616,58 +616,13 @@ tcf_kernel(const __grid_constant__ CUtensorMap xmap, Prob p, const unsigned char
   }
 }
 
-int num_sms_f() {
-  static int cached[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
-  if (!cached[dev]) {
-    int n = 0;
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cached[dev] = n > 0 ? n : 148;
-  }
-  return cached[dev];
-}
-
-// cuTensorMapEncodeTiled, looked up through the runtime once (the library
-// does not link the driver library, so it loads on machines without one).
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static std::once_flag once;
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  std::call_once(once, [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-    else
-      cudaGetLastError();
-  });
-  return fn;
-}
-
 // 2-D tensor map of x viewed as [B N rows, C channels] (16-bit), box of 64
 // channels x 1 row, 128-byte swizzle: the row-gather source of the kernel.
 int make_xmap(CUtensorMap* map, const void* x, const Prob& p, bool bf16) {
-  auto encode = encode_fn();
-  if (!encode) {
-    set_error("tc forward: cuTensorMapEncodeTiled is not available from the CUDA driver");
-    return OW_ERR_CUDA;
-  }
-  const cuuint64_t dims[2] = {(cuuint64_t)p.C, (cuuint64_t)p.B * p.N};
-  const cuuint64_t strides[1] = {(cuuint64_t)p.C * 2};
-  const cuuint32_t box[2] = {64, 1};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                            const_cast<void*>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    set_error("tc forward: cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
-    return OW_ERR_CUDA;
-  }
-  return OW_OK;
+  const uint64_t dims[2] = {(uint64_t)p.C, (uint64_t)p.B * p.N};
+  const uint64_t strides[1] = {(uint64_t)p.C * 2};
+  const uint32_t box[2] = {64, 1};
+  return encode_tiled_map(map, bf16, 2, x, dims, strides, box, "tc forward");
 }
 
 template <int D, bool BF16>
@@ -678,7 +633,7 @@ int tcf_forward_t(const ow_bigemm_args_t* a, const Prob& p, const unsigned char*
   int* fault = nullptr;
   OW_RETURN_IF(fault_word(&fault));
   const int64_t items = (int64_t)p.Qc * ((p.BQ() + 7) / 8);
-  const int grid = (int)std::min<int64_t>(items, num_sms_f());
+  const int grid = (int)std::min<int64_t>(items, device_sm_count());
   if (grid == 0) return OW_OK;
   auto go = [&](auto* to) -> int {
     using TO = std::remove_pointer_t<decltype(to)>;
@@ -701,6 +656,55 @@ int tcf_forward_t(const ow_bigemm_args_t* a, const Prob& p, const unsigned char*
 }
 
 }  // namespace
+
+// cuTensorMapEncodeTiled, looked up through the runtime once (the library
+// does not link the driver library, so it loads on machines without one).
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
+int encode_tiled_map(void* map, bool bf16, int rank, const void* base, const uint64_t* dims,
+                     const uint64_t* strides, const uint32_t* box, const char* who) {
+  auto encode = encode_fn();
+  if (!encode) {
+    set_error("%s: cuTensorMapEncodeTiled is not available from the CUDA driver", who);
+    return OW_ERR_CUDA;
+  }
+  if (rank < 1 || rank > 5) {
+    set_error("%s: tensor map rank %d", who, rank);
+    return OW_ERR_INVALID;
+  }
+  cuuint64_t d[5], s[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+    if (i + 1 < rank) s[i] = strides[i];
+  }
+  const CUresult r = encode(static_cast<CUtensorMap*>(map),
+                            bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                            (cuuint32_t)rank, const_cast<void*>(base), d, s, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("%s: cuTensorMapEncodeTiled failed (CUresult %d)", who, (int)r);
+    return OW_ERR_CUDA;
+  }
+  return OW_OK;
+}
 
 bool tcf_covers(const ow_bigemm_args_t* a, const Prob& p) {
   const int c16 = a->compute_dtype;

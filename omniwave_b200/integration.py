@@ -18,6 +18,11 @@ training engine -- run on the B200 kernels when built with
   ``omniweave.models.block`` too, which imported it by value.
 * ``OmniWeaveBlock.forward`` (block.py:80-108) runs the fused block (RMSNorm in
   the gather, residual and drop-path scale in the epilogue) for ``"cuda"``.
+* ``OmniWeaveBackbone.forward_features`` (backbone.py:166-187) of a model whose
+  blocks all use ``"cuda"`` runs the stem and the downsamples as fused
+  space-to-depth GEMMs, each stage anchor folded into the GEMM before it
+  (``omniwave_b200.s2d``), when the compute dtype is 16-bit and the kernels
+  take the shapes; otherwise the reference method runs.
 
 Parameter names, shapes and initialisation are the reference's own (nothing
 here constructs parameters), so state dicts interchange by construction.
@@ -31,7 +36,7 @@ from typing import Any
 
 from torch import Tensor
 
-from omniwave_b200 import ops
+from omniwave_b200 import ops, s2d
 
 __all__ = ["install", "installed", "uses_cuda"]
 
@@ -75,10 +80,12 @@ def install() -> Any:
             return pkg
         od = importlib.import_module("omniweave.ops.dispatch")
         mb = importlib.import_module("omniweave.models.block")
+        mbb = importlib.import_module("omniweave.models.backbone")
 
         ref_select = od.select_backend
         ref_bigemm = ob.bigemm
         ref_block_forward = mb.OmniWeaveBlock.forward
+        ref_forward_features = mbb.OmniWeaveBackbone.forward_features
 
         def select_backend(x, requested, support_check):
             """dispatch.py:13-49 with ``"cuda"`` added to the valid names."""
@@ -110,10 +117,17 @@ def install() -> Any:
             return ops.block_forward(x, self.plan, self.norm_weight, self.a_u, self.a_v, self.a_o,
                                      self.b_u, self.b_v, self.b_o, self.gamma, scale)
 
+        def forward_features(self, x: Tensor):
+            """backbone.py:166-187 with fused stem and downsamples on the cuda backend."""
+            if x.is_cuda and uses_cuda(self) and s2d.features_supported(self, x)[0]:
+                return s2d.forward_features(self, x)
+            return ref_forward_features(self, x)
+
         od.select_backend = select_backend
         ob.bigemm = bigemm
         mb.bigemm = bigemm
         mb.OmniWeaveBlock.forward = block_forward
+        mbb.OmniWeaveBackbone.forward_features = forward_features
         setattr(ob, _MARK, True)
         return pkg
 
