@@ -157,15 +157,21 @@ struct BPlan {
     nH = C::NH;
     // Split one wave of CTAs across the roles so that the slowest role
     // finishes first: each role's time is its items per CTA times its
-    // steady-state time per item, measured on B200 from each CTA's finish
-    // time (us per item; UV per 128-feature half): DGRAD 5.5, UV 3.05, O 3.65
-    // at d = 64; 17.9, 8.0, 14.9 at d = 128.  Every split of one wave is tried.
-    const double tD = D == 64 ? 5.5 : 17.9, tU = D == 64 ? 3.05 : 8.0, tO = D == 64 ? 3.65 : 14.9;
+    // steady-state time per item (us per item; UV per 128-feature half),
+    // measured on B200 from per-CTA start / end timestamps of the role kernel
+    // at B = 128: DGRAD 4.9, UV 2.97, O 3.5 at d = 64; 17.8, 7.75, 14.5 at
+    // d = 128.  DGRAD's dX stores of channel groups with stride > 1 (radix
+    // levels 1, 2) take about 11% longer.  The split is a pure function of the
+    // shape and the SM count, so the weight-gradient partials (one per CTA,
+    // summed in a fixed order) and hence the results are the same on every
+    // run.  Every split of one wave is tried.
+    const double tD = (D == 64 ? 4.9 : 17.8) * (p.chs > 1 ? 1.11 : 1.0);
+    const double tU = D == 64 ? 2.97 : 7.75, tO = D == 64 ? 3.5 : 14.5;
     const int64_t nMB = (p.BQ() + 7) / 8;
     // The search is a few thousand steps; its result is kept per shape.
     static std::mutex mu;
-    static std::map<std::array<int64_t, 4>, std::pair<int, int>> memo;
-    const std::array<int64_t, 4> key{nMB, p.Qc, nH, sms};
+    static std::map<std::array<int64_t, 5>, std::pair<int, int>> memo;
+    const std::array<int64_t, 5> key{nMB, p.Qc, nH, sms, p.chs > 1 ? 1 : 0};
     {
       std::lock_guard<std::mutex> lk(mu);
       auto f = memo.find(key);
@@ -1227,23 +1233,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           tmem_ld_cols<HC>(trow + tcol + SC, vr);
           tmem_ld_cols<HC>(trow + tcol + 2 * SC, zr);
           tmem_ld_wait();
-          unsigned char* du_at;
-          int col0;
-          int dv_off;
-          if (role == R_DGRAD) {
-            if (c >= 2) mbar_wait(bar_b + b, ((c - 2) >> 1) & 1, sAbort);  // dP(c-2) read this buffer
-            du_at = sm + C::D_S + buf_atom(b, 2);
-            dv_off = C::Z_BYTES;
-            col0 = buf_col(b);
-          } else {
-            if (j == 0 && it > 0) mbar_wait(bar_w, (it - 1) & 1, sAbort);  // products read dU_h / dV_h
-            du_at = sm + C::U_S;
-            dv_off = 2 * C::Z_BYTES;
-            col0 = sub_of(j) * SC;
-          }
+          // The math runs before the wait for the destination buffer, so it
+          // overlaps the MMAs still reading that buffer (DGRAD: dP of
+          // sub-chunk c - 2; UV: the previous item's weight-gradient products).
+          uint32_t wu[HC / 8][4], wv[HC / 8][4];
 #pragma unroll
           for (int jj = 0; jj < HC / 8; ++jj) {
-            uint32_t wu[4], wv[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               // Two features at a time in packed f32x2 arithmetic:
@@ -1263,12 +1258,29 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
               const uint64_t ds2 = mul2(z2, s2);
               const float2 dv = f2unpack(mul2(ds2, u2));
               const float2 du = f2unpack(mul2(mul2(ds2, v2), fma2(u2, oms, one)));
-              wu[e] = pack2<BF16>(du.x, du.y);
-              wv[e] = pack2<BF16>(dv.x, dv.y);
+              wu[jj][e] = pack2<BF16>(du.x, du.y);
+              wv[jj][e] = pack2<BF16>(dv.x, dv.y);
             }
+          }
+          unsigned char* du_at;
+          int col0;
+          int dv_off;
+          if (role == R_DGRAD) {
+            if (c >= 2) mbar_wait(bar_b + b, ((c - 2) >> 1) & 1, sAbort);  // dP(c-2) read this buffer
+            du_at = sm + C::D_S + buf_atom(b, 2);
+            dv_off = C::Z_BYTES;
+            col0 = buf_col(b);
+          } else {
+            if (j == 0 && it > 0) mbar_wait(bar_w, (it - 1) & 1, sAbort);  // products read dU_h / dV_h
+            du_at = sm + C::U_S;
+            dv_off = 2 * C::Z_BYTES;
+            col0 = sub_of(j) * SC;
+          }
+#pragma unroll
+          for (int jj = 0; jj < HC / 8; ++jj) {
             const uint32_t off = sw128_off(r, col0 + cb + jj * 8, BM);
-            *reinterpret_cast<uint4*>(du_at + off) = make_uint4(wu[0], wu[1], wu[2], wu[3]);
-            *reinterpret_cast<uint4*>(du_at + dv_off + off) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            *reinterpret_cast<uint4*>(du_at + off) = make_uint4(wu[jj][0], wu[jj][1], wu[jj][2], wu[jj][3]);
+            *reinterpret_cast<uint4*>(du_at + dv_off + off) = make_uint4(wv[jj][0], wv[jj][1], wv[jj][2], wv[jj][3]);
           }
         } else {  // R_O: Z = silu(U) * V into the pair buffer at feature offset fo
           uint32_t ur[HC], vr[HC];
@@ -1277,22 +1289,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_bwd_kernel(BwdArgs a) {
           tmem_ld_cols<HC>(trow + tcol + SC, vr);
           tmem_ld_wait();
           const int fo = (j % (128 / SC)) * SC;
-          // The previous pair's M_o (issued after its Y MMAs) has read the buffer.
-          if (fo == 0 && pc > 0) mbar_wait(bar_w, (pc - 1) & 1, sAbort);
-          unsigned char* sz = sm + C::O_ZP;
+          uint32_t wz[HC / 8][4];
 #pragma unroll
           for (int jj = 0; jj < HC / 8; ++jj) {
-            uint32_t wz[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const int i0 = jj * 8 + 2 * e;
               const uint32_t u2 = pack2<BF16>(__uint_as_float(ur[i0]), __uint_as_float(ur[i0 + 1]));
               const uint32_t v2 = pack2<BF16>(__uint_as_float(vr[i0]), __uint_as_float(vr[i0 + 1]));
-              wz[e] = silu_mul2<BF16>(u2, v2);
+              wz[jj][e] = silu_mul2<BF16>(u2, v2);
             }
-            *reinterpret_cast<uint4*>(sz + sw128_off(r, fo + cb + jj * 8, BM)) =
-                make_uint4(wz[0], wz[1], wz[2], wz[3]);
           }
+          // The previous pair's M_o (issued after its Y MMAs) has read the buffer.
+          if (fo == 0 && pc > 0) mbar_wait(bar_w, (pc - 1) & 1, sAbort);
+          unsigned char* sz = sm + C::O_ZP;
+#pragma unroll
+          for (int jj = 0; jj < HC / 8; ++jj)
+            *reinterpret_cast<uint4*>(sz + sw128_off(r, fo + cb + jj * 8, BM)) =
+                make_uint4(wz[jj][0], wz[jj][1], wz[jj][2], wz[jj][3]);
           if (fo + SC == 128) ++pc;
         }
         fence_proxy_async_smem();
