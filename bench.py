@@ -62,6 +62,7 @@ ROUTES = [("local", 0), ("shifted", 0), ("radix", 0), ("radix", 1), ("radix", 2)
 BATCH = 128
 G = 16
 METRIC = "BiGEMM TFLOP/s (fwd+bwd, bf16, operator sweep B=128)"
+_COMPUTE = {"bf16": torch.bfloat16, "fp32": torch.float32}
 REF_SITE = os.path.join(ROOT, "baseline", "_ref")
 
 
@@ -92,12 +93,27 @@ def _kernel_flops(name: str, b: int, h: int, w: int, c: int, d: int) -> float:
 
 
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu
-# capture of the same kernel and case (dram__bytes_read.sum +
-# dram__bytes_write.sum), keyed by (kernel, case, batch).
-_TRAFFIC = {
-    ("tc_bwd_kernel", "56x56x128/local0", 128): 1100.8e6,
-    ("tc_bwd_kernel", "14x14x512/local0", 128): 214.3e6,
-}
+# capture of that kernel and case (dram__bytes_read.sum +
+# dram__bytes_write.sum), keyed by (kernel, case, batch) and valid only for
+# the kernel sources they were measured on: SRC_DIGEST is the sha256 of the
+# library's CUDA sources at capture time, and a line whose sources differ
+# reports traffic null instead of a stale figure.
+SRC_DIGEST = "unset"
+_TRAFFIC: dict = {}
+
+
+def _src_digest() -> str:
+    import hashlib
+
+    h = hashlib.sha256()
+    csrc = os.path.join(ROOT, "omniwave_b200", "csrc")
+    for f in sorted(os.listdir(csrc)):
+        if f.endswith((".cu", ".cuh", ".h")):
+            with open(os.path.join(csrc, f), "rb") as fh:
+                h.update(f.encode() + b"\0" + fh.read())
+    with open(os.path.join(ROOT, "include", "omniwave_b200.h"), "rb") as fh:
+        h.update(fh.read())
+    return h.hexdigest()
 
 
 def fwd_bytes(b, h, w, c, elem=2) -> float:
@@ -116,19 +132,19 @@ def _dist():
     return world, rank, local
 
 
-def _make_case(h, w, c, d, route, level, batch, dev, seed):
+def _make_case(h, w, c, d, route, level, batch, dev, seed, dtype=torch.bfloat16):
     """Operator tensors in BASELINE config 2's order: seed, an fp32
     ``OmniWeaveBlock`` with default init (orthogonal A_u/A_v, identity A_o,
-    xavier B, gamma 1e-5), then x and dY ~ N(0,1), all cast to bf16
-    (scripts/benchmark.py:56-110)."""
+    xavier B, gamma 1e-5), then x and dY ~ N(0,1), all cast to ``dtype``
+    (bf16 as config 2; scripts/benchmark.py:56-110)."""
     from omniwave_b200 import OmniWeaveBlock
 
     torch.manual_seed(seed)
     blk = OmniWeaveBlock(h, w, c, d, route, level)
-    tensors = {k: getattr(blk, k).detach().to(dev, torch.bfloat16)
+    tensors = {k: getattr(blk, k).detach().to(dev, dtype)
                for k in ("a_u", "a_v", "a_o", "b_u", "b_v", "b_o", "gamma")}
-    tensors["x"] = torch.randn(batch, h, w, c, device=dev).to(torch.bfloat16)
-    dout = torch.randn(batch, h, w, c, device=dev).to(torch.bfloat16)
+    tensors["x"] = torch.randn(batch, h, w, c, device=dev).to(dtype)
+    dout = torch.randn(batch, h, w, c, device=dev).to(dtype)
     return blk.plan, tensors, dout
 
 
@@ -215,7 +231,8 @@ def run_ours(args) -> None:
         for ri, (route, lvl) in enumerate(ROUTES):
             if only is not None and f"{h}x{w}x{c}/{route}{lvl}" not in only:
                 continue
-            plan, tensors, dout = _make_case(h, w, c, d, route, lvl, batch, dev, seed=1 + 1000 * rank)
+            plan, tensors, dout = _make_case(h, w, c, d, route, lvl, batch, dev, seed=1 + 1000 * rank,
+                                             dtype=_COMPUTE[args.compute])
             leaves = {k: v.detach().requires_grad_(True) for k, v in tensors.items()}
             cases.append(dict(shape=(h, w, c, d), route=f"{route}{lvl}", plan=plan,
                               leaves=leaves, dout=dout))
@@ -300,8 +317,9 @@ def run_ours(args) -> None:
     (h, w, c, d), route = dom_key
     dom_flops = _kernel_flops(dom_name, batch, h, w, c, d)
     peaks = _peaks()
-    achieved = dom_flops / (dom_ms * 1e-3) / 1e12
-    traffic = _TRAFFIC.get((dom_name, f"{h}x{w}x{c}/{route}", batch))
+    # (The fp32 profiling mode runs no tensor-core kernel: no launch is timed.)
+    achieved = dom_flops / (dom_ms * 1e-3) / 1e12 if dom_ms > 1e-4 else 0.0
+    traffic = _TRAFFIC.get((dom_name, f"{h}x{w}x{c}/{route}", batch)) if _src_digest() == SRC_DIGEST else None
 
     # --- end-to-end through the public API with host buffers -----------------
     e2e = None if args.no_e2e else _e2e(args, cases, names, dev, world, sweep_flops)
@@ -330,7 +348,7 @@ def run_ours(args) -> None:
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": "bf16",
+            "dtype": args.compute,
             "data": "synthetic (seeded N(0,1) inputs and upstream grads, default-init weights)",
             "config": {
                 "workload": "bigemm_sweep_fwd_bwd",
@@ -578,7 +596,7 @@ def _model_bench(args, dev, world, rank, lib):
     model = create_model("omniweave_t", backend="cuda").to(dev)
     broadcast_parameters(model)
     model = model.to(torch.bfloat16).eval()
-    bi = 256
+    bi = args.model_batch or 256
     g = torch.Generator(device=dev).manual_seed(100 + rank)
     imgs = torch.randn(bi, 3, 224, 224, device=dev, generator=g, dtype=torch.bfloat16)
 
@@ -600,7 +618,7 @@ def _model_bench(args, dev, world, rank, lib):
     graph = world == 1 and not args.no_graph
     ts = TrainStep(model, lr=1e-3, weight_decay=0.05, amp_dtype=torch.bfloat16, cuda_graph=graph,
                    graph_warmup=2)
-    bt = 128
+    bt = args.model_batch or 128
     x = torch.randn(bt, 3, 224, 224, device=dev, generator=g)
     y = torch.randint(0, 1000, (bt,), device=dev, generator=g)
     launches0 = lib.ow_launch_count()
@@ -836,6 +854,10 @@ def main(argv=None) -> None:
     ap.add_argument("--no-graph", action="store_true", help="train step without CUDA-graph capture")
     ap.add_argument("--no-ref-gpu", action="store_true", help="skip timing the reference's own GPU paths")
     ap.add_argument("--model-only", action="store_true", help="profiling aid: only the OmniWeave-T legs")
+    ap.add_argument("--model-batch", type=int, default=0,
+                    help="profiling aid: images per GPU for both OmniWeave-T legs (default 256 / 128)")
+    ap.add_argument("--compute", choices=sorted(_COMPUTE), default="bf16",
+                    help="profiling aid: operator-sweep dtype (fp32 runs the CUDA-core kernels)")
     args = ap.parse_args(argv)
     if args.impl == "reference":
         run_reference(args)

@@ -3,12 +3,13 @@
 A drop-in ``cuda`` backend for the BiGEMM hot path of QuackPhuc/omniwave:
 route tables on the device, tile gathers folded into the kernels' loads,
 sm_100a kernels for the forward and backward, RMSNorm and residual fused in
-block mode.  The compute lives in ``libomniwave_b200.so`` (C ABI in
-``include/omniwave_b200.h``); this package is the host-side mirror of the
-reference's Python interface.  ``omniwave_b200.integration.install()`` plugs
-the backend into the reference package itself, so its own ``OmniWeaveBlock``,
-``OmniWeaveBackbone`` and training engine run on these kernels with
-``backend="cuda"``.
+block mode, and the backbone's stem and downsamples as fused space-to-depth
+GEMMs (``omniwave_b200.s2d``).  The compute lives in ``libomniwave_b200.so``
+(C ABI in ``include/omniwave_b200.h``); this package is the host-side mirror of
+the reference's Python interface.  ``omniwave_b200.integration.install()``
+plugs the backend into the reference package itself, so its own
+``OmniWeaveBlock``, ``OmniWeaveBackbone`` and training engine run on these
+kernels with ``backend="cuda"``.
 """
 
 from omniwave_b200.block import OmniWeaveBlock

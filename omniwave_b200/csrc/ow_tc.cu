@@ -381,7 +381,6 @@ tc_fwd_kernel(Prob p, const TX* __restrict__ x, const unsigned char* __restrict_
     }
   } else {
     // ------------------------------------------------ compute warps
-    const int tid = threadIdx.x;
     const int g = lane >> 2, t4 = lane & 3;
     uint32_t fo[4];  // A_o as an m16n8k16 A fragment
     load_afrag(amat + 512, false, g, t4, fo);

@@ -592,12 +592,6 @@ __device__ __forceinline__ void gram16(float (&acc)[2][4], LA lrow, RA rrow, int
   }
 }
 
-__device__ __forceinline__ float sigm_fast(float u) {
-  float t;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * u));
-  return fmaf(0.5f, t, 0.5f);
-}
-
 struct BwdArgs {
   Prob p;
   const void* x;
