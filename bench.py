@@ -93,27 +93,37 @@ def _kernel_flops(name: str, b: int, h: int, w: int, c: int, d: int) -> float:
 
 
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu
-# capture of that kernel and case (dram__bytes_read.sum +
-# dram__bytes_write.sum), keyed by (kernel, case, batch) and valid only for
-# the kernel sources they were measured on: SRC_DIGEST is the sha256 of the
-# library's CUDA sources at capture time, and a line whose sources differ
-# reports traffic null instead of a stale figure.
-SRC_DIGEST = "unset"
-_TRAFFIC: dict = {}
+# capture (dram__bytes_read.sum + dram__bytes_write.sum), keyed by (kernel,
+# case, batch), with the sha256 of the kernel's source file and the shared
+# headers at capture time: a line whose sources differ reports traffic null
+# instead of a stale figure.  The B=128 figure is the B=64 capture scaled by
+# the items processed (the role kernel's traffic is per item: operand images
+# in, dX out).
+_KERNEL_SRC = {"tc_bwd_kernel": "ow_tc_bwd.cu", "tc_pack_kernel": "ow_tc_bwd.cu", "tcf_kernel": "ow_tcf.cu",
+               "tc_fwd_kernel": "ow_tc.cu", "tc_fwd_gather_kernel": "ow_tcf.cu"}
+_TRAFFIC = {
+    ("tc_bwd_kernel", "56x56x128/radix1", 128): (2 * (540.913152e6 + 94.254336e6), "5268a930e947b307d2b09d60cee8494fe8c6c2d9e397bc72b79b69044ce2177f"),
+    ("tc_bwd_kernel", "56x56x128/local0", 128): (2 * (438.878208e6 + 46.275840e6), "5268a930e947b307d2b09d60cee8494fe8c6c2d9e397bc72b79b69044ce2177f"),
+}
 
 
-def _src_digest() -> str:
+def _src_digest(kernel: str) -> str:
     import hashlib
 
-    h = hashlib.sha256()
     csrc = os.path.join(ROOT, "omniwave_b200", "csrc")
-    for f in sorted(os.listdir(csrc)):
-        if f.endswith((".cu", ".cuh", ".h")):
-            with open(os.path.join(csrc, f), "rb") as fh:
-                h.update(f.encode() + b"\0" + fh.read())
-    with open(os.path.join(ROOT, "include", "omniwave_b200.h"), "rb") as fh:
-        h.update(fh.read())
+    files = [os.path.join(csrc, _KERNEL_SRC.get(kernel, "ow_api.cu"))]
+    files += sorted(os.path.join(csrc, f) for f in os.listdir(csrc) if f.endswith((".cuh", ".h")))
+    files.append(os.path.join(ROOT, "include", "omniwave_b200.h"))
+    h = hashlib.sha256()
+    for f in files:
+        with open(f, "rb") as fh:
+            h.update(os.path.basename(f).encode() + b"\0" + fh.read())
     return h.hexdigest()
+
+
+def _traffic(kernel: str, case: str, batch: int):
+    t = _TRAFFIC.get((kernel, case, batch))
+    return t[0] if t is not None and t[1] == _src_digest(kernel) else None
 
 
 def fwd_bytes(b, h, w, c, elem=2) -> float:
@@ -319,7 +329,7 @@ def run_ours(args) -> None:
     peaks = _peaks()
     # (The fp32 profiling mode runs no tensor-core kernel: no launch is timed.)
     achieved = dom_flops / (dom_ms * 1e-3) / 1e12 if dom_ms > 1e-4 else 0.0
-    traffic = _TRAFFIC.get((dom_name, f"{h}x{w}x{c}/{route}", batch)) if _src_digest() == SRC_DIGEST else None
+    traffic = _traffic(dom_name, f"{h}x{w}x{c}/{route}", batch)
 
     # --- end-to-end through the public API with host buffers -----------------
     e2e = None if args.no_e2e else _e2e(args, cases, names, dev, world, sweep_flops)
@@ -373,7 +383,8 @@ def run_ours(args) -> None:
                 "algorithmic_flops_per_launch": dom_flops,
                 "traffic": traffic,
                 "traffic_source": None if traffic is None else
-                "one ncu capture of this kernel and case (dram__bytes_read.sum + dram__bytes_write.sum)",
+                "ncu capture of this kernel and case at B=64 (dram__bytes_read.sum + dram__bytes_write.sum), "
+                "scaled by the items to B=128; same kernel sources",
             },
             "per_call_ms": {f"{k[0][0]}x{k[0][1]}x{k[0][2]}/{k[1]}": [round(v[0], 4), round(v[1], 4)]
                             for k, v in per.items()},

@@ -434,6 +434,63 @@ __global__ void rstd_kernel(const TX* __restrict__ x, int64_t rows, int C, doubl
   }
 }
 
+// Vectorised statistics: a row is ``lpr`` lanes (16 or 32) of 16-byte loads,
+// a warp covers 32 / lpr rows per step and RU steps per iteration, and every
+// lane issues all of its RU loads before it reduces any of them, so each lane
+// keeps RU loads in flight (one row per warp left rows of 256 B with a single
+// load per lane and the kernel latency-bound).  Same sum and rounding as
+// rstd_kernel; only the order of the double-precision partial sums differs.
+template <typename TX, typename TC>
+__device__ __forceinline__ double sumsq16(const uint4& u) {
+  const TX* e = reinterpret_cast<const TX*>(&u);
+  double a = 0;
+#pragma unroll
+  for (int k = 0; k < 16 / (int)sizeof(TX); ++k) {
+    const float v = Elem<TX>::to_f(e[k]);
+    a += (double)(v * v);
+  }
+  return a;
+}
+
+template <typename TX, typename TC>
+__global__ void __launch_bounds__(256) rstd_vec_kernel(const TX* __restrict__ x, int64_t rows, int C, double eps,
+                                                       int x_dt, TC* __restrict__ rstd, int lpr) {
+  constexpr int RU = 4;
+  constexpr int EV = 16 / (int)sizeof(TX);
+  const int lane = threadIdx.x & 31;
+  const int rpw = 32 / lpr, sub = lane / lpr, sl = lane % lpr;
+  const int vpr = C / EV;  // 16-byte vectors per row
+  const int64_t gw = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r0 = gw * rpw * RU; r0 < rows; r0 += nwarps * rpw * RU) {
+    double acc[RU];
+#pragma unroll
+    for (int u = 0; u < RU; ++u) acc[u] = 0;
+    for (int v0 = sl; v0 < vpr; v0 += lpr) {
+      uint4 q[RU];
+#pragma unroll
+      for (int u = 0; u < RU; ++u) {
+        const int64_t row = r0 + u * rpw + sub;
+        // Rows past the end load row 0 (always valid); their sums are dropped.
+        q[u] = __ldg(reinterpret_cast<const uint4*>(x + (row < rows ? row : 0) * C) + v0);
+      }
+#pragma unroll
+      for (int u = 0; u < RU; ++u) acc[u] += sumsq16<TX, TC>(q[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < RU; ++u) {
+      for (int o = lpr >> 1; o > 0; o >>= 1) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], o);
+      const int64_t row = r0 + u * rpw + sub;
+      if (sl == 0 && row < rows) {
+        float var32 = (float)(acc[u] / C);
+        TC v = round_through((TC)var32, x_dt);
+        v = round_through(v + (TC)eps, x_dt);
+        rstd[row] = round_through(TC(1) / sqrt(v), x_dt);
+      }
+    }
+  }
+}
+
 // One warp per row; lane l owns channels l, l+32, ... (J per lane, C <= 32*J).
 // The norm-weight gradient is accumulated per warp; when the block's eight
 // warp sums fit 32 KB of shared memory they are added in warp order and the
@@ -795,19 +852,33 @@ int norm_bwd_run(const NormBwd& nb, const void* x, int x_dt, const void* dout, i
 int rmsnorm_rstd(const void* x, int x_dtype, int compute_dtype, int64_t rows, int C, double eps,
                  void* rstd, void* stream) {
   cudaStream_t st = (cudaStream_t)stream;
+  const int es = (int)dtype_size(x_dtype);
+  const int vec = ((uintptr_t)x % 16 == 0) && (C * es % 16 == 0);
+  // Vectorised path: 16 lanes per row when a row is at most 16 vectors and
+  // that divides evenly, else 32.
+  const int vpr = vec ? C * es / 16 : 0;
+  const int lpr = vpr > 0 && vpr <= 16 && 16 % vpr == 0 ? 16 : 32;
+  const int64_t rows_per_block = 8LL * (32 / lpr) * 4;  // 8 warps x rows per step x 4 steps
+  const int vgrid = (int)std::max<int64_t>(1, std::min<int64_t>((rows + rows_per_block - 1) / rows_per_block,
+                                                                 (int64_t)device_sm_count() * 16));
   int grid = grid_for(rows * 32, 256, 148 * 16);
-  const int vec = ((uintptr_t)x % 16 == 0) && (C * (int)dtype_size(x_dtype) % 16 == 0);
   if (compute_dtype == OW_DTYPE_F64) {
     if (x_dtype != OW_DTYPE_F64) {
       set_error("rmsnorm: float64 compute needs float64 input");
       return OW_ERR_UNSUPPORTED;
     }
-    launch(rstd_kernel<double, double>, grid, 256, 0, st, (const double*)x, rows, C, eps, x_dtype, (double*)rstd, vec);
+    if (vec) launch(rstd_vec_kernel<double, double>, vgrid, 256, 0, st, (const double*)x, rows, C, eps, x_dtype, (double*)rstd, lpr);
+    else launch(rstd_kernel<double, double>, grid, 256, 0, st, (const double*)x, rows, C, eps, x_dtype, (double*)rstd, vec);
   } else {
+    auto go = [&](auto* tx) {
+      using TX = std::remove_pointer_t<decltype(tx)>;
+      if (vec) launch(rstd_vec_kernel<TX, float>, vgrid, 256, 0, st, (const TX*)x, rows, C, eps, x_dtype, (float*)rstd, lpr);
+      else launch(rstd_kernel<TX, float>, grid, 256, 0, st, (const TX*)x, rows, C, eps, x_dtype, (float*)rstd, vec);
+    };
     switch (x_dtype) {
-      case OW_DTYPE_F32: launch(rstd_kernel<float, float>, grid, 256, 0, st, (const float*)x, rows, C, eps, x_dtype, (float*)rstd, vec); break;
-      case OW_DTYPE_BF16: launch(rstd_kernel<__nv_bfloat16, float>, grid, 256, 0, st, (const __nv_bfloat16*)x, rows, C, eps, x_dtype, (float*)rstd, vec); break;
-      case OW_DTYPE_F16: launch(rstd_kernel<__half, float>, grid, 256, 0, st, (const __half*)x, rows, C, eps, x_dtype, (float*)rstd, vec); break;
+      case OW_DTYPE_F32: go((float*)nullptr); break;
+      case OW_DTYPE_BF16: go((__nv_bfloat16*)nullptr); break;
+      case OW_DTYPE_F16: go((__half*)nullptr); break;
       default:
         set_error("rmsnorm: unsupported input dtype %s", dtype_name(x_dtype));
         return OW_ERR_UNSUPPORTED;
