@@ -90,11 +90,11 @@ int rmsnorm_rstd(const void* x, int x_dtype, int compute_dtype, int64_t rows, in
 bool tc_supported(const ow_bigemm_args_t* a, const Prob& p, const char** why);
 // Forward with TMA row gathers and tensor-core token mixes (ow_tcf.cu): true
 // when it covers this call (contiguous channel groups, 16-bit x, operator
-// mode); tcf_forward() then runs it with the weight images the forward prep
-// kernel wrote (``img``, ``amat``, ``gg``, ``layout``).
+// or block mode); tcf_forward() then runs it with the weight images the forward prep
+// kernel wrote (``img``, ``amat``, ``gg``, ``nwc``, ``layout``).
 bool tcf_covers(const ow_bigemm_args_t* a, const Prob& p);
 int tcf_forward(const ow_bigemm_args_t* a, const Prob& p, const unsigned char* img, const uint16_t* amat,
-                const float* gg, const int* layout, void* stream);
+                const float* gg, const float* nwc, const int* layout, void* stream);
 int tc_forward(const ow_bigemm_args_t* a, const Prob& p, void* stream, Carver& ws);
 // The forward's pre-pass: [P_u | P_v] operand images per item (ow_tc_bwd.cu).
 int tc_pack_forward(const ow_bigemm_args_t* a, const Prob& p, const uint16_t* amat, const float* nwc,

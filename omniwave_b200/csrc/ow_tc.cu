@@ -698,7 +698,7 @@ int tc_forward_t(const ow_bigemm_args_t* a, const Prob& p, cudaStream_t st, Carv
     profile_mark(OW_PROF_FPACK, false, st);
     profile_mark(OW_PROF_FPACK, true, st);
     return tcf_forward(a, p, base + w.img, (const uint16_t*)(base + w.amat), (const float*)(base + w.gg),
-                       (const int*)(base + w.contig), st);
+                       (const float*)(base + w.nwc), (const int*)(base + w.contig), st);
   }
   profile_mark(OW_PROF_FPACK, false, st);
   OW_RETURN_IF((tc_pack_forward(a, p, (const uint16_t*)(base + w.amat), (const float*)(base + w.nwc),

@@ -1,6 +1,8 @@
 // Tensor-core BiGEMM forward with TMA row gathers and tcgen05 token mixes
 // (sm_100a; bf16/f16 compute; g = 16, d in {64, 128}, rd = 2d; channel
-// groups that are runs of d consecutive channels; operator mode).
+// groups that are runs of d consecutive channels; operator mode, and block
+// mode with a 16-bit x: RMSNorm applied to the gathered tile in shared
+// memory, the residual added in the epilogue).
 //
 // Work unit ("item"): one channel group q and an M-block of 128 token rows
 // (8 tiles of 16).  Per item (reference.py:147-171, with pack_tiles folded
@@ -77,8 +79,12 @@ struct FC {
   // keep their zero lines).  d = 128: the Y image overwrites the Z buffers
   // once the last Y MMA has read them, and the weights stream per chunk,
   // [B_u | B_v] through two stages and B_o through one.
+  // d = 64 double-buffers the T image, so the next item's rows land (and, in
+  // block mode, are normalised) while this item's image is still in use.
+  static constexpr int NTB = PAIR ? 2 : 1;
   static constexpr int OFF_T = 0;
-  static constexpr int OFF_PU = T_BYTES;
+  __host__ __device__ static constexpr int T_OFF(int b) { return OFF_T + b * T_BYTES; }
+  static constexpr int OFF_PU = NTB * T_BYTES;
   static constexpr int OFF_PV = OFF_PU + PI_BYTES;
   static constexpr int R_END = OFF_PV + PI_BYTES;
   static constexpr int OFF_Z = R_END;
@@ -90,8 +96,9 @@ struct FC {
   static constexpr int OFF_BUV = W_END;                               // mix B images (K-major, SW128)
   static constexpr int OFF_BO = OFF_BUV + 32 * 128;
   static constexpr int OFF_ROWS = OFF_BO + 16 * 128;                  // 2 x output row of each token row
-  static constexpr int OFF_BAR = OFF_ROWS + 2 * BM * 4;
-  static constexpr int NBAR = 22;
+  static constexpr int OFF_RS = OFF_ROWS + 2 * BM * 4;                // block mode: 2 x rstd of each token row
+  static constexpr int OFF_BAR = OFF_RS + 2 * BM * 4;
+  static constexpr int NBAR = 24;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
   // TMEM columns.
   static constexpr int T_PM = 0;                                 // P^T blocks (32 columns each)
@@ -145,16 +152,27 @@ __device__ __forceinline__ uint32_t img_off(int r, int c) {
   }
 }
 
-template <int D, bool BF16, typename TO>
+// Block mode (fused OmniWeaveBlock, reference block.py:80-108): the gathered
+// tile is RMS-normalised in shared memory, T = round(round(x rstd) nw) in x's
+// dtype, and the epilogue adds the residual, out = x + scale_b Delta.
+struct BlockArgs {
+  const float* rstd;  // [B N] per token row
+  const float* nw;    // [C] norm weight (f32 copy)
+  const void* x;      // the residual (x itself, in the 16-bit compute type)
+};
+
+template <int D, bool BF16, typename TO, bool RES>
 __global__ void __launch_bounds__(THREADS, 1)
 tcf_kernel(const __grid_constant__ CUtensorMap xmap, Prob p, const unsigned char* __restrict__ img,
            const uint16_t* __restrict__ amat, const float* __restrict__ gg, const int* __restrict__ layout,
-           const float* __restrict__ scale, TO* __restrict__ out, int* fault, uint32_t probe_ns) {
+           const float* __restrict__ scale, TO* __restrict__ out, BlockArgs blk, int* fault, uint32_t probe_ns) {
   using C = FC<D>;
+  using T16 = std::conditional_t<BF16, __nv_bfloat16, __half>;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
-  uint64_t* bar_t = bars + 0;       // T image gathered (tx)
+  // Per T buffer b (selects, not arrays: no local memory):
+  auto bar_t = [&](int b) { return b ? bars + 21 : bars + 0; };       // image gathered (tx)
   uint64_t* bar_pm = bars + 1;      // P^T mix done (commit)
   uint64_t* bar_p = bars + 2;       // P images written (compute)
   uint64_t* bar_uv = bars + 3;      // [2] U/V of TMEM buffer s computed (commit)
@@ -163,15 +181,17 @@ tcf_kernel(const __grid_constant__ CUtensorMap xmap, Prob p, const unsigned char
   uint64_t* bar_wuv = bars + 9;     // [2] d = 128: [B_u | B_v] stage loaded (tx); d = 64: group loaded (tx)
   uint64_t* bar_wo = bars + 11;     // d = 128: B_o stage loaded (tx)
   uint64_t* bar_wfree = bars + 13;  // d = 64: the resident group is no longer read (commit)
-  uint64_t* bar_rfree = bars + 14;  // the T image is read: the region may take the next item (commit)
+  auto bar_rfree = [&](int b) { return b ? bars + 22 : bars + 14; };  // image read: it may take the next item (commit)
   uint64_t* bar_y = bars + 15;      // Y of the item complete (commit)
   uint64_t* bar_yi = bars + 16;     // Y image written (compute)
   uint64_t* bar_dt = bars + 17;     // Delta^T mix done (commit)
   uint64_t* bar_epd = bars + 18;    // epilogue done: Delta^T columns read (compute)
   uint64_t* bar_probe = bars + 19;  // wait-timeout self-check: nothing arrives on it
+  auto bar_tn = [&](int b) { return b ? bars + 23 : bars + 20; };     // block mode: image normalised (producer, all lanes)
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + C::NBAR);
   volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
   int* sRows = reinterpret_cast<int*>(sm + C::OFF_ROWS);
+  float* sRs = reinterpret_cast<float*>(sm + C::OFF_RS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t BQ = (int64_t)p.B * p.Qs;
@@ -196,7 +216,7 @@ tcf_kernel(const __grid_constant__ CUtensorMap xmap, Prob p, const unsigned char
     for (int i = 0; i < C::NBAR; ++i) {
       const bool comp = bars + i == bar_p || bars + i == bar_yi || bars + i == bar_epd || bars + i == bar_z ||
                         bars + i == bar_z + 1;
-      mbar_init(bars + i, comp ? NCT : 1);
+      mbar_init(bars + i, comp ? NCT : (bars + i == bar_tn(0) || bars + i == bar_tn(1) ? 32 : 1));
     }
     *sAbort = 0;
     // The kernel covers channel groups that are one aligned run of d channels.
@@ -227,7 +247,8 @@ tcf_kernel(const __grid_constant__ CUtensorMap xmap, Prob p, const unsigned char
         const int kc = i & 7, ln16 = (i >> 3) & 15, j = (i >> 7) & 3, a = i >> 9;
         const int ln = 32 * j + (a == 0 ? 16 : 0) + ln16;
         const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-        *reinterpret_cast<uint4*>(sm + C::OFF_T + a * ATOM + line_chunk(ln, kc)) = z;
+#pragma unroll
+        for (int b = 0; b < C::NTB; ++b) *reinterpret_cast<uint4*>(sm + C::T_OFF(b) + a * ATOM + line_chunk(ln, kc)) = z;
         *reinterpret_cast<uint4*>(sm + C::OFF_Y + a * ATOM + line_chunk(ln, kc)) = z;
       }
     }
@@ -239,6 +260,42 @@ tcf_kernel(const __grid_constant__ CUtensorMap xmap, Prob p, const unsigned char
   tc_fence_after();
   const uint32_t tbase = *sTmem;
 
+  // Block mode: T <- round(round(T rstd[row]) nw[channel]) in place once the
+  // rows of item it have landed (pad rows are zero and have rstd 0), by one
+  // warp with all lanes: the weight warp at d = 64 (its weights are
+  // resident), the producer at d = 128.  The item's mix waits on bar_tn.
+  // Lane l always handles 16-byte chunk l % (D / 8) of its rows, so its eight
+  // norm-weight values are loaded once per item.
+  auto normalize = [&](int it) -> bool {
+    const int tb = it % C::NTB, tk = it / C::NTB;
+    constexpr int CPR = D / 8;  // 16-byte chunks per row
+    const int c = (lane % CPR) * 8;
+    const float* nwq = blk.nw + p.ch[qc_of(it) * D] + c;
+    const float4 n0 = __ldg(reinterpret_cast<const float4*>(nwq));
+    const float4 n1 = __ldg(reinterpret_cast<const float4*>(nwq + 4));
+    const float nv[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+    if (!mbar_wait(bar_t(tb), tk & 1, sAbort)) return false;
+    const float* srs = sRs + (it & 1) * BM;
+#pragma unroll 4
+    for (int row = lane / CPR; row < BM; row += 32 / CPR) {
+      const float rs = srs[row];
+      uint4* ptr = reinterpret_cast<uint4*>(sm + C::T_OFF(tb) + img_off<D>(row, c));
+      uint4 w = *ptr;
+      uint32_t* wp = &w.x;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        // x is in the compute type here, so both roundings go through it.
+        const float2 f = unpack2<BF16>(wp[e]);
+        const float2 t = unpack2<BF16>(pack2<BF16>(f.x * rs, f.y * rs));
+        wp[e] = pack2<BF16>(t.x * nv[2 * e], t.y * nv[2 * e + 1]);
+      }
+      *ptr = w;
+    }
+    fence_proxy_async_smem();
+    mbar_arrive(bar_tn(tb));
+    return true;
+  };
+
   if (*sAbort) {
     // The wait-timeout self-check ran out, or a group is not a channel run:
     // nothing is issued.
@@ -246,46 +303,70 @@ tcf_kernel(const __grid_constant__ CUtensorMap xmap, Prob p, const unsigned char
     // ------------------------------------------------ producer: TMA row gathers
     for (int it = 0; it < nit && !*sAbort; ++it) {
       const int qc = qc_of(it), mb = mb_of(it);
-      // The T region is free once the previous item's mix has read it.
-      if (it >= 1 && !mbar_wait(bar_rfree, (it - 1) & 1, sAbort)) break;
+      // Rows (and, in block mode, their RMS factors) are fetched before the
+      // wait for the T region, so their loads overlap it.
       int rw[4];
+      float rsv[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int r = row_of(mb, 4 * lane + j);
         rw[j] = r >= 0 ? r : oob;
+        if constexpr (RES) rsv[j] = r >= 0 ? blk.rstd[r] : 0.f;
       }
-      if (lane == 0) mbar_arrive_expect_tx(bar_t, BM * D * 2);
+      // T buffer tb is free once the mix of its previous item has read it.
+      const int tb = it % C::NTB, tk = it / C::NTB;
+      if (it >= C::NTB && !mbar_wait(bar_rfree(tb), (tk - 1) & 1, sAbort)) break;
+      if constexpr (RES) {
+        // Published to the compute warps by the arrive below (release) and
+        // the completion of bar_t (acquire).
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sRs[(it & 1) * BM + 4 * lane + j] = rsv[j];
+        __syncwarp();
+      }
+      if (lane == 0) mbar_arrive_expect_tx(bar_t(tb), BM * D * 2);
       __syncwarp();
       const int ch0 = p.ch[qc * D];  // first channel of the group's run
       if constexpr (C::PAIR) {
         const int t = lane >> 2;
-        const uint32_t dst = C::OFF_T + (t & 1) * ATOM + (32 * (t >> 1) + 16 * (t & 1) + 4 * (lane & 3)) * 128;
-        tma_gather4(sm + dst, &xmap, ch0, rw[0], rw[1], rw[2], rw[3], bar_t);
+        const uint32_t dst = C::T_OFF(tb) + (t & 1) * ATOM + (32 * (t >> 1) + 16 * (t & 1) + 4 * (lane & 3)) * 128;
+        tma_gather4(sm + dst, &xmap, ch0, rw[0], rw[1], rw[2], rw[3], bar_t(tb));
       } else {
 #pragma unroll
         for (int a = 0; a < 2; ++a)
-          tma_gather4(sm + C::OFF_T + a * ATOM + 4 * lane * 128, &xmap, ch0 + 64 * a, rw[0], rw[1], rw[2], rw[3],
-                      bar_t);
+          tma_gather4(sm + C::T_OFF(tb) + a * ATOM + 4 * lane * 128, &xmap, ch0 + 64 * a, rw[0], rw[1], rw[2],
+                      rw[3], bar_t(tb));
+      }
+      if constexpr (RES && !C::PAIR) {
+        if (!normalize(it)) break;
       }
     }
   } else if (warp == WGT_W) {
     // ------------------------------------------------ weight copies
-    if (lane == 0) {
-      int wq = -1, ge = 0;  // d = 64: resident group and number of group loads
+    if constexpr (C::PAIR) {
+      // d = 64: the group's weights, resident, reloaded when the group
+      // changes (lane 0); in block mode the warp also normalises each item.
+      int wq = -1, ge = 0;  // resident group and number of group loads
       for (int it = 0; it < nit && !*sAbort; ++it) {
         const int qc = qc_of(it);
-        if constexpr (C::PAIR) {
-          if (qc != wq) {
-            if (ge > 0 && !mbar_wait(bar_wfree, (ge - 1) & 1, sAbort)) break;
+        const bool newg = qc != wq;
+        bool ok = true;
+        if (lane == 0 && newg) {
+          if (ge > 0 && !mbar_wait(bar_wfree, (ge - 1) & 1, sAbort)) ok = false;
+          if (ok) {
             mbar_arrive_expect_tx(bar_wuv, C::NQ * C::IMG_BYTES);
             bulk_g2s(sm + C::OFF_W, img + (int64_t)qc * C::NQ * C::IMG_BYTES, C::NQ * C::IMG_BYTES, bar_wuv);
-            wq = qc;
-            ++ge;
           }
-        } else {
-          break;  // d = 128: the chunk stream below
+        }
+        if (newg) {
+          wq = qc;
+          ++ge;
+        }
+        if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+        if constexpr (RES) {
+          if (!normalize(it)) break;
         }
       }
+    } else if (lane == 0) {
       if constexpr (!C::PAIR) {
         // [B_u | B_v] of chunk c into stage c & 1 once U/V(c - 2) is done,
         // two chunks ahead; B_o into its single stage once Y(c - 1) is done.
@@ -336,11 +417,12 @@ tcf_kernel(const __grid_constant__ CUtensorMap xmap, Prob p, const unsigned char
       // item's Delta mix runs, and the next item's first U/V chunks run
       // while they store this item's outputs.
       auto item_mix = [&](int it) {
-        mbar_wait(bar_t, it & 1, sAbort);
+        const int tb = it % C::NTB, tk = it / C::NTB;
+        mbar_wait(RES ? bar_tn(tb) : bar_t(tb), tk & 1, sAbort);
         tc_fence_after();
-        if (!*sAbort) mix(s0 + C::OFF_T, C::T_PM, 32, dBUV, ID_MUV);
+        if (!*sAbort) mix(s0 + C::T_OFF(tb), C::T_PM, 32, dBUV, ID_MUV);
         umma_commit(bar_pm);
-        umma_commit(bar_rfree);  // the T image is read
+        umma_commit(bar_rfree(tb));  // the T image is read
       };
       if (nit > 0) item_mix(0);
       for (int it = 0; it < nit && !*sAbort; ++it) {
@@ -529,18 +611,38 @@ tcf_kernel(const __grid_constant__ CUtensorMap xmap, Prob p, const unsigned char
     // are whole row segments (D channels per row, 16 bytes per lane).  f32
     // outputs at d = 128 take two passes of 64 tokens.
     auto epilogue = [&](int it) {
+      const int qc = qc_of(it);
+      const int* rows = sRows + (it & 1) * BM;
+      const int c0ch = p.ch[qc * D];
+      // Block mode stages f32 so the residual add rounds once.
+      using TS = std::conditional_t<RES, float, TO>;
+      constexpr int STG_ROWS = (BM * D * (int)sizeof(TS) <= 2 * C::Z_BYTES) ? BM : BM / 2;
+      constexpr int NPASS = BM / STG_ROWS;
+      // Block mode: the residual x of every unit this thread stores (four
+      // channels each; rows < 0 load row 0 and store nothing), loaded before
+      // the wait for Delta so the loads overlap it.
+      constexpr int RVPR = D / 4;
+      constexpr int RNU = RES ? STG_ROWS * RVPR / NCT : 1;
+      static_assert(!RES || STG_ROWS * RVPR % NCT == 0, "whole units per thread");
+      uint2 xv[NPASS][RNU];
+      if constexpr (RES) {
+        const T16* xr = reinterpret_cast<const T16*>(blk.x);
+#pragma unroll
+        for (int pass = 0; pass < NPASS; ++pass)
+#pragma unroll
+          for (int j = 0; j < RNU; ++j) {
+            const int u = tid + j * NCT, rl = u / RVPR, vi = u - rl * RVPR;
+            const int rw = rows[pass * STG_ROWS + rl];
+            xv[pass][j] = __ldg(reinterpret_cast<const uint2*>(xr + (int64_t)(rw >= 0 ? rw : 0) * p.C + c0ch + vi * 4));
+          }
+      }
       mbar_wait(bar_dt, it & 1, sAbort);
       __syncwarp();
       tc_fence_after();
       if (*sAbort) return;
-      const int qc = qc_of(it);
-      const int* rows = sRows + (it & 1) * BM;
       const float gm = gg[(int64_t)qc * D + mc];
-      const int c0ch = p.ch[qc * D];
       constexpr int NCOL = C::PAIR ? 32 : 64;  // Delta^T columns of this warp half
-      constexpr int STG_ROWS = (BM * D * (int)sizeof(TO) <= 2 * C::Z_BYTES) ? BM : BM / 2;
-      constexpr int NPASS = BM / STG_ROWS;
-      TO* stg = reinterpret_cast<TO*>(sm + C::OFF_Z);  // [STG_ROWS][D]
+      TS* stg = reinterpret_cast<TS*>(sm + C::OFF_Z);  // [STG_ROWS][D]
       uint32_t v[NCOL];
 #pragma unroll
       for (int cc = 0; cc < NCOL; cc += 32) tmem_ld32(tq + C::T_DT + NCOL * half + cc, *reinterpret_cast<uint32_t(*)[32]>(v + cc));
@@ -562,25 +664,46 @@ tcf_kernel(const __grid_constant__ CUtensorMap xmap, Prob p, const unsigned char
             if (tok / STG_ROWS == pass) {
               const int rw = rows[tok];
               const float sc = rw >= 0 ? scale[rw / p.N] : 0.f;
-              stg[(tok % STG_ROWS) * D + mc] = Elem<TO>::from(__uint_as_float(v[k]) * gm * sc);
+              stg[(tok % STG_ROWS) * D + mc] = Elem<TS>::from(__uint_as_float(v[k]) * gm * sc);
             }
           }
         } else {
 #pragma unroll
           for (int k = 0; k < NCOL; ++k) {
             const int tok = tok_of(k);
-            if (tok / STG_ROWS == pass) stg[(tok % STG_ROWS) * D + mc] = Elem<TO>::from(__uint_as_float(v[k]) * gm);
+            if (tok / STG_ROWS == pass) stg[(tok % STG_ROWS) * D + mc] = Elem<TS>::from(__uint_as_float(v[k]) * gm);
           }
         }
         asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "memory");
-        // Row stores: 16 bytes per thread, consecutive threads along a row.
-        constexpr int VPR = D * (int)sizeof(TO) / 16;  // 16-byte vectors per row segment
-        for (int u = tid; u < STG_ROWS * VPR; u += NCT) {
-          const int rl = u / VPR, vi = u - rl * VPR;
-          const int rw = rows[pass * STG_ROWS + rl];
-          if (rw >= 0) {
-            const uint4 val = *reinterpret_cast<const uint4*>(stg + rl * D + vi * (16 / (int)sizeof(TO)));
-            *reinterpret_cast<uint4*>(out + (int64_t)rw * p.C + c0ch + vi * (16 / (int)sizeof(TO))) = val;
+        if constexpr (RES) {
+          // out = x + staged, four channels per unit.
+#pragma unroll
+          for (int j = 0; j < RNU; ++j) {
+            const int u = tid + j * NCT, rl = u / RVPR, vi = u - rl * RVPR;
+            const int rw = rows[pass * STG_ROWS + rl];
+            if (rw >= 0) {
+              const float4 sv = *reinterpret_cast<const float4*>(stg + rl * D + vi * 4);
+              const uint2 xw = pass == 0 ? xv[0][j] : xv[NPASS - 1][j];
+              const float2 x0 = unpack2<BF16>(xw.x), x1 = unpack2<BF16>(xw.y);
+              TO* o = out + (int64_t)rw * p.C + c0ch + vi * 4;
+              if constexpr (sizeof(TO) == 2) {
+                *reinterpret_cast<uint2*>(o) = make_uint2(pack2<BF16>(x0.x + sv.x, x0.y + sv.y),
+                                                          pack2<BF16>(x1.x + sv.z, x1.y + sv.w));
+              } else {
+                *reinterpret_cast<float4*>(o) = make_float4(x0.x + sv.x, x0.y + sv.y, x1.x + sv.z, x1.y + sv.w);
+              }
+            }
+          }
+        } else {
+          // Row stores: 16 bytes per thread, consecutive threads along a row.
+          constexpr int VPR = D * (int)sizeof(TO) / 16;  // 16-byte vectors per row segment
+          for (int u = tid; u < STG_ROWS * VPR; u += NCT) {
+            const int rl = u / VPR, vi = u - rl * VPR;
+            const int rw = rows[pass * STG_ROWS + rl];
+            if (rw >= 0) {
+              const uint4 val = *reinterpret_cast<const uint4*>(stg + rl * D + vi * (16 / (int)sizeof(TO)));
+              *reinterpret_cast<uint4*>(out + (int64_t)rw * p.C + c0ch + vi * (16 / (int)sizeof(TO))) = val;
+            }
           }
         }
         asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "memory");  // staging reused by the next pass / the gates
@@ -627,7 +750,7 @@ int make_xmap(CUtensorMap* map, const void* x, const Prob& p, bool bf16) {
 
 template <int D, bool BF16>
 int tcf_forward_t(const ow_bigemm_args_t* a, const Prob& p, const unsigned char* img, const uint16_t* amat,
-                  const float* gg, const int* layout, cudaStream_t st) {
+                  const float* gg, const float* nwc, const int* layout, cudaStream_t st) {
   CUtensorMap map;
   OW_RETURN_IF(make_xmap(&map, a->x, p, BF16));
   int* fault = nullptr;
@@ -635,9 +758,10 @@ int tcf_forward_t(const ow_bigemm_args_t* a, const Prob& p, const unsigned char*
   const int64_t items = (int64_t)p.Qc * ((p.BQ() + 7) / 8);
   const int grid = (int)std::min<int64_t>(items, device_sm_count());
   if (grid == 0) return OW_OK;
-  auto go = [&](auto* to) -> int {
+  const BlockArgs blk{(const float*)a->rstd, nwc, a->x};
+  auto go = [&](auto* to, auto res) -> int {
     using TO = std::remove_pointer_t<decltype(to)>;
-    auto kern = tcf_kernel<D, BF16, TO>;
+    auto kern = tcf_kernel<D, BF16, TO, decltype(res)::value>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FC<D>::SMEM);
     if (e != cudaSuccess) {
       set_error("tc forward: cannot reserve %d bytes of shared memory: %s", FC<D>::SMEM, cudaGetErrorString(e));
@@ -645,14 +769,15 @@ int tcf_forward_t(const ow_bigemm_args_t* a, const Prob& p, const unsigned char*
     }
     profile_mark(OW_PROF_FWD, false, st);
     launch(kern, grid, THREADS, FC<D>::SMEM, st, map, p, img, amat, gg, layout, a->sample_scale, (TO*)a->out,
-           fault, wait_probe_ns());
+           blk, fault, wait_probe_ns());
     profile_mark(OW_PROF_FWD, true, st);
     OW_CHECK_LAUNCH("tcf_kernel");
     return OW_OK;
   };
   using T16 = std::conditional_t<BF16, __nv_bfloat16, __half>;
-  if (a->out_dtype == (BF16 ? OW_DTYPE_BF16 : OW_DTYPE_F16)) return go((T16*)nullptr);
-  return go((float*)nullptr);
+  const bool o16 = a->out_dtype == (BF16 ? OW_DTYPE_BF16 : OW_DTYPE_F16);
+  if (a->rstd) return o16 ? go((T16*)nullptr, std::true_type{}) : go((float*)nullptr, std::true_type{});
+  return o16 ? go((T16*)nullptr, std::false_type{}) : go((float*)nullptr, std::false_type{});
 }
 
 }  // namespace
@@ -708,7 +833,8 @@ int encode_tiled_map(void* map, bool bf16, int rank, const void* base, const uin
 
 bool tcf_covers(const ow_bigemm_args_t* a, const Prob& p) {
   const int c16 = a->compute_dtype;
-  return (c16 == OW_DTYPE_BF16 || c16 == OW_DTYPE_F16) && a->x_dtype == c16 && !a->rstd && !a->residual &&
+  // Operator mode, or block mode (rstd given and the residual added).
+  return (c16 == OW_DTYPE_BF16 || c16 == OW_DTYPE_F16) && a->x_dtype == c16 && (!a->rstd) == (!a->residual) &&
          p.chs == 1 && (p.d == 64 || p.d == 128) && p.rd == 2 * p.d && p.C % 8 == 0 &&
          (uintptr_t)a->x % 16 == 0 && (uintptr_t)a->out % 16 == 0 &&
          (a->out_dtype == c16 || a->out_dtype == OW_DTYPE_F32) &&
@@ -716,14 +842,14 @@ bool tcf_covers(const ow_bigemm_args_t* a, const Prob& p) {
 }
 
 int tcf_forward(const ow_bigemm_args_t* a, const Prob& p, const unsigned char* img, const uint16_t* amat,
-                const float* gg, const int* layout, void* stream) {
+                const float* gg, const float* nwc, const int* layout, void* stream) {
   cudaStream_t st = (cudaStream_t)stream;
   const bool bf = a->compute_dtype == OW_DTYPE_BF16;
   if (p.d == 64)
-    return bf ? tcf_forward_t<64, true>(a, p, img, amat, gg, layout, st)
-              : tcf_forward_t<64, false>(a, p, img, amat, gg, layout, st);
-  return bf ? tcf_forward_t<128, true>(a, p, img, amat, gg, layout, st)
-            : tcf_forward_t<128, false>(a, p, img, amat, gg, layout, st);
+    return bf ? tcf_forward_t<64, true>(a, p, img, amat, gg, nwc, layout, st)
+              : tcf_forward_t<64, false>(a, p, img, amat, gg, nwc, layout, st);
+  return bf ? tcf_forward_t<128, true>(a, p, img, amat, gg, nwc, layout, st)
+            : tcf_forward_t<128, false>(a, p, img, amat, gg, nwc, layout, st);
 }
 
 }  // namespace ow
