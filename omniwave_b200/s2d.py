@@ -131,7 +131,9 @@ def s2d_linear_supported(x: Tensor, weight: Tensor, factor: int, nchw: bool = Fa
     return _shape_supported(x.device, tuple(x.shape), x.dtype, weight, factor, nchw, compute)
 
 
-def _fwd(x: Tensor, weight: Tensor, factor: int, nchw: bool, compute: torch.dtype) -> Tensor:
+def _fwd(x: Tensor, weight: Tensor, factor: int, nchw: bool,
+         compute: torch.dtype) -> tuple[Tensor, Tensor]:
+    """Runs the kernel; returns the output and x as the kernel read it."""
     lib = _lib.load()
     xk, wk = _kernel_dtypes(x.dtype, weight.dtype, nchw, compute)
     x = x.to(xk).contiguous()
@@ -152,7 +154,7 @@ def _fwd(x: Tensor, weight: Tensor, factor: int, nchw: bool, compute: torch.dtyp
     with torch.cuda.device(x.device):  # the library launches on the current device
         _lib.check(lib.ow_s2d_linear_fwd(args, stream), "ow_s2d_linear_fwd")
     del ws
-    return out
+    return out, x
 
 
 class _S2dLinear(torch.autograd.Function):
@@ -166,22 +168,28 @@ class _S2dLinear(torch.autograd.Function):
                 w_eff = w_a.detach().to(compute) @ wd.to(compute)
         else:
             w_eff = wd
-        out = _fwd(x.detach(), w_eff, factor, nchw, compute)
-        ctx.save_for_backward(x.detach(), wd, None if w_a is None else w_a.detach(), w_eff)
-        ctx.factor, ctx.nchw, ctx.compute = factor, nchw, compute
+        out, xk = _fwd(x.detach(), w_eff, factor, nchw, compute)
+        # The backward needs x in the compute type: a 16-bit copy made for the
+        # kernel is kept instead of x (half the bytes, no second cast).
+        ctx.save_for_backward(xk if xk.dtype == compute else x.detach(), wd,
+                              None if w_a is None else w_a.detach(), w_eff)
+        ctx.factor, ctx.nchw, ctx.compute, ctx.x_dtype = factor, nchw, compute, x.dtype
         return out
 
     @staticmethod
     def backward(ctx, dy):
         x, wd, wa, w_eff = ctx.saved_tensors
         return (*s2d_linear_backward(dy, x, wd, wa, w_eff, ctx.factor, ctx.nchw, ctx.compute,
-                                     ctx.needs_input_grad[:3]), None, None, None)
+                                     ctx.needs_input_grad[:3], ctx.x_dtype), None, None, None)
 
 
 def s2d_linear_backward(dy: Tensor, x: Tensor, wd: Tensor, wa: Tensor | None, w_eff: Tensor,
                         factor: int, nchw: bool, compute: torch.dtype,
-                        needs: tuple[bool, ...] = (True, True, True)):
+                        needs: tuple[bool, ...] = (True, True, True),
+                        x_dtype: torch.dtype | None = None):
     """Gradients ``(dx, dW_d, dW_a)`` of ``y = s2d(x) w_eff^T``, ``w_eff = W_a W_d``.
+
+    ``dx`` is returned in ``x_dtype`` (default: x's dtype).
 
     Every product is taken in ``compute`` (the forward's dtype, f32
     accumulation on the GPU), as the reference's autocast GEMMs take theirs:
@@ -197,9 +205,17 @@ def s2d_linear_backward(dy: Tensor, x: Tensor, wd: Tensor, wa: Tensor | None, w_
     dw_eff = dy2.t() @ a
     dx = dwd = dwa = None
     if needs[0]:
-        da = (dy2 @ w_eff.to(compute)).reshape(*dy.shape[:3], -1)
-        dxn = depth_to_space_nhwc(da, factor)
-        dx = (dxn.permute(0, 3, 1, 2) if nchw else dxn).to(x.dtype).contiguous()
+        b, ho, wo = dy.shape[:3]
+        f = factor
+        c = w_eff.shape[1] // (f * f)
+        da = (dy2 @ w_eff.to(compute)).view(b, ho, wo, f, f, c)  # [b, i, j, dy, dx, c]
+        # One copy: the inverse rearrangement and the cast in the same pass.
+        if nchw:
+            dx = torch.empty((b, c, ho * f, wo * f), dtype=x_dtype or x.dtype, device=da.device)
+            dx.view(b, c, ho, f, wo, f).copy_(da.permute(0, 5, 1, 3, 2, 4))
+        else:
+            dx = torch.empty((b, ho * f, wo * f, c), dtype=x_dtype or x.dtype, device=da.device)
+            dx.view(b, ho, f, wo, f, c).copy_(da.permute(0, 1, 3, 2, 4, 5))
     if wa is None:
         if needs[1]:
             dwd = dw_eff.to(wd.dtype)
