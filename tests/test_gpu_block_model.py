@@ -95,15 +95,17 @@ def test_block_autocast_bf16_drop_path(cuda_device):
     assert torch.equal(out[0], x[0])
 
 
+@pytest.mark.parametrize("shape", [(14, 14, 256, 128), (10, 10, 128, 64)], ids=["14x14x256-d128", "10x10x128-d64"])
 @pytest.mark.parametrize("route", [("shifted", 0), ("radix", 1)])
-def test_block_bf16_d128_scale_vs_oracle(cuda_device, route):
-    """bf16 residual stream at d = 128 (pad tokens at 14x14, RMSNorm in the
-    forward pre-pass, scale and residual in the epilogue) against the oracle
-    on the bf16-rounded operands."""
+def test_block_bf16_scale_vs_oracle(cuda_device, route, shape):
+    """bf16 residual stream (pad tokens, RMSNorm on the gathered tile --
+    contiguous groups in the TMA-gather forward, strided ones in the pre-pass --
+    scale and residual in the epilogue) against the oracle on the
+    bf16-rounded operands."""
     from omniwave_b200 import build_route_plan
     from omniwave_b200.ops import block_forward
 
-    h, w, c, d, b = 14, 14, 256, 128, 3
+    (h, w, c, d), b = shape, 3
     rng = np.random.default_rng(11)
     qc = c // d
 
