@@ -479,7 +479,7 @@ __device__ __forceinline__ void rows_store(const RowRegs<TS, NHF>& R, int h, int
 // L2), and each vector contributes its 8 / S elements of this group.  Same
 // arithmetic as rows_store: x mode round(round(v * rstd) * nw[c]), gradient
 // mode v * scale[b]; pad rows are zero.
-template <typename TS, bool BF16, int S>
+template <typename TS, bool BF16, int S, int UPP>
 __device__ __forceinline__ void gather_half_strided_t(const GatherCtx& gc, const TS* __restrict__ src, int hf,
                                                       bool xnorm, const float* __restrict__ rstd,
                                                       const float* __restrict__ nw, int x_dt,
@@ -488,7 +488,6 @@ __device__ __forceinline__ void gather_half_strided_t(const GatherCtx& gc, const
   constexpr int VW = sizeof(TS) == 2 ? 1 : 2;  // 16-byte vectors per 8 elements
   constexpr int VPR = 8 * S;                   // vectors of 8 elements per row span
   constexpr int UNITS = BM * VPR;              // 4 S units per thread
-  constexpr int UPP = 4;                       // units whose loads are in flight together
   const int c0 = gc.c0;
   const int64_t span0 = (int64_t)S * hf * 64;
 #pragma unroll 1
@@ -511,9 +510,11 @@ __device__ __forceinline__ void gather_half_strided_t(const GatherCtx& gc, const
       const int unit = u0 + j * NCOMP + tid;
       const int r = unit / VPR, vi = unit % VPR;
       const bool pad = gc.row[r] < 0;
+      constexpr int NT = 8 / S;  // this group's elements in the vector
+      float fv[NT];
 #pragma unroll
-      for (int t = 0; t < 8 / S; ++t) {
-        const int i = c0 + S * t;  // this group's elements of the vector
+      for (int t = 0; t < NT; ++t) {
+        const int i = c0 + S * t;
         const uint32_t w32 = (i >> 1) == 0 ? v[j][0].x : (i >> 1) == 1 ? v[j][0].y : (i >> 1) == 2 ? v[j][0].z : v[j][0].w;
         float f;
         if constexpr (sizeof(TS) == 2) {
@@ -524,29 +525,40 @@ __device__ __forceinline__ void gather_half_strided_t(const GatherCtx& gc, const
           const int e = i & 3;
           f = __uint_as_float(e == 0 ? q.x : e == 1 ? q.y : e == 2 ? q.z : q.w);
         }
-        const int k = vi * (8 / S) + t;
         if (xnorm) {
           f = round_through(f * rs[j], x_dt);
           f = round_through(f * nw[span0 + vi * 8 + i], x_dt);
         } else {
           f *= rs[j];
         }
-        const uint32_t pk = pack2<BF16>(pad ? 0.f : f, 0.f);
-        *reinterpret_cast<uint16_t*>(stg + (r * STG_LD + k) * 2) = (uint16_t)(pk & 0xFFFF);
+        fv[t] = pad ? 0.f : f;
+      }
+      // The NT consecutive k of this vector in one store (8, 4 or 2 bytes).
+      unsigned char* dst = stg + (r * STG_LD + vi * NT) * 2;
+      if constexpr (NT == 4) {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(pack2<BF16>(fv[0], fv[1]), pack2<BF16>(fv[2], fv[3]));
+      } else if constexpr (NT == 2) {
+        *reinterpret_cast<uint32_t*>(dst) = pack2<BF16>(fv[0], fv[1]);
+      } else {
+        *reinterpret_cast<uint16_t*>(dst) = (uint16_t)(pack2<BF16>(fv[0], 0.f) & 0xFFFF);
       }
     }
   }
 }
 
-template <typename TS, bool BF16>
+// Units per thread whose 16-byte loads are in flight together: eight for a
+// 16-bit source, except in the forward pre-pass at stride 2, whose smaller
+// CTAs run more per SM (measured faster with four); f32 sources four
+// (register budget).
+template <typename TS, bool BF16, bool FWD>
 __device__ __forceinline__ void gather_half_strided(const GatherCtx& gc, const TS* __restrict__ src, int hf,
                                                     bool xnorm, const float* __restrict__ rstd,
                                                     const float* __restrict__ nw, int x_dt,
                                                     const float* __restrict__ scale, unsigned char* stg, int tid) {
   switch (gc.stride) {
-    case 2: gather_half_strided_t<TS, BF16, 2>(gc, src, hf, xnorm, rstd, nw, x_dt, scale, stg, tid); break;
-    case 4: gather_half_strided_t<TS, BF16, 4>(gc, src, hf, xnorm, rstd, nw, x_dt, scale, stg, tid); break;
-    default: gather_half_strided_t<TS, BF16, 8>(gc, src, hf, xnorm, rstd, nw, x_dt, scale, stg, tid); break;
+    case 2: gather_half_strided_t<TS, BF16, 2, (sizeof(TS) == 2 && !FWD) ? 8 : 4>(gc, src, hf, xnorm, rstd, nw, x_dt, scale, stg, tid); break;
+    case 4: gather_half_strided_t<TS, BF16, 4, sizeof(TS) == 2 ? 8 : 4>(gc, src, hf, xnorm, rstd, nw, x_dt, scale, stg, tid); break;
+    default: gather_half_strided_t<TS, BF16, 8, sizeof(TS) == 2 ? 8 : 4>(gc, src, hf, xnorm, rstd, nw, x_dt, scale, stg, tid); break;
   }
 }
 
@@ -700,7 +712,7 @@ __global__ void __launch_bounds__(NCOMP) tc_pack_kernel(BwdArgs a) {
       if (!FWD) rows_issue<TO, 1>(rg, gc, dout, hf, nullptr, a.scale, tid);
       rows_store<TX, 1, BF16>(rx, 0, hf, gc, stg, false, a.rstd != nullptr, a.nw, nullptr, a.x_dt, tid);
     } else if (gc.stride) {
-      gather_half_strided<TX, BF16>(gc, x, hf, a.rstd != nullptr, a.rstd, a.nw, a.x_dt, nullptr, stg, tid);
+      gather_half_strided<TX, BF16, FWD>(gc, x, hf, a.rstd != nullptr, a.rstd, a.nw, a.x_dt, nullptr, stg, tid);
     } else {
       gather_half<TX, BF16>(gc, x, hf, a.rstd, a.nw, a.x_dt, nullptr, nullptr, stg, false, tid);
     }
@@ -723,7 +735,7 @@ __global__ void __launch_bounds__(NCOMP) tc_pack_kernel(BwdArgs a) {
     }
     if (FWD) continue;
     if (gc.cont) rows_store<TO, 1, BF16>(rg, 0, hf, gc, stg, false, false, nullptr, nullptr, 0, tid);
-    else if (gc.stride) gather_half_strided<TO, BF16>(gc, dout, hf, false, nullptr, nullptr, 0, a.scale, stg, tid);
+    else if (gc.stride) gather_half_strided<TO, BF16, FWD>(gc, dout, hf, false, nullptr, nullptr, 0, a.scale, stg, tid);
     else gather_half<TO, BF16>(gc, dout, hf, nullptr, nullptr, 0, a.scale, nullptr, stg, false, tid);
     atoms_free();
     to_atom(atom0);
