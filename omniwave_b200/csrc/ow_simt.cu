@@ -438,18 +438,30 @@ __global__ void rstd_kernel(const TX* __restrict__ x, int64_t rows, int C, doubl
 // a warp covers 32 / lpr rows per step and RU steps per iteration, and every
 // lane issues all of its RU loads before it reduces any of them, so each lane
 // keeps RU loads in flight (one row per warp left rows of 256 B with a single
-// load per lane and the kernel latency-bound).  Same sum and rounding as
-// rstd_kernel; only the order of the double-precision partial sums differs.
+// load per lane and the kernel latency-bound).  Same finishing steps as
+// rstd_kernel; each 16-byte vector's squares are summed in f32 (at most eight
+// terms), the rest in double.
 template <typename TX, typename TC>
 __device__ __forceinline__ double sumsq16(const uint4& u) {
   const TX* e = reinterpret_cast<const TX*>(&u);
-  double a = 0;
+  if constexpr (sizeof(TX) == 8) {
+    double a = 0;
 #pragma unroll
-  for (int k = 0; k < 16 / (int)sizeof(TX); ++k) {
-    const float v = Elem<TX>::to_f(e[k]);
-    a += (double)(v * v);
+    for (int k = 0; k < 2; ++k) {
+      const double v = (double)e[k];
+      a += v * v;
+    }
+    return a;
+  } else {
+    // The vector's (at most eight) squares in f32, then double from there on.
+    float a = 0.f;
+#pragma unroll
+    for (int k = 0; k < 16 / (int)sizeof(TX); ++k) {
+      const float v = Elem<TX>::to_f(e[k]);
+      a = fmaf(v, v, a);
+    }
+    return (double)a;
   }
-  return a;
 }
 
 template <typename TX, typename TC>
