@@ -42,7 +42,7 @@
 extern "C" {
 #endif
 
-#define OW_ABI_VERSION 3
+#define OW_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define OW_API __attribute__((visibility("default")))
@@ -289,6 +289,47 @@ typedef struct ow_s2d_linear_t {
 /* Workspace bytes ow_s2d_linear_fwd needs (0 if the arguments are unsupported). */
 OW_API size_t ow_s2d_linear_workspace_size(const ow_s2d_linear_t* args);
 OW_API int ow_s2d_linear_fwd(const ow_s2d_linear_t* args, void* stream);
+
+/*
+ * Global average pool + classifier head, the backbone's tail
+ * (omniweave/models/backbone.py:193-197: ``pooled = stage4.mean(dim=(1, 2))``
+ * then ``self.head(pooled)``, an ``nn.Linear`` with bias), as one kernel in
+ * which the pooled matrix feeds the tensor-core GEMM from shared memory:
+ *
+ *   pooled[b, c] = round(sum_t x[b, t, c] / tokens)                 (f32 sum)
+ *   out[b, n]    = round(bias[n] + sum_c weight[n, c] pooled[b, c])  (f32 acc)
+ *
+ * round() is to ``compute_dtype`` (bf16 or f16), which is also the dtype of
+ * ``out`` [batch, classes] and of ``pooled`` [batch, channels] (written only
+ * when non-NULL; the head's backward needs it), as under the reference's
+ * autocast, where the f32 mean, weight and bias are cast before the GEMM.
+ * x is [batch, tokens, channels] (the NHWC stage-4 map, f32 or compute_dtype);
+ * weight [classes, channels] f32 or compute_dtype; bias [classes] (f32, bf16
+ * or f16; rounded to compute_dtype) or NULL.  Supported: channels a multiple
+ * of 512 up to 2048 and classes up to 1024; x, weight and pooled 16-byte
+ * aligned.  Anything else returns OW_ERR_UNSUPPORTED.  Results are bitwise
+ * reproducible (fixed summation order).
+ */
+typedef struct ow_pool_head_t {
+  const void* x;
+  int32_t x_dtype;
+  int32_t batch, tokens, channels;
+  const void* weight;
+  int32_t w_dtype;
+  const void* bias;
+  int32_t bias_dtype;
+  int32_t classes;
+  int32_t compute_dtype;
+  void* out;
+  void* pooled;
+  void* workspace;         /* ow_pool_head_workspace_size() bytes */
+  size_t workspace_bytes;
+} ow_pool_head_t;
+
+/* Workspace bytes ow_pool_head_fwd needs (0 if the arguments are
+ * unsupported): 256, plus room for the converted weight when weight is f32. */
+OW_API size_t ow_pool_head_workspace_size(const ow_pool_head_t* args);
+OW_API int ow_pool_head_fwd(const ow_pool_head_t* args, void* stream);
 
 #ifdef __cplusplus
 }

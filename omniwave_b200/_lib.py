@@ -16,7 +16,7 @@ import torch
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_PKG, "libomniwave_b200.so")
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 DTYPE_CODE = {
     torch.float32: 0,
@@ -74,6 +74,18 @@ class S2dLinear(ctypes.Structure):
     ]
 
 
+class PoolHead(ctypes.Structure):
+    _fields_ = [
+        ("x", _vp), ("x_dtype", _c_i32),
+        ("batch", _c_i32), ("tokens", _c_i32), ("channels", _c_i32),
+        ("weight", _vp), ("w_dtype", _c_i32),
+        ("bias", _vp), ("bias_dtype", _c_i32),
+        ("classes", _c_i32), ("compute_dtype", _c_i32),
+        ("out", _vp), ("pooled", _vp),
+        ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
 LAYOUT_NHWC = 0
 LAYOUT_NCHW = 1
 
@@ -83,6 +95,7 @@ EXPORTS = (
     "ow_rmsnorm_rstd", "ow_bigemm_fwd", "ow_bigemm_bwd", "ow_bigemm_fwd_noalloc",
     "ow_noalloc_scratch_limit", "ow_profile_events", "ow_debug_wait_probe",
     "ow_s2d_linear_workspace_size", "ow_s2d_linear_fwd",
+    "ow_pool_head_workspace_size", "ow_pool_head_fwd",
 )
 
 _lock = threading.Lock()
@@ -133,6 +146,10 @@ def load() -> ctypes.CDLL:
         lib.ow_s2d_linear_workspace_size.restype = ctypes.c_size_t
         lib.ow_s2d_linear_fwd.argtypes = [ctypes.POINTER(S2dLinear), _vp]
         lib.ow_s2d_linear_fwd.restype = ctypes.c_int
+        lib.ow_pool_head_workspace_size.argtypes = [ctypes.POINTER(PoolHead)]
+        lib.ow_pool_head_workspace_size.restype = ctypes.c_size_t
+        lib.ow_pool_head_fwd.argtypes = [ctypes.POINTER(PoolHead), _vp]
+        lib.ow_pool_head_fwd.restype = ctypes.c_int
         v = lib.ow_abi_version()
         if v != ABI_VERSION:
             raise NativeLibraryError(f"ABI version mismatch: library {v}, binding {ABI_VERSION}")

@@ -23,6 +23,10 @@ training engine -- run on the B200 kernels when built with
   space-to-depth GEMMs, each stage anchor folded into the GEMM before it
   (``omniwave_b200.s2d``), when the compute dtype is 16-bit and the kernels
   take the shapes; otherwise the reference method runs.
+* ``OmniWeaveBackbone.forward`` (backbone.py:190-197) of such a model on a GPU
+  runs the global average pool and the classifier head as one kernel
+  (``omniwave_b200.head``) under the same conditions; otherwise the
+  reference's ``head(stage4.mean(dim=(1, 2)))``.
 
 Parameter names, shapes and initialisation are the reference's own (nothing
 here constructs parameters), so state dicts interchange by construction.
@@ -36,7 +40,7 @@ from typing import Any
 
 from torch import Tensor
 
-from omniwave_b200 import ops, s2d
+from omniwave_b200 import head, ops, s2d
 
 __all__ = ["install", "installed", "uses_cuda"]
 
@@ -86,6 +90,7 @@ def install() -> Any:
         ref_bigemm = ob.bigemm
         ref_block_forward = mb.OmniWeaveBlock.forward
         ref_forward_features = mbb.OmniWeaveBackbone.forward_features
+        ref_forward = mbb.OmniWeaveBackbone.forward
 
         def select_backend(x, requested, support_check):
             """dispatch.py:13-49 with ``"cuda"`` added to the valid names."""
@@ -123,11 +128,21 @@ def install() -> Any:
                 return s2d.forward_features(self, x)
             return ref_forward_features(self, x)
 
+        def forward(self, x: Tensor) -> Tensor:
+            """backbone.py:191-197 with the pool and the head fused on the cuda backend."""
+            if not (x.is_cuda and uses_cuda(self)):
+                return ref_forward(self, x)
+            stage4 = self.forward_features(x)["stage4"]
+            if head.head_supported(self, stage4)[0]:
+                return head.pool_head(stage4, self.head.weight, self.head.bias)
+            return self.head(stage4.mean(dim=(1, 2)))
+
         od.select_backend = select_backend
         ob.bigemm = bigemm
         mb.bigemm = bigemm
         mb.OmniWeaveBlock.forward = block_forward
         mbb.OmniWeaveBackbone.forward_features = forward_features
+        mbb.OmniWeaveBackbone.forward = forward
         setattr(ob, _MARK, True)
         return pkg
 
