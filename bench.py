@@ -649,7 +649,58 @@ def _model_bench(args, dev, world, rank, lib):
         "inside one CUDA graph per step (launch counter counts host-side launches only)")
     del ts, model, x, y
     torch.cuda.empty_cache()
+    if world == 1:
+        out["pool_head"] = _head_bench(dev)
     return out
+
+
+def _head_bench(dev):
+    """The model's tail, ``head(stage4.mean(dim=(1, 2)))``, at the two model
+    workloads: the fused pool + head kernel (``omniwave_b200.head``) against
+    PyTorch's mean + ``nn.Linear`` (cuBLAS).  Device time per call from a
+    CUDA graph of eight calls on eight different inputs (205 MB > L2)."""
+    from omniwave_b200 import head
+
+    def graph_us(fns, reps=20):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for f in fns:
+                f()
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for f in fns:
+                f()
+        for _ in range(3):
+            g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / reps / len(fns)
+        del g
+        return round(us, 2)
+
+    res = {"timing": "device time per call, CUDA graph of 8 calls on 8 inputs (> L2)"}
+    gen = torch.Generator(device=dev).manual_seed(7)
+    for name, b, xdt, amp in (("infer_b256_bf16", 256, torch.bfloat16, False),
+                              ("train_b128_f32_autocast", 128, torch.float32, True)):
+        xs = [torch.randn(b, 7, 7, 1024, device=dev, generator=gen).to(xdt) for _ in range(8)]
+        lin = torch.nn.Linear(1024, 1000).to(dev)
+        if not amp:
+            lin = lin.to(xdt)
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16, enabled=amp):
+            fused = graph_us([lambda x=x: head.pool_head(x, lin.weight, lin.bias) for x in xs])
+            ref = graph_us([lambda x=x: lin(x.mean(dim=(1, 2))) for x in xs])
+        res[name] = {"fused_us": fused, "torch_mean_linear_us": ref,
+                     "fused_gbs": round(xs[0].numel() * xs[0].element_size() / (fused * 1e-6) / 1e9, 1)}
+        del xs, lin
+    torch.cuda.empty_cache()
+    return res
 
 
 def _peaks():
