@@ -2,8 +2,8 @@
 
 omniwave_b200 is a drop-in backend for the BiGEMM operator of
 QuackPhuc/omniwave (package ``omniweave``).  ``install()`` applies, at run
-time, the same small patch a maintainer would make to the reference sources
-(the source form is in INTEGRATION.md); after it the reference's own modules
+time, the same small patch a maintainer would make to the reference sources;
+after it the reference's own modules
 -- ``OmniWeaveBlock``, ``OmniWeaveBackbone``, ``create_model`` and the
 training engine -- run on the B200 kernels when built with
 ``backend="cuda"`` (or ``"auto"`` on a supported GPU), unchanged otherwise:
