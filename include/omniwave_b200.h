@@ -42,7 +42,7 @@
 extern "C" {
 #endif
 
-#define OW_ABI_VERSION 4
+#define OW_ABI_VERSION 5
 
 #if defined(__GNUC__)
 #define OW_API __attribute__((visibility("default")))
@@ -289,6 +289,42 @@ typedef struct ow_s2d_linear_t {
 /* Workspace bytes ow_s2d_linear_fwd needs (0 if the arguments are unsupported). */
 OW_API size_t ow_s2d_linear_workspace_size(const ow_s2d_linear_t* args);
 OW_API int ow_s2d_linear_fwd(const ow_s2d_linear_t* args, void* stream);
+
+/*
+ * Linear followed by depth-to-space, the input gradient of the downsample
+ * above: the autograd of ``Linear(space_to_depth_nhwc(x, f))``
+ * (omniweave/models/backbone.py:14-27, :128-132) with respect to x, without
+ * the rearranged intermediate:
+ *
+ *   out[b, f i + dy, f j + dx, c] = sum_n y[b, i, j, n] * weight[n, (dy f + dx) C + c]
+ *
+ * y is NHWC [batch, height/factor, width/factor, in_features] (bf16 or f16,
+ * the compute type: products in it, f32 accumulation); weight
+ * [in_features, factor^2 channels] row-major (f32 or y's dtype; the folded
+ * anchor weight W_a W_d where there is one); out NHWC
+ * [batch, height, width, channels] in out_dtype: y's dtype, or f32 holding
+ * the values rounded to y's dtype (as autocast's backward casts the 16-bit
+ * input gradient to an f32 input's dtype).
+ * Supported: channels and in_features multiples of 64, factor^2 channels a
+ * multiple of 256, width/factor <= 128; y and out 16-byte aligned.  Anything
+ * else returns OW_ERR_UNSUPPORTED.
+ */
+typedef struct ow_d2s_linear_t {
+  const void* y;
+  int32_t y_dtype;
+  int32_t batch, height, width, channels, factor;   /* of the output image */
+  int32_t in_features;
+  const void* weight;
+  int32_t w_dtype;
+  void* out;
+  int32_t out_dtype;
+  void* workspace;         /* ow_d2s_linear_workspace_size() bytes */
+  size_t workspace_bytes;
+} ow_d2s_linear_t;
+
+/* Workspace bytes ow_d2s_linear_fwd needs (0 if the arguments are unsupported). */
+OW_API size_t ow_d2s_linear_workspace_size(const ow_d2s_linear_t* args);
+OW_API int ow_d2s_linear_fwd(const ow_d2s_linear_t* args, void* stream);
 
 /*
  * Global average pool + classifier head, the backbone's tail

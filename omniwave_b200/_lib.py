@@ -16,7 +16,7 @@ import torch
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_PKG, "libomniwave_b200.so")
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 DTYPE_CODE = {
     torch.float32: 0,
@@ -74,6 +74,17 @@ class S2dLinear(ctypes.Structure):
     ]
 
 
+class D2sLinear(ctypes.Structure):
+    _fields_ = [
+        ("y", _vp), ("y_dtype", _c_i32),
+        ("batch", _c_i32), ("height", _c_i32), ("width", _c_i32), ("channels", _c_i32),
+        ("factor", _c_i32), ("in_features", _c_i32),
+        ("weight", _vp), ("w_dtype", _c_i32),
+        ("out", _vp), ("out_dtype", _c_i32),
+        ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
 class PoolHead(ctypes.Structure):
     _fields_ = [
         ("x", _vp), ("x_dtype", _c_i32),
@@ -96,6 +107,7 @@ EXPORTS = (
     "ow_noalloc_scratch_limit", "ow_profile_events", "ow_debug_wait_probe",
     "ow_s2d_linear_workspace_size", "ow_s2d_linear_fwd",
     "ow_pool_head_workspace_size", "ow_pool_head_fwd",
+    "ow_d2s_linear_workspace_size", "ow_d2s_linear_fwd",
 )
 
 _lock = threading.Lock()
@@ -150,6 +162,10 @@ def load() -> ctypes.CDLL:
         lib.ow_pool_head_workspace_size.restype = ctypes.c_size_t
         lib.ow_pool_head_fwd.argtypes = [ctypes.POINTER(PoolHead), _vp]
         lib.ow_pool_head_fwd.restype = ctypes.c_int
+        lib.ow_d2s_linear_workspace_size.argtypes = [ctypes.POINTER(D2sLinear)]
+        lib.ow_d2s_linear_workspace_size.restype = ctypes.c_size_t
+        lib.ow_d2s_linear_fwd.argtypes = [ctypes.POINTER(D2sLinear), _vp]
+        lib.ow_d2s_linear_fwd.restype = ctypes.c_int
         v = lib.ow_abi_version()
         if v != ABI_VERSION:
             raise NativeLibraryError(f"ABI version mismatch: library {v}, binding {ABI_VERSION}")

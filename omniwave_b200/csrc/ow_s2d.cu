@@ -20,6 +20,13 @@
 //   loads (4 dx values of one (c, dy) each), rounding f32 to the compute
 //   type as autocast does; the weight images stay resident.
 //
+// * depth-to-space (the input gradient of the downsample): the same
+//   pipeline with A = the gradient rows y [B Ho Wo, N] (a 3-D TMA box of R
+//   whole rows) and the weight read transposed, so the GEMM produces
+//   s2d-ordered features k = (dy, dx, c); the epilogue stores every
+//   32-feature chunk (one (dy, dx) block, 32 channels) at its place in the
+//   NHWC image [B, f Ho, f Wo, C], in f32 or the compute type.
+//
 // Weights go through a prep kernel into pre-swizzled K-major images of the
 // compute type (128 or 256 features x 64 K).  The epilogue converts the f32
 // accumulator to the compute type and leaves through a per-warp staging
@@ -84,6 +91,7 @@ struct S2dArgs {
   int N;
   const unsigned char* wimg;  // [NT][KC] images of SN x 64 (SW128 K-major)
   void* out;
+  int oC, oW;            // depth-to-space output: channels and width (f Wo) of the image
   int* fault;
   uint32_t probe_ns;
 };
@@ -98,56 +106,123 @@ __device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// 3-D TMA tile load into shared memory, completing on ``bar``.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Weight images: W[n, k] -> image (n / SN, k / 64), row n % SN, column
 // k % 64, SW128 K-major, in the compute type; columns k >= K are zero.
-template <typename TW, typename T16, int SN>
+// TR: the weight is stored transposed, W[n, k] at w[k N + n].
+template <typename TW, typename T16, int SN, bool TR = false>
 __global__ void s2d_wprep_kernel(const TW* __restrict__ w, int N, int K, int KC, unsigned char* __restrict__ img) {
   const int64_t total = (int64_t)N * KC * KE;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int n = (int)(i / (KC * KE)), k = (int)(i - (int64_t)n * KC * KE);
-    const float v = k < K ? load_as<float>(w, (int64_t)n * K + k) : 0.f;
+    const float v = k < K ? load_as<float>(w, TR ? (int64_t)k * N + n : (int64_t)n * K + k) : 0.f;
     unsigned char* base = img + ((int64_t)(n / SN) * KC + k / KE) * (SN * 128);
     *reinterpret_cast<T16*>(base + sw128_off(n % SN, k % KE, SN)) = Elem<T16>::from(v);
   }
 }
 
+// Output modes of the epilogue: OUT_ROWS writes tile row m as out row m (the
+// compute type); OUT_D2S16 / OUT_D2S32 write feature k = (dy, dx, c) of row
+// m = (b, i, j) to pixel (b, f i + dy, f j + dx), channel c of an NHWC image
+// with oC channels and width oW (depth-to-space), in the compute type or as
+// f32 holding the compute-type rounding (what the reference's autocast
+// backward produces: a 16-bit GEMM output cast to the f32 input's dtype).
+constexpr int OUT_ROWS = 0, OUT_D2S16 = 1, OUT_D2S32 = 2;
+
 // Epilogue of one tile for the calling warp.  A warp may only read the TMEM
 // lane quarter q = (warp id) % 4, which holds tile rows 32 q .. 32 q + 31.
 // Per 32-feature chunk the warp converts its 32 x 32 block, stages it in
 // ``stg`` (16-byte units rotated by the row pair, conflict free both ways)
-// and stores 8 rows x 64 bytes per instruction.
-template <int SN, bool BF16>
+// and stores 8 rows x 64 bytes per instruction (f32: the chunk in two
+// 16-feature halves).
+template <int SN, bool BF16, int OM>
 __device__ __forceinline__ void epilogue_tile(uint32_t tacc, unsigned char* stg, const S2dArgs& a, int64_t mrow0,
                                               int ncol0) {
   using T16 = std::conditional_t<BF16, __nv_bfloat16, __half>;
   const int lane = threadIdx.x & 31, q = (threadIdx.x >> 5) & 3;
-  T16* out = reinterpret_cast<T16*>(a.out);
+  // Element offset of the start of each row this lane stores (it = 0..3),
+  // -1 for rows past the tile or the matrix.  Depth-to-space: tile row r is
+  // output row (mrow0 / Wo + r / Wo, r % Wo) of y, i.e. pixel
+  // (f (mrow0 / Wo + r / Wo), f (r % Wo)) before the (dy, dx) of the chunk.
+  int64_t rowoff[4];
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int r = q * 32 + it * 8 + (lane >> 2);
+    const int64_t m = mrow0 + r;
+    if (r >= a.MT || m >= a.M) {
+      rowoff[it] = -1;
+    } else if constexpr (OM == OUT_ROWS) {
+      rowoff[it] = m * a.N;
+    } else {
+      const int io = r / a.Wo, j = r - io * a.Wo;
+      const int64_t bi = mrow0 / a.Wo + io;
+      rowoff[it] = (bi * a.f * a.oW + (int64_t)a.f * j) * a.oC;
+    }
+  }
 #pragma unroll 1
   for (int cb = 0; cb < SN / 32; ++cb) {
     uint32_t v[32];
     tmem_ld32(tacc + ((uint32_t)(q * 32) << 16) + cb * 32, v);
     tmem_ld_wait();
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      uint4 o;
-      o.x = pack2<BF16>(__uint_as_float(v[8 * u + 0]), __uint_as_float(v[8 * u + 1]));
-      o.y = pack2<BF16>(__uint_as_float(v[8 * u + 2]), __uint_as_float(v[8 * u + 3]));
-      o.z = pack2<BF16>(__uint_as_float(v[8 * u + 4]), __uint_as_float(v[8 * u + 5]));
-      o.w = pack2<BF16>(__uint_as_float(v[8 * u + 6]), __uint_as_float(v[8 * u + 7]));
-      *reinterpret_cast<uint4*>(stg + lane * 64 + ((u ^ ((lane >> 1) & 3)) << 4)) = o;
+    // Offset of the chunk's first feature inside a row (depth-to-space: the
+    // chunk is 32 channels of one (dy, dx) block).
+    int64_t coff = ncol0 + cb * 32;
+    if constexpr (OM != OUT_ROWS) {
+      const int k0 = ncol0 + cb * 32, blk = k0 / a.oC, c0 = k0 - blk * a.oC;
+      const int dy = blk / a.f, dx = blk - dy * a.f;
+      coff = ((int64_t)dy * a.oW + dx) * a.oC + c0;
     }
-    __syncwarp();
+    if constexpr (OM == OUT_D2S32) {
+      float* out = reinterpret_cast<float*>(a.out);
 #pragma unroll
-    for (int it = 0; it < 4; ++it) {
-      const int row = it * 8 + (lane >> 2), pc = lane & 3;
-      const int r = q * 32 + row;
-      const uint4 o = *reinterpret_cast<const uint4*>(stg + row * 64 + ((pc ^ ((row >> 1) & 3)) << 4));
-      const int64_t m = mrow0 + r;
-      if (r < a.MT && m < a.M)
-        *reinterpret_cast<uint4*>(out + m * a.N + ncol0 + cb * 32 + pc * 8) = o;
+      for (int h = 0; h < 2; ++h) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          auto rd = [&](int i) {
+            return __float_as_uint(Elem<T16>::to_f(Elem<T16>::from(__uint_as_float(v[16 * h + 4 * u + i]))));
+          };
+          const uint4 o = make_uint4(rd(0), rd(1), rd(2), rd(3));
+          *reinterpret_cast<uint4*>(stg + lane * 64 + ((u ^ ((lane >> 1) & 3)) << 4)) = o;
+        }
+        __syncwarp();
+#pragma unroll
+        for (int it = 0; it < 4; ++it) {
+          const int row = it * 8 + (lane >> 2), pc = lane & 3;
+          const uint4 o = *reinterpret_cast<const uint4*>(stg + row * 64 + ((pc ^ ((row >> 1) & 3)) << 4));
+          if (rowoff[it] >= 0) *reinterpret_cast<uint4*>(out + rowoff[it] + coff + 16 * h + pc * 4) = o;
+        }
+        __syncwarp();
+      }
+    } else {
+      T16* out = reinterpret_cast<T16*>(a.out);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        uint4 o;
+        o.x = pack2<BF16>(__uint_as_float(v[8 * u + 0]), __uint_as_float(v[8 * u + 1]));
+        o.y = pack2<BF16>(__uint_as_float(v[8 * u + 2]), __uint_as_float(v[8 * u + 3]));
+        o.z = pack2<BF16>(__uint_as_float(v[8 * u + 4]), __uint_as_float(v[8 * u + 5]));
+        o.w = pack2<BF16>(__uint_as_float(v[8 * u + 6]), __uint_as_float(v[8 * u + 7]));
+        *reinterpret_cast<uint4*>(stg + lane * 64 + ((u ^ ((lane >> 1) & 3)) << 4)) = o;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int row = it * 8 + (lane >> 2), pc = lane & 3;
+        const uint4 o = *reinterpret_cast<const uint4*>(stg + row * 64 + ((pc ^ ((row >> 1) & 3)) << 4));
+        if (rowoff[it] >= 0) *reinterpret_cast<uint4*>(out + rowoff[it] + coff + pc * 8) = o;
+      }
+      __syncwarp();
     }
-    __syncwarp();
   }
 }
 
@@ -187,7 +262,7 @@ __device__ __forceinline__ void mma_loop(unsigned char* sm, uint64_t* full, uint
   }
 }
 
-template <class K, bool BF16>
+template <class K, bool BF16, int OM = OUT_ROWS>
 __device__ __forceinline__ void epilogue_loop(unsigned char* sm, uint64_t* tfull, uint64_t* tfree, uint32_t tbase,
                                               const S2dArgs& a, int ntiles, volatile int* abort) {
   const int w = (threadIdx.x >> 5) - K::EPI_W;
@@ -199,7 +274,7 @@ __device__ __forceinline__ void epilogue_loop(unsigned char* sm, uint64_t* tfull
     __syncwarp();
     tc_fence_after();
     const int mt = t / a.NT, nt = t % a.NT;
-    epilogue_tile<K::SN, BF16>(tbase + acc * K::SN, stg, a, (int64_t)mt * a.MT, nt * K::SN);
+    epilogue_tile<K::SN, BF16, OM>(tbase + acc * K::SN, stg, a, (int64_t)mt * a.MT, nt * K::SN);
     tc_fence_before();
     mbar_arrive(tfree + acc);
   }
@@ -270,7 +345,10 @@ __device__ __forceinline__ void teardown(const Bars& B, uint32_t tbase, int* fau
 }
 
 // ---------------------------------------------------------------- downsample
-template <int SN, bool BF16>
+// OM == OUT_ROWS: the downsample, A rows through the 5-D box over x.
+// Depth-to-space modes: A = the gradient rows y through a 3-D box
+// {64, Wo, R} over y viewed as [B Ho, Wo, K] (the same R whole rows).
+template <int SN, bool BF16, int OM = OUT_ROWS>
 __global__ void __launch_bounds__(SC<false, SN>::THREADS, 1)
     s2d_ds_kernel(const __grid_constant__ CUtensorMap xmap, S2dArgs a) {
   using K = SC<false, SN>;
@@ -294,9 +372,13 @@ __global__ void __launch_bounds__(SC<false, SN>::THREADS, 1)
           const int s = g % STAGES;
           if (g >= STAGES && !mbar_wait(B.empty + s, ((g / STAGES) - 1) & 1, B.abort)) break;
           const int k0 = kc * KE;
-          const int dy = k0 / (a.f * a.C), dx = (k0 / a.C) % a.f, c0 = k0 % a.C;
           mbar_arrive_expect_tx(B.full + s, bytes);
-          tma_load_5d(sm + K::OFF_A + s * A_ST, &xmap, c0, dx, 0, dy, mt * a.R, B.full + s);
+          if constexpr (OM == OUT_ROWS) {
+            const int dy = k0 / (a.f * a.C), dx = (k0 / a.C) % a.f, c0 = k0 % a.C;
+            tma_load_5d(sm + K::OFF_A + s * A_ST, &xmap, c0, dx, 0, dy, mt * a.R, B.full + s);
+          } else {
+            tma_load_3d(sm + K::OFF_A + s * A_ST, &xmap, k0, 0, mt * a.R, B.full + s);
+          }
           bulk_g2s(sm + K::OFF_B + s * K::B_ST, a.wimg + ((int64_t)nt * a.KC + kc) * K::B_ST, K::B_ST, B.full + s);
         }
       }
@@ -304,7 +386,7 @@ __global__ void __launch_bounds__(SC<false, SN>::THREADS, 1)
   } else if (warp == K::MMA_W) {
     if (lane == 0) mma_loop<K, BF16>(sm, B.full, B.empty, B.tfull, B.tfree, B.w, tbase, a, ntiles, B.abort);
   } else {
-    epilogue_loop<K, BF16>(sm, B.tfull, B.tfree, tbase, a, ntiles, B.abort);
+    epilogue_loop<K, BF16, OM>(sm, B.tfull, B.tfree, tbase, a, ntiles, B.abort);
   }
   teardown<K>(B, tbase, a.fault);
 }
@@ -427,6 +509,29 @@ size_t wimg_bytes(const ow_s2d_linear_t* a) {
   const int K = a->factor * a->factor * a->channels;
   const int KC = (K + KE - 1) / KE;
   return (size_t)a->out_features * KC * KE * 2;
+}
+
+int d2s_check(const ow_d2s_linear_t* a, const char** why) {
+  auto no = [&](const char* m) {
+    if (why) *why = m;
+    return OW_ERR_UNSUPPORTED;
+  };
+  if (!a) return no("args is NULL");
+  if (a->batch <= 0 || a->height <= 0 || a->width <= 0 || a->channels <= 0 || a->factor <= 0 ||
+      a->in_features <= 0)
+    return no("batch, height, width, channels, factor and in_features must be positive");
+  if (a->height % a->factor || a->width % a->factor) return no("height and width must be divisible by factor");
+  if (!is16(a->y_dtype)) return no("y dtype must be bfloat16 or float16");
+  if (a->w_dtype != OW_DTYPE_F32 && a->w_dtype != a->y_dtype) return no("weight dtype must be float32 or y's dtype");
+  if (a->out_dtype != OW_DTYPE_F32 && a->out_dtype != a->y_dtype) return no("out dtype must be float32 or y's dtype");
+  if (a->channels % KE) return no("channels must be a multiple of 64");
+  if (a->in_features % KE) return no("in_features must be a multiple of 64");
+  if ((int64_t)a->factor * a->factor * a->channels % 256) return no("factor^2 * channels must be a multiple of 256");
+  if (a->width / a->factor > TM) return no("width / factor must be at most 128");
+  if ((int64_t)a->batch * a->height * a->width * a->channels >= (1LL << 40)) return no("out too large");
+  if ((int64_t)a->batch * (a->height / a->factor) * (a->width / a->factor) >= (1LL << 31) - TM)
+    return no("too many rows");
+  return OW_OK;
 }
 
 }  // namespace
@@ -556,6 +661,118 @@ int ow_s2d_linear_fwd(const ow_s2d_linear_t* a, void* stream) {
               : go(s2d_ds_kernel<128, false>, K128::SMEM, K128::THREADS);
   return bf ? go(s2d_ds_kernel<256, true>, K256::SMEM, K256::THREADS)
             : go(s2d_ds_kernel<256, false>, K256::SMEM, K256::THREADS);
+}
+
+size_t ow_d2s_linear_workspace_size(const ow_d2s_linear_t* a) {
+  if (d2s_check(a, nullptr) != OW_OK) return 0;
+  const size_t nf = (size_t)a->factor * a->factor * a->channels;
+  return nf * (size_t)a->in_features * 2 + 256;
+}
+
+int ow_d2s_linear_fwd(const ow_d2s_linear_t* a, void* stream) {
+  clear_error();
+  const char* why = nullptr;
+  if (d2s_check(a, &why) != OW_OK) {
+    set_error("ow_d2s_linear_fwd: %s", why);
+    return OW_ERR_UNSUPPORTED;
+  }
+  OW_CHECK_ARG(a->y && a->weight && a->out, "ow_d2s_linear_fwd: a pointer is NULL");
+  OW_CHECK_ARG((uintptr_t)a->y % 16 == 0 && (uintptr_t)a->out % 16 == 0,
+               "ow_d2s_linear_fwd: y and out must be 16-byte aligned");
+  const size_t need = ow_d2s_linear_workspace_size(a);
+  if (!a->workspace || a->workspace_bytes < need) {
+    set_error("ow_d2s_linear_fwd needs %zu workspace bytes, got %zu", need, a->workspace_bytes);
+    return OW_ERR_WORKSPACE;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool bf = a->y_dtype == OW_DTYPE_BF16;
+  const int f = a->factor;
+  S2dArgs k{};
+  k.x = a->y;
+  k.B = a->batch;
+  k.H = a->height;
+  k.W = a->width;
+  k.f = f;
+  k.C = a->in_features;
+  k.Ho = a->height / f;
+  k.Wo = a->width / f;
+  k.M = (int64_t)k.B * k.Ho * k.Wo;
+  k.N = f * f * a->channels;               // s2d-ordered features (dy, dx, c)
+  k.KC = a->in_features / KE;
+  k.R = TM / k.Wo;
+  k.MT = k.R * k.Wo;
+  k.mtiles = (int)(((int64_t)k.B * k.Ho + k.R - 1) / k.R);
+  k.oC = a->channels;
+  k.oW = a->width;
+  const int sms = device_sm_count();
+  auto fill = [&](int w) {
+    const int64_t t = (int64_t)k.mtiles * (k.N / w);
+    return (double)t / (double)(((t + sms - 1) / sms) * sms);
+  };
+  const int sn = fill(128) > fill(256) + 0.25 ? 128 : 256;
+  k.NT = k.N / sn;
+  unsigned char* img = (unsigned char*)(((uintptr_t)a->workspace + 255) & ~(uintptr_t)255);
+  k.wimg = img;
+  k.out = a->out;
+  OW_RETURN_IF(fault_word(&k.fault));
+  k.probe_ns = wait_probe_ns();
+
+  {  // weight images of W^T: feature k' = (dy, dx, c), K = the input feature n
+    const int64_t nw = (int64_t)k.N * k.KC * KE;
+    const int pg = (int)std::min<int64_t>((nw + 255) / 256, (int64_t)sms * 8);
+    auto prep = [&](auto* tw, auto* t16) {
+      using TW = std::remove_pointer_t<decltype(tw)>;
+      using T16 = std::remove_pointer_t<decltype(t16)>;
+      if (sn == 128)
+        launch(s2d_wprep_kernel<TW, T16, 128, true>, pg, 256, 0, st, (const TW*)a->weight, k.N, a->in_features,
+               k.KC, img);
+      else
+        launch(s2d_wprep_kernel<TW, T16, 256, true>, pg, 256, 0, st, (const TW*)a->weight, k.N, a->in_features,
+               k.KC, img);
+    };
+    if (bf) {
+      if (a->w_dtype == OW_DTYPE_F32) prep((float*)nullptr, (__nv_bfloat16*)nullptr);
+      else prep((__nv_bfloat16*)nullptr, (__nv_bfloat16*)nullptr);
+    } else {
+      if (a->w_dtype == OW_DTYPE_F32) prep((float*)nullptr, (__half*)nullptr);
+      else prep((__half*)nullptr, (__half*)nullptr);
+    }
+    OW_CHECK_LAUNCH("s2d_wprep_kernel");
+  }
+  const int ntiles = k.mtiles * k.NT;
+  const int grid = std::min(ntiles, sms);
+  if (grid <= 0) return OW_OK;
+
+  // y viewed as [B Ho, Wo, K], listed innermost first
+  CUtensorMap map;
+  const uint64_t K = (uint64_t)a->in_features;
+  const uint64_t dims[3] = {K, (uint64_t)k.Wo, (uint64_t)k.B * k.Ho};
+  const uint64_t strides[2] = {K * 2, (uint64_t)k.Wo * K * 2};
+  const uint32_t box[3] = {(uint32_t)KE, (uint32_t)k.Wo, (uint32_t)k.R};
+  OW_RETURN_IF(encode_tiled_map(&map, bf, 3, a->y, dims, strides, box, "d2s linear"));
+  auto go = [&](auto kern, int smem, int threads) -> int {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) {
+      set_error("d2s linear: cannot reserve %d bytes of shared memory: %s", smem, cudaGetErrorString(e));
+      return OW_ERR_CUDA;
+    }
+    launch(kern, grid, threads, smem, st, map, k);
+    OW_CHECK_LAUNCH("s2d_ds_kernel (depth-to-space)");
+    return OW_OK;
+  };
+  using K128 = SC<false, 128>;
+  using K256 = SC<false, 256>;
+  const bool o32 = a->out_dtype == OW_DTYPE_F32;
+  if (sn == 128) {
+    if (bf) return o32 ? go(s2d_ds_kernel<128, true, OUT_D2S32>, K128::SMEM, K128::THREADS)
+                       : go(s2d_ds_kernel<128, true, OUT_D2S16>, K128::SMEM, K128::THREADS);
+    return o32 ? go(s2d_ds_kernel<128, false, OUT_D2S32>, K128::SMEM, K128::THREADS)
+               : go(s2d_ds_kernel<128, false, OUT_D2S16>, K128::SMEM, K128::THREADS);
+  }
+  if (bf) return o32 ? go(s2d_ds_kernel<256, true, OUT_D2S32>, K256::SMEM, K256::THREADS)
+                     : go(s2d_ds_kernel<256, true, OUT_D2S16>, K256::SMEM, K256::THREADS);
+  return o32 ? go(s2d_ds_kernel<256, false, OUT_D2S32>, K256::SMEM, K256::THREADS)
+             : go(s2d_ds_kernel<256, false, OUT_D2S16>, K256::SMEM, K256::THREADS);
 }
 
 }  // extern "C"

@@ -14,9 +14,11 @@ space-to-depth projection that feeds its stage, so it is folded into that
 GEMM: ``y = s2d(x) (W_a W_d)^T``, the product of the two 16-bit weights
 formed once per call.  The backward recovers both weight
 gradients from the gradient of the folded weight
-``dW = dy^T s2d(x)``: ``dW_a = dW W_d^T``, ``dW_d = W_a^T dW``, and the input
-gradient from ``dy (W_a W_d)`` with the space-to-depth inverted.  The backward
-runs on PyTorch GEMMs.
+``dW = dy^T s2d(x)``: ``dW_a = dW W_d^T``, ``dW_d = W_a^T dW`` (PyTorch
+GEMMs), and the input gradient from ``dy (W_a W_d)`` with the space-to-depth
+inverted: for the downsamples one kernel (``ow_d2s_linear_fwd``) whose
+epilogue stores each output chunk at its place in the NHWC image, so neither
+the GEMM's output nor a rearranging copy goes through memory.
 
 The fused path takes 16-bit compute (autocast bf16/f16, or a 16-bit model),
 which is how the reference trains; float32 compute stays on the reference
@@ -38,6 +40,7 @@ __all__ = [
     "depth_to_space_nhwc",
     "s2d_linear",
     "s2d_linear_backward",
+    "d2s_linear",
     "s2d_linear_supported",
     "forward_features",
     "features_supported",
@@ -204,7 +207,10 @@ def s2d_linear_backward(dy: Tensor, x: Tensor, wd: Tensor, wa: Tensor | None, w_
     acc = compute
     dw_eff = dy2.t() @ a
     dx = dwd = dwa = None
-    if needs[0]:
+    if needs[0] and not nchw and _d2s_supported(dy, w_eff, factor, x_dtype or x.dtype)[0]:
+        # one kernel: the GEMM stores through the inverse rearrangement
+        dx = _d2s(dy, w_eff, factor, x_dtype or x.dtype)
+    elif needs[0]:
         b, ho, wo = dy.shape[:3]
         f = factor
         c = w_eff.shape[1] // (f * f)
@@ -225,6 +231,75 @@ def s2d_linear_backward(dy: Tensor, x: Tensor, wd: Tensor, wa: Tensor | None, w_
         if needs[2]:
             dwa = (dw_eff @ wd.to(acc).t()).to(wa.dtype)
     return dx, dwd, dwa
+
+
+def _d2s_args(y: Tensor | None, shape: tuple[int, int, int, int], y_dtype: torch.dtype, weight: Tensor,
+              factor: int, out: Tensor | None, out_dtype: torch.dtype) -> _lib.D2sLinear:
+    b, ho, wo, n = shape
+    c = weight.shape[1] // (factor * factor)
+    return _lib.D2sLinear(
+        _lib.ptr(y), _lib.DTYPE_CODE.get(y_dtype, -1), b, ho * factor, wo * factor, c, factor, n,
+        _lib.ptr(weight), _lib.DTYPE_CODE.get(weight.dtype, -1),
+        _lib.ptr(out), _lib.DTYPE_CODE.get(out_dtype, -1), None, 0,
+    )
+
+
+def _d2s_supported(y: Tensor, weight: Tensor, factor: int,
+                   out_dtype: torch.dtype) -> tuple[bool, str | None]:
+    if y.device.type != "cuda":
+        return False, "CUDA is unavailable"
+    if y.dim() != 4 or weight.dim() != 2 or weight.shape[0] != y.shape[3]:
+        return False, "y must be [B, Ho, Wo, N] and the weight [N, f^2 C]"
+    if weight.shape[1] % (factor * factor):
+        return False, "weight columns must be a multiple of factor^2"
+    if weight.dtype not in (torch.float32, y.dtype):
+        return False, f"weight dtype {weight.dtype} is neither float32 nor y's dtype"
+    try:
+        lib = _lib.load()
+    except _lib.NativeLibraryError as exc:
+        return False, str(exc)
+    idx = y.device.index if y.device.index is not None else torch.cuda.current_device()
+    if not lib.ow_device_supported(idx):
+        return False, f"device {idx} is not sm_100 (B200-class)"
+    args = _d2s_args(None, tuple(y.shape), y.dtype, weight, factor, None, out_dtype)
+    args.weight = None  # a size query reads no pointer
+    if lib.ow_d2s_linear_workspace_size(args) == 0:
+        return False, "shape or dtype not supported by ow_d2s_linear_fwd"
+    return True, None
+
+
+def _d2s(y: Tensor, weight: Tensor, factor: int, out_dtype: torch.dtype) -> Tensor:
+    lib = _lib.load()
+    y = y.contiguous()
+    weight = weight.contiguous()
+    b, ho, wo, _ = y.shape
+    c = weight.shape[1] // (factor * factor)
+    out = torch.empty((b, ho * factor, wo * factor, c), dtype=out_dtype, device=y.device)
+    args = _d2s_args(y, tuple(y.shape), y.dtype, weight, factor, out, out_dtype)
+    n = lib.ow_d2s_linear_workspace_size(args)
+    ws = torch.empty(max(n, 1), dtype=torch.uint8, device=y.device)
+    args.workspace, args.workspace_bytes = ws.data_ptr(), n
+    with torch.cuda.device(y.device):  # the library launches on the current device
+        _lib.check(lib.ow_d2s_linear_fwd(args, _lib.stream_handle(y.device)), "ow_d2s_linear_fwd")
+    del ws
+    return out
+
+
+def d2s_linear(y: Tensor, weight: Tensor, factor: int, out_dtype: torch.dtype | None = None) -> Tensor:
+    """``depth_to_space_nhwc(y @ weight, factor)`` as one kernel (``ow_d2s_linear_fwd``).
+
+    The input gradient of the downsample ``Linear(space_to_depth_nhwc(x))``
+    (backbone.py:14-27, :128-132): ``y`` is the 16-bit gradient
+    ``[B, Ho, Wo, N]``, ``weight`` the projection's ``[N, f^2 C]`` (f32 or
+    y's dtype); the result is ``[B, f Ho, f Wo, C]`` in ``out_dtype`` (y's
+    dtype by default, or float32 holding the values rounded to y's dtype).
+    Raises ``RuntimeError`` when the kernel does not support the arguments.
+    """
+    out_dtype = out_dtype or y.dtype
+    ok, why = _d2s_supported(y, weight, factor, out_dtype)
+    if not ok:
+        raise RuntimeError(f"d2s_linear not supported: {why}")
+    return _d2s(y, weight, factor, out_dtype)
 
 
 def s2d_linear(x: Tensor, weight: Tensor, factor: int, *, nchw: bool = False,

@@ -94,6 +94,32 @@ def test_stem_with_identity_weight_is_the_rearrangement(cuda_device):
     assert not out[..., 48:].any()
 
 
+@pytest.mark.parametrize("b,h,c,n,dtype,odt", [
+    (2, 56, 128, 256, torch.bfloat16, torch.float32),    # downsample 1's input gradient, f32 stream
+    (3, 28, 256, 512, torch.bfloat16, torch.float32),    # downsample 2, partial last tile
+    (5, 14, 512, 1024, torch.bfloat16, torch.bfloat16),  # downsample 3, 16-bit out
+    (1, 256, 64, 256, torch.bfloat16, torch.float32),    # W / f = 128: one row per tile
+    (3, 28, 128, 256, torch.float16, torch.float16),
+], ids=["ds1-f32", "ds2-partial", "ds3-bf16", "wo128", "f16"])
+def test_depth_to_space_linear_matches_exact(cuda_device, b, h, c, n, dtype, odt):
+    """depth_to_space(y W) against float64 from the same rounded operands:
+    within 1.5 ulp of the compute dtype (f32 out holds the compute-type
+    rounding, as the reference's autocast backward does)."""
+    g = torch.Generator(device=cuda_device).manual_seed(4)
+    y = torch.randn(b, h // 2, h // 2, n, device=cuda_device, generator=g).to(dtype)
+    w = torch.randn(n, 4 * c, device=cuda_device, generator=g) * n ** -0.5
+    out = s2d.d2s_linear(y, w, 2, out_dtype=odt)
+    assert out.dtype == odt and out.shape == (b, h, h, c)
+    exact = s2d.depth_to_space_nhwc(y.double() @ w.to(dtype).double(), 2)
+    _check_ulp(out, exact, dtype)
+    if odt == torch.float32:  # exactly the compute-type values
+        assert torch.equal(out, out.to(dtype).float())
+    # the downsample backward takes it and agrees with the PyTorch path
+    x = torch.randn(b, h, h, c, device=cuda_device, generator=g)
+    dx, _, _ = s2d.s2d_linear_backward(y, x, w, None, w, 2, False, dtype, (True, False, False), odt)
+    assert torch.equal(dx, out.to(odt))
+
+
 def test_anchor_fold_matches_two_linears(cuda_device):
     g = torch.Generator(device=cuda_device).manual_seed(2)
     x = torch.randn(4, 28, 28, 256, device=cuda_device, generator=g).bfloat16()

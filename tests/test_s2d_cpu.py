@@ -79,3 +79,32 @@ def test_installed_forward_features_keeps_the_reference_path_on_the_host(omniwea
 def test_s2d_linear_refuses_host_tensors():
     with pytest.raises(RuntimeError, match="CUDA is unavailable"):
         s2d.s2d_linear(torch.zeros(1, 4, 4, 64), torch.zeros(256, 256), 2)
+
+
+def test_d2s_linear_validation_without_gpu():
+    """The depth-to-space entry point sizes and refuses without touching CUDA."""
+    import ctypes
+
+    from omniwave_b200 import _lib
+
+    lib = _lib.load()
+    F32, BF16, F16 = 0, 2, 3
+
+    def args(**over):
+        a = _lib.D2sLinear(None, BF16, 2, 56, 56, 128, 2, 256, None, BF16, None, F32, None, 0)
+        for k, v in over.items():
+            setattr(a, k, v)
+        return a
+
+    assert lib.ow_d2s_linear_workspace_size(ctypes.byref(args())) == 512 * 256 * 2 + 256
+    for over, msg in (({"y_dtype": F32}, "y dtype"), ({"channels": 96}, "multiple of 64"),
+                      ({"in_features": 200}, "multiple of 64"), ({"out_dtype": F16}, "out dtype"),
+                      ({"width": 57}, "divisible"), ({"factor": 1}, "multiple of 256"),
+                      ({"width": 512, "channels": 64}, "at most 128")):
+        a = args(**over)
+        assert lib.ow_d2s_linear_workspace_size(ctypes.byref(a)) == 0, over
+        assert lib.ow_d2s_linear_fwd(ctypes.byref(a), None) == 2  # OW_ERR_UNSUPPORTED
+        assert msg in lib.ow_last_error().decode(), over
+    assert lib.ow_d2s_linear_fwd(ctypes.byref(args()), None) == 1  # NULL pointers: OW_ERR_INVALID
+    with pytest.raises(RuntimeError, match="CUDA is unavailable"):
+        s2d.d2s_linear(torch.zeros(1, 4, 4, 256, dtype=torch.bfloat16), torch.zeros(256, 256), 2)
