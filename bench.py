@@ -102,9 +102,8 @@ def _kernel_flops(name: str, b: int, h: int, w: int, c: int, d: int) -> float:
 _KERNEL_SRC = {"tc_bwd_kernel": "ow_tc_bwd.cu", "tc_pack_kernel": "ow_tc_bwd.cu", "tcf_kernel": "ow_tcf.cu",
                "tc_fwd_kernel": "ow_tc.cu", "tc_fwd_gather_kernel": "ow_tcf.cu"}
 _TRAFFIC = {
-    ("tc_bwd_kernel", "56x56x128/radix1", 128): (2 * (541.092608e6 + 94.050048e6), "ed67ad225802f5f4ce52ac06c06330bc966a9272664fdb7c381b30ab83c89604"),
-    ("tc_bwd_kernel", "56x56x128/radix2", 128): (2 * (542.858240e6 + 94.941696e6), "ed67ad225802f5f4ce52ac06c06330bc966a9272664fdb7c381b30ab83c89604"),
-    ("tc_bwd_kernel", "56x56x128/local0", 128): (2 * (437.841920e6 + 46.002176e6), "ed67ad225802f5f4ce52ac06c06330bc966a9272664fdb7c381b30ab83c89604"),
+    ("tc_bwd_kernel", "56x56x128/radix1", 128): (2 * (541.915392e6 + 93.980928e6), "cb20fe4683d3ebcb08543c290d60815c09ec506ae55ba551c49fc0a086f1ec1e"),
+    ("tc_bwd_kernel", "56x56x128/radix2", 128): (2 * (541.527552e6 + 94.035712e6), "cb20fe4683d3ebcb08543c290d60815c09ec506ae55ba551c49fc0a086f1ec1e"),
 }
 
 
